@@ -1,0 +1,348 @@
+"""bench.py — NVFP4 GEMM throughput on B200 (driver contract: one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: D[M,N] = alpha * A[M,K] . B[N,K]^T with
+M = N = K = 8192 per GPU, A and B drawn bf16 N(0,1) on the device (seeded) and
+quantized to NVFP4 by this library's quantizer; bf16 output.  A step is one GEMM
+launch.  Multi-GPU is column-parallel (weak scaling): rank p owns an 8192-column
+shard of B (N_total = 8192 * P), A is replicated, no collective is needed for the
+result, so none runs in the timed region.
+
+`value` is the whole-job TFLOP/s (sum of 2*M*N_shard*K over ranks / max-over-ranks
+device time).  Inputs rotate over enough distinct operand sets to exceed 3x L2.
+`e2e` times the same GEMM through the public API from pinned HOST buffers: the
+H2D copies of A, SFA, B, SFB and the D2H copy of D are inside the timed region.
+
+`--impl reference` times the reference's path on the host cores: the CPU
+dequantise + fp32 GEMM (oracle/, the reference has no CPU implementation of its
+own) on a bounded row sample of the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "gpu-kernels_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+M_ = N_ = K_ = 8192
+METRIC = "NVFP4 GEMM TFLOPS/GPU & % FP4 peak (8192^3); decode-shape HBM GB/s; 1/2/4/8 GPU"
+UNIT = "TFLOP/s"
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained"), "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def committed_traffic():
+    """DRAM bytes per GEMM launch from the committed ncu capture summary, if any."""
+    path = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_operand_sets(nv, n_sets, M, N, K, seed, dev):
+    """Quantized operand sets generated on the device by the product's own kernels."""
+    g = torch.Generator(device=dev)
+    sets = []
+    for i in range(n_sets):
+        g.manual_seed(seed + 1000 * i)
+        xa = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+        xb = torch.randn(N, K, device=dev, generator=g).to(torch.bfloat16)
+        _, gsa = nv.global_scale(xa)
+        _, gsb = nv.global_scale(xb)
+        a, sfa = nv.quantize(xa, gsa)
+        b, sfb = nv.quantize(xb, gsb)
+        alpha = float(gsa.item()) * float(gsb.item())
+        del xa, xb
+        sets.append((a, sfa, b, sfb, alpha))
+    torch.cuda.synchronize()
+    return sets
+
+
+def cpu_reference_sample(a, sfa, b, sfb, alpha, M, N, K, target_s=12.0):
+    """Time the CPU dequant + fp32 GEMM (oracle) on a row sample sized to ~target_s."""
+    from oracle import oracle as o
+    an, sfan, bn, sfbn = (t.cpu().numpy() for t in (a, sfa, b, sfb))
+    threads = o.max_threads()
+    rows = 16
+    t0 = time.perf_counter()
+    o.gemm(an, sfan, bn, sfbn, alpha, M, N, K, m0=0, mrows=rows, nthreads=threads)
+    t_small = time.perf_counter() - t0
+    # the call dequantises all of B (fixed cost) plus `rows` rows of A and their dot products
+    rows = int(max(16, min(M, rows * target_s / max(t_small, 1e-3))))
+    rows = max(16, rows // 16 * 16)
+    t0 = time.perf_counter()
+    o.gemm(an, sfan, bn, sfbn, alpha, M, N, K, m0=0, mrows=rows, nthreads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": 2.0 * rows * N * K / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"A rows 0..{rows} x N={N} x K={K} (dequantise A rows + all of B, fp32 GEMM, bf16 out); "
+                      f"{dt:.1f} s"}, rows, dt
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import oracle as o
+    import numpy as np
+    M, N, K = M_, N_, K_
+    # same workload semantics: N(0,1) bf16 quantized per tensor; operands built on the host
+    threads = o.max_threads()
+    xa = o.normal_bf16((M, K), seed=1, nthreads=threads)
+    xb = o.normal_bf16((N, K), seed=2, nthreads=threads)
+    gsa, gsb = o.global_scale_for(o.amax_bf16(xa)), o.global_scale_for(o.amax_bf16(xb))
+    a, sfa = o.quantize(xa, gsa, nthreads=threads)
+    b, sfb = o.quantize(xb, gsb, nthreads=threads)
+    alpha = float(np.float32(gsa) * np.float32(gsb))
+    del xa, xb
+    rows = 64
+    t0 = time.perf_counter()
+    o.gemm(a, sfa, b, sfb, alpha, M, N, K, m0=0, mrows=rows, nthreads=threads)
+    t1 = time.perf_counter() - t0
+    # size each step to ~ (120 s / (steps + warmup)) so the whole run stays within minutes
+    per_step = max(2.0, min(20.0, 120.0 / max(1, args.steps + args.warmup)))
+    rows = int(max(16, min(M, rows * per_step / max(t1, 1e-3)))) // 16 * 16
+    for _ in range(args.warmup):
+        o.gemm(a, sfa, b, sfb, alpha, M, N, K, m0=0, mrows=rows, nthreads=threads)
+    times = []
+    for s in range(args.steps):
+        m0 = (s * rows) % max(1, M - rows + 1)
+        t0 = time.perf_counter()
+        o.gemm(a, sfa, b, sfb, alpha, M, N, K, m0=m0, mrows=rows, nthreads=threads)
+        times.append(time.perf_counter() - t0)
+    dt = sum(times)
+    value = 2.0 * rows * N * K * len(times) / dt / 1e12
+    sample = f"per step A rows {rows} x N={N} x K={K} (dequantise + fp32 GEMM + bf16), host threads {threads}"
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp4(e2m1)xfp4->fp32",
+            "data": "synthetic: bf16 N(0,1) quantized to NVFP4 (seeded)",
+            "config": {"workload": "square NVFP4 GEMM M=N=K=8192 (BASELINE configs[1]), CPU row sample",
+                       "M": M, "N": N, "K": K, "parallelism": "host threads"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import nvfp4_b200 as nv
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", local)
+    M, N, K = M_, N_, K_
+    flops = 2.0 * M * N * K
+    in_bytes = M * K // 2 + N * K // 2 + nv.sf_bytes(M, K) + nv.sf_bytes(N, K)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    n_sets = args.sets if args.sets else max(2, -(-3 * l2 // in_bytes))
+    sets = make_operand_sets(nv, n_sets, M, N, K, seed=1234 + 7919 * rank, dev=dev)
+    d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        a, sfa, b, sfb, alpha = sets[i % n_sets]
+        nv.gemm(a, sfa, b, sfb, alpha, out=d)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    nv.device_status()
+
+    # ---- timed region: device time with CUDA events on the launching stream
+    launches0 = nv.launch_count()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(local) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        ev[0].record(stream)
+        for i in range(args.steps):
+            step(i)
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    launches = nv.launch_count() - launches0
+    nv.device_status()
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    total_ms = max_over_ranks(sum(per), world)
+    ms_step = total_ms / args.steps
+    value = flops * world * args.steps / (total_ms / 1e3) / 1e12
+    kernel_ms = statistics.mean(per)
+    achieved = flops / (kernel_ms / 1e3) / 1e12
+
+    # ---- end to end through the public API from pinned host buffers
+    a, sfa, b, sfb, alpha = sets[0]
+    host_in = [t.cpu().pin_memory() for t in (a, sfa, b, sfb)]
+    dev_in = [torch.empty_like(t) for t in (a, sfa, b, sfb)]
+    host_out = torch.empty(M, N, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_step():
+        for src, dst in zip(host_in, dev_in):
+            dst.copy_(src, non_blocking=True)
+        nv.gemm(dev_in[0], dev_in[1], dev_in[2], dev_in[3], alpha, out=d)
+        host_out.copy_(d, non_blocking=True)
+
+    e2e_ms = e2e_value = None
+    if not args.no_e2e:
+        e2e_steps = max(3, min(args.steps, 20))
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / e2e_steps
+        e2e_value = flops * world / (e2e_ms / 1e3) / 1e12
+        barrier(world)
+
+    pk = peaks()
+    fp4_peak_est = 4.0 * pk["bf16_tflops"]
+    traffic = committed_traffic().get("gemm_8192", {}).get("dram_bytes_per_launch")
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu, _, _ = cpu_reference_sample(a, sfa, b, sfb, alpha, M, N, K, target_s=args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp4(e2m1)xfp4->fp32",
+            "data": "synthetic: bf16 N(0,1) drawn on device (seeded), quantized by nvfp4_quantize",
+            "config": {"workload": "square NVFP4 GEMM M=N=K=8192 per GPU (BASELINE configs[1])",
+                       "M": M, "N_per_gpu": N, "K": K, "out": "bf16", "alpha": "gsA*gsB",
+                       "parallelism": f"column-parallel N shards x{world}",
+                       "l2": f"rotating {n_sets} operand sets of {in_bytes / 1e6:.1f} MB (> 3x L2)"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": fp4_peak_est, "unit": "TFLOP/s",
+                         "frac": achieved / fp4_peak_est, "traffic": traffic,
+                         "peak_basis": f"4 x {pk['source']} dense bf16 ({pk['bf16_tflops']} TFLOP/s): FP4 "
+                                       "tensor rate is 4x bf16 per SM; no FP4 peak is measured on this pool",
+                         "frac_of_nominal_9000": achieved / 9000.0,
+                         "kernel_ms": kernel_ms, "flops_per_launch": flops},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                    "ms_per_step": e2e_ms, "path": "pinned host -> nvfp4_gemm -> pinned host"},
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--sets", type=int, default=0, help="operand sets to rotate (default: > 3x L2)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,406 @@
+// gemm.cu — persistent, warp-specialised NVFP4 block-scaled GEMM for sm_100a.
+//
+//   D[M,N] = alpha * sum_k (e2m1 A[m,k] * e4m3 SFA[m,k/16]) * (e2m1 B[n,k] * e4m3 SFB[n,k/16])
+//
+// Same contract as the reference's best B200 kernel (_matmul_nvfp4_v5,
+// matmul/sm100_nvfp4/nvfp4_v5.cu:21-231 of Parth-Badgujar/gpu-kernels): e2m1 K-major
+// operands, 128x4-blocked e4m3 scales, tcgen05 kind::mxf4nvf4 MMAs with the scales
+// staged through tensor memory.  What is different, and why:
+//   * the accumulator is released as soon as the epilogue has pulled it into
+//     registers, so the next tile's MMAs overlap the conversion and stores
+//     (the reference serialises the whole epilogue against the mainloop);
+//   * 8 epilogue warps (two per TMEM lane quarter) drain 256 columns in one pass;
+//   * a 4-stage, 54 KB/stage ring (BLOCK_K = 256) with per-stage scale columns;
+//   * any M >= 1, N % 8 == 0, K % 64 == 0: TMA zero-fills ragged tiles, the last
+//     k-stage issues only the k-groups that exist, stores are bounds-checked;
+//   * grouped rasterisation for L2 reuse without the reference's divisibility rule;
+//   * every wait is bounded; a timed-out CTA drains its in-flight copies and MMAs,
+//     frees its tensor memory and returns (status latched for the host);
+//   * alpha and bf16 (or fp16) output; explicit stream; tensor maps cached.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace nvfp4 {
+
+namespace gemm {
+
+constexpr int kBlockM = 128;
+constexpr int kBlockKBytes = 128;               // one 128-byte swizzle row = 256 fp4
+constexpr int kKGroups = 4;                     // 64-element MMA k-steps per stage
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 32 * (2 + kEpiWarps);  // producer, MMA, 8 epilogue warps
+constexpr int kGroupM = 16;                     // m-tiles per raster group
+
+template <int BN, int STAGES>
+struct Layout {
+    static constexpr int kSfbBlocks = BN / 128;
+    static constexpr int kA = kBlockM * kBlockKBytes;        // 16 KB
+    static constexpr int kB = BN * kBlockKBytes;             // 32 KB at BN=256
+    static constexpr int kSfa = kKGroups * 512;              // 2 KB
+    static constexpr int kSfb = kSfbBlocks * kKGroups * 512; // 4 KB at BN=256
+    static constexpr int kOffA = 0;
+    static constexpr int kOffB = kOffA + STAGES * kA;
+    static constexpr int kOffSfa = kOffB + STAGES * kB;
+    static constexpr int kOffSfb = kOffSfa + STAGES * kSfa;
+    static constexpr int kOffBar = kOffSfb + STAGES * kSfb;
+    // barriers: full[S], empty[S], acc_full, acc_empty, drain; then tmem slot + abort flag
+    static constexpr int kBarBytes = (2 * STAGES + 3) * 8 + 16;
+    static constexpr int kBytes = kOffBar + kBarBytes;
+    static constexpr int kDynamicSmem = kBytes + 1024;       // manual 1024-B alignment slack
+    // tensor memory: accumulator columns [0, BN), two sets of scale columns after it
+    static constexpr int kSfColsPerGroup = 4 + 4 * kSfbBlocks;
+    static constexpr int kSfColsPerStage = kKGroups * kSfColsPerGroup;
+    static constexpr int kTmemCols = 512;
+    static_assert(BN + 2 * kSfColsPerStage <= kTmemCols, "tensor memory budget");
+    static_assert(kDynamicSmem <= 232448, "shared memory budget");
+};
+
+struct Params {
+    const uint8_t *sfa;
+    const uint8_t *sfb;
+    void *d;
+    int M, N, K;
+    float alpha;
+    int num_m_tiles, num_n_tiles, num_tiles;
+    int num_kb;       // ceil(K / 256)
+    int k_groups;     // K / 64
+    int vec32_store;  // D 32-byte aligned and N % 16 == 0
+    KernelCtl ctl;
+};
+
+__device__ __forceinline__ void tile_coords(int t, const Params &p, int &tm, int &tn) {
+    const int per_group = kGroupM * p.num_n_tiles;
+    const int g = t / per_group;
+    const int first_m = g * kGroupM;
+    const int gm = min(p.num_m_tiles - first_m, kGroupM);
+    const int local = t - g * per_group;
+    tm = first_m + local % gm;
+    tn = local / gm;
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, bool f16) {
+    if (f16) {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t *>(&h);
+    }
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+template <int BN, int STAGES, bool F16>
+__global__ void __launch_bounds__(kThreads, 1)
+    nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                      const Params p) {
+    using L = Layout<BN, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    uint8_t *base_ptr = smem_raw + (base - smem_u32(smem_raw));
+    const uint32_t sA = base + L::kOffA, sB = base + L::kOffB, sSfa = base + L::kOffSfa, sSfb = base + L::kOffSfb;
+    const uint32_t bar_full = base + L::kOffBar;
+    const uint32_t bar_empty = bar_full + 8 * STAGES;
+    const uint32_t bar_acc_full = bar_empty + 8 * STAGES;
+    const uint32_t bar_acc_empty = bar_acc_full + 8;
+    const uint32_t bar_drain = bar_acc_empty + 8;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(base_ptr + L::kOffBar + (2 * STAGES + 3) * 8);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        mbar_init(bar_acc_full, 1);
+        mbar_init(bar_acc_empty, kEpiWarps);
+        mbar_init(bar_drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint64_t tmo = p.ctl.wait_timeout_ns;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (elect_one()) {
+            const int64_t rest_k = p.K >> 6;  // 64-element k-groups per 128-row scale block
+            const int sfb_rows_padded = ((p.N + 127) / 128) * 128;
+            uint32_t it = 0;
+            bool ok = true;
+            uint32_t issued_mask = 0, issued_parity = 0;
+            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+                int tm, tn;
+                tile_coords(t, p, tm, tn);
+                for (int kb = 0; kb < p.num_kb; kb++, it++) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!wait_parity(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
+                        report_timeout(abort_flag, p.ctl.status);
+                        ok = false;
+                        break;
+                    }
+                    const int kg = min(kKGroups, p.k_groups - kb * kKGroups);
+                    int sfb_blocks = 0;
+                    for (int rb = 0; rb < L::kSfbBlocks; rb++)
+                        if (tn * BN + rb * 128 < sfb_rows_padded) sfb_blocks++;
+                    const uint32_t bytes = L::kA + L::kB + (uint32_t)kg * 512u * (1u + sfb_blocks);
+                    mbar_arrive_expect_tx(bar_full + 8 * s, bytes);
+                    issued_mask |= 1u << s;
+                    issued_parity = (issued_parity & ~(1u << s)) | (ph << s);
+                    tma_load_2d(sA + s * L::kA, &tmap_a, bar_full + 8 * s, kb * kBlockKBytes, tm * kBlockM);
+                    tma_load_2d(sB + s * L::kB, &tmap_b, bar_full + 8 * s, kb * kBlockKBytes, tn * BN);
+                    bulk_load(sSfa + s * L::kSfa, p.sfa + ((int64_t)tm * rest_k + kb * kKGroups) * 512,
+                              kg * 512u, bar_full + 8 * s);
+                    for (int rb = 0; rb < sfb_blocks; rb++)
+                        bulk_load(sSfb + s * L::kSfb + rb * kKGroups * 512,
+                                  p.sfb + ((int64_t)(tn * L::kSfbBlocks + rb) * rest_k + kb * kKGroups) * 512,
+                                  kg * 512u, bar_full + 8 * s);
+                }
+            }
+            if (!ok) {
+                // Drain: every load already issued must land before the CTA exits.
+                volatile int never = 0;
+                for (int s = 0; s < STAGES; s++)
+                    if (issued_mask & (1u << s))
+                        wait_parity(bar_full + 8 * s, (issued_parity >> s) & 1, p.ctl.drain_timeout_ns, &never);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (elect_one()) {
+            constexpr uint32_t idesc = idesc_mxf4nvf4(kBlockM, BN);
+            const uint32_t tmem_acc = tmem_base;
+            uint32_t it = 0;
+            int local = 0;
+            bool ok = true, any_issued = false;
+            for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x, local++) {
+                if (!wait_parity(bar_acc_empty, (local & 1) ^ 1, tmo, abort_flag)) {
+                    report_timeout(abort_flag, p.ctl.status);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int kb = 0; kb < p.num_kb; kb++, it++) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!wait_parity(bar_full + 8 * s, ph, tmo, abort_flag)) {
+                        report_timeout(abort_flag, p.ctl.status);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const int kg = min(kKGroups, p.k_groups - kb * kKGroups);
+                    const uint32_t sf_cols = tmem_base + BN + (it & 1) * L::kSfColsPerStage;
+                    for (int j = 0; j < kg; j++) {
+                        const uint32_t col = sf_cols + j * L::kSfColsPerGroup;
+                        tmem_cp_32x128_x4(col, smem_desc(sSfa + s * L::kSfa + j * 512, 16, 128, 0));
+#pragma unroll
+                        for (int rb = 0; rb < L::kSfbBlocks; rb++)
+                            tmem_cp_32x128_x4(col + 4 + 4 * rb,
+                                              smem_desc(sSfb + s * L::kSfb + (rb * kKGroups + j) * 512, 16, 128, 0));
+                        const uint64_t adesc = smem_desc(sA + s * L::kA + j * 32, 16, 1024, 2);
+                        const uint64_t bdesc = smem_desc(sB + s * L::kB + j * 32, 16, 1024, 2);
+                        mma_mxf4nvf4(tmem_acc, adesc, bdesc, idesc, col, col + 4, (kb | j) != 0);
+                    }
+                    any_issued = true;
+                    mma_commit(bar_empty + 8 * s);  // frees the smem slot once these MMAs finish
+                }
+                if (!ok) break;
+                mma_commit(bar_acc_full);
+            }
+            if (!ok && any_issued) {
+                volatile int never = 0;
+                mma_commit(bar_drain);
+                wait_parity(bar_drain, 0, p.ctl.drain_timeout_ns, &never);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int quarter = warp & 3;                 // TMEM lanes this warp may read
+        const int half = (warp - 2) >> 2;             // column half of the tile
+        constexpr int kCols = BN / 2;                 // columns per warp
+        int local = 0;
+        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, local++) {
+            int tm, tn;
+            tile_coords(t, p, tm, tn);
+            bool ok = true;
+            if (lane == 0) ok = wait_parity(bar_acc_full, local & 1, tmo, abort_flag);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0) report_timeout(abort_flag, p.ctl.status);
+                break;
+            }
+            tc_fence_after();
+            uint32_t acc[kCols];
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * kCols;
+#pragma unroll
+            for (int c = 0; c < kCols / 32; c++)
+                tmem_ld_32x32b_x32(taddr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&acc[c * 32]));
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_acc_empty);  // accumulator may be overwritten now
+
+            const int row = tm * kBlockM + quarter * 32 + lane;
+            const int col0 = tn * BN + half * kCols;
+            if (row < p.M) {
+                uint8_t *drow = static_cast<uint8_t *>(p.d) + ((int64_t)row * p.N + col0) * 2;
+                if (p.vec32_store) {
+#pragma unroll
+                    for (int c = 0; c < kCols / 16; c++) {
+                        if (col0 + c * 16 < p.N) {
+                            uint32_t v[8];
+#pragma unroll
+                            for (int i = 0; i < 8; i++)
+                                v[i] = pack2(__uint_as_float(acc[c * 16 + 2 * i]) * p.alpha,
+                                             __uint_as_float(acc[c * 16 + 2 * i + 1]) * p.alpha, F16);
+                            st_global_v8(drow + c * 32, v);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < kCols / 8; c++) {
+                        if (col0 + c * 8 < p.N) {
+                            uint4 v;
+                            v.x = pack2(__uint_as_float(acc[c * 8 + 0]) * p.alpha,
+                                        __uint_as_float(acc[c * 8 + 1]) * p.alpha, F16);
+                            v.y = pack2(__uint_as_float(acc[c * 8 + 2]) * p.alpha,
+                                        __uint_as_float(acc[c * 8 + 3]) * p.alpha, F16);
+                            v.z = pack2(__uint_as_float(acc[c * 8 + 4]) * p.alpha,
+                                        __uint_as_float(acc[c * 8 + 5]) * p.alpha, F16);
+                            v.w = pack2(__uint_as_float(acc[c * 8 + 6]) * p.alpha,
+                                        __uint_as_float(acc[c * 8 + 7]) * p.alpha, F16);
+                            *reinterpret_cast<uint4 *>(drow + c * 16) = v;
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, L::kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+struct MapKey {
+    int device;
+    const void *ptr;
+    int64_t rows, kbytes;
+    int box_rows;
+    bool operator==(const MapKey &o) const {
+        return device == o.device && ptr == o.ptr && rows == o.rows && kbytes == o.kbytes && box_rows == o.box_rows;
+    }
+};
+
+// Small LRU of encoded operand tensor maps (the reference re-encodes on every
+// call, nvfp4_v5.cu:294-308).  Thread-safe.
+static int operand_map(const void *ptr, int64_t rows, int64_t K, int box_rows, CUtensorMap *out) {
+    static std::mutex mu;
+    constexpr int kCap = 64;
+    static MapKey keys[kCap];
+    static CUtensorMap maps[kCap];
+    static uint64_t stamp[kCap];
+    static uint64_t clock = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    MapKey key{dev, ptr, rows, K / 2, box_rows};
+    std::lock_guard<std::mutex> lock(mu);
+    int victim = 0;
+    for (int i = 0; i < kCap; i++) {
+        if (stamp[i] && keys[i] == key) {
+            stamp[i] = ++clock;
+            *out = maps[i];
+            return NVFP4_OK;
+        }
+        if (stamp[i] < stamp[victim]) victim = i;
+    }
+    CUtensorMap m;
+    int st = encode_tiled_2d(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, ptr, (uint64_t)(K / 2), (uint64_t)rows,
+                             (uint64_t)(K / 2), kBlockKBytes, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    keys[victim] = key;
+    maps[victim] = m;
+    stamp[victim] = ++clock;
+    *out = m;
+    return NVFP4_OK;
+}
+
+template <int BN, int STAGES, bool F16>
+static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
+                  int M, int N, int K, cudaStream_t stream, const DeviceInfo &di) {
+    using L = Layout<BN, STAGES>;
+    auto kern = nvfp4_gemm_kernel<BN, STAGES, F16>;
+    static int configured[64] = {};
+    if (!configured[di.device]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamicSmem) != cudaSuccess)
+            return NVFP4_ERR_CUDA;
+        configured[di.device] = 1;
+    }
+    CUtensorMap ta, tb;
+    int st = operand_map(A, M, K, kBlockM, &ta);
+    if (!st) st = operand_map(B, N, K, BN, &tb);
+    if (st) return st;
+    Params p;
+    p.sfa = SFA;
+    p.sfb = SFB;
+    p.d = D;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.alpha = alpha;
+    p.num_m_tiles = (M + kBlockM - 1) / kBlockM;
+    p.num_n_tiles = (N + BN - 1) / BN;
+    p.num_tiles = p.num_m_tiles * p.num_n_tiles;
+    p.num_kb = (K + 255) / 256;
+    p.k_groups = K / 64;
+    p.vec32_store = ((reinterpret_cast<uintptr_t>(D) & 31u) == 0) && (N % 16 == 0);
+    if ((st = kernel_ctl(&p.ctl))) return st;
+    const int grid = p.num_tiles < di.sm_count ? p.num_tiles : di.sm_count;
+    kern<<<grid, kThreads, L::kDynamicSmem, stream>>>(ta, tb, p);
+    count_launch();
+    return cuda_status(cudaGetLastError());
+}
+
+}  // namespace gemm
+
+int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const void *D, int M,
+                  int N, int K) {
+    if (!A || !SFA || !B || !SFB || !D) return NVFP4_ERR_INVALID;
+    if (M < 1 || N < 8 || N % 8 || K < 64 || K % 64) return NVFP4_ERR_SHAPE;
+    if (!aligned16(A) || !aligned16(SFA) || !aligned16(B) || !aligned16(SFB) || !aligned16(D)) return NVFP4_ERR_ALIGN;
+    return NVFP4_OK;
+}
+
+int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
+                  int M, int N, int K, cudaStream_t stream, bool f16) {
+    int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
+    if (st) return st;
+    DeviceInfo di;
+    if ((st = device_info(&di))) return st;
+    if (f16) return gemm::launch<256, 4, true>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di);
+    return gemm::launch<256, 4, false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di);
+}
+
+}  // namespace nvfp4

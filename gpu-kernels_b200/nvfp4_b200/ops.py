@@ -1,0 +1,128 @@
+"""torch-facing front end of the C ABI (the reference's Python side,
+matmul/sm100_nvfp4/main.py, works on torch tensors in exactly these formats).
+
+Operands may be given as uint8 / int8 / float4_e2m1fn_x2 (codes) and uint8 /
+float8_e4m3fn (scales) tensors: only the bytes matter.  All calls are
+asynchronous on torch's current CUDA stream and raise NVFP4Error on a bad
+status.  Nothing here computes on the CPU.
+"""
+from typing import Optional, Tuple, Union
+
+import torch
+
+from ._lib import NVFP4Error, check, lib
+from .layout import sf_bytes, to_blocked
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _bytes_tensor(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.element_size() != 1:
+        raise ValueError(f"{name} must be a 1-byte dtype (codes/scales), got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+def _scale_tensor(gs: Union[torch.Tensor, float], device: torch.device) -> torch.Tensor:
+    if isinstance(gs, torch.Tensor):
+        if gs.dtype != torch.float32 or gs.numel() != 1 or gs.device != device:
+            raise ValueError("global_scale must be a 1-element float32 tensor on the input's device")
+        return gs
+    return torch.tensor([float(gs)], dtype=torch.float32, device=device)
+
+
+def global_scale(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(amax, gs) of a bf16 tensor as 1-element fp32 device tensors, gs = amax/(6*448)."""
+    if x.dtype != torch.bfloat16 or not x.is_cuda or not x.is_contiguous():
+        raise ValueError("x must be a contiguous bf16 CUDA tensor")
+    amax = torch.empty(1, dtype=torch.float32, device=x.device)
+    gs = torch.empty(1, dtype=torch.float32, device=x.device)
+    check(lib().nvfp4_global_scale(x.data_ptr(), x.numel(), amax.data_ptr(), gs.data_ptr(),
+                                   _stream(x.device)), "nvfp4_global_scale")
+    return amax, gs
+
+
+def quantize(x: torch.Tensor, global_scale: Union[torch.Tensor, float],
+             q_out: Optional[torch.Tensor] = None,
+             sf_out: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [M, K] -> (codes uint8 [M, K/2], blocked e4m3 scales uint8 [pad128(M)*K/16])."""
+    if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous 2-D bf16 CUDA tensor")
+    M, K = x.shape
+    gs = _scale_tensor(global_scale, x.device)
+    q = q_out if q_out is not None else torch.empty(M, K // 2, dtype=torch.uint8, device=x.device)
+    sf = sf_out if sf_out is not None else torch.empty(sf_bytes(M, K), dtype=torch.uint8, device=x.device)
+    check(lib().nvfp4_quantize(x.data_ptr(), q.data_ptr(), sf.data_ptr(), gs.data_ptr(), M, K,
+                               _stream(x.device)), "nvfp4_quantize")
+    return q, sf
+
+
+def gemm(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, alpha: float = 1.0,
+         out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """D[M, N] = alpha * A . B^T for NVFP4 A [M, K/2], B [N, K/2] with blocked scales."""
+    for t, n in ((a, "a"), (sfa, "sfa"), (b, "b"), (sfb, "sfb")):
+        _bytes_tensor(t, n)
+    M, K = a.shape[0], a.shape[1] * 2
+    N = b.shape[0]
+    if b.shape[1] * 2 != K:
+        raise ValueError("A and B must have the same K")
+    if sfa.numel() < sf_bytes(M, K) or sfb.numel() < sf_bytes(N, K):
+        raise ValueError("scale tensors too small for the blocked layout (rows padded to 128)")
+    if out_dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("out_dtype must be bf16 or fp16")
+    d = out if out is not None else torch.empty(M, N, dtype=out_dtype, device=a.device)
+    if d.dtype != out_dtype or d.shape != (M, N) or not d.is_contiguous():
+        raise ValueError("out must be a contiguous [M, N] tensor of out_dtype")
+    fn = lib().nvfp4_gemm if out_dtype == torch.bfloat16 else lib().nvfp4_gemm_f16
+    check(fn(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), float(alpha), d.data_ptr(), M, N, K,
+             _stream(a.device)), "nvfp4_gemm")
+    return d
+
+
+def matmul_nvfp4(c: torch.Tensor, sfa: torch.Tensor, sfb: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
+                 M: int, N: int, K: int) -> None:
+    """Reference launcher signature (matmul/sm100_nvfp4/block_scaled_nvfp4.cuh:7-18):
+    fp16 c [M, N] = A . B^T on the legacy default stream, through the C shim
+    matmul_nvfp4_b200; raises if the call's status is not OK."""
+    lib().matmul_nvfp4_b200(c.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), a.data_ptr(), b.data_ptr(), M, N, K)
+    check(lib().nvfp4_last_status(), "matmul_nvfp4_b200")
+
+
+def create_tensors(M: int, N: int, K: int, sf_vec_size: int = 16, seed: int = 42, device: str = "cuda"):
+    """Operands in the reference's test distribution (matmul/sm100_nvfp4/main.py:9-23):
+    uniformly random e2m1 byte codes, e4m3 scale codes 0..3, scales blocked."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    a = torch.randint(-128, 127, (M, K // 2), dtype=torch.int8, device=device, generator=g)
+    b = torch.randint(-128, 127, (N, K // 2), dtype=torch.int8, device=device, generator=g)
+    sfa = torch.randint(0, 4, (M, K // sf_vec_size), dtype=torch.int8, device=device, generator=g)
+    sfb = torch.randint(0, 4, (N, K // sf_vec_size), dtype=torch.int8, device=device, generator=g)
+    return (a.view(torch.uint8), b.view(torch.uint8), to_blocked(sfa.view(torch.uint8)),
+            to_blocked(sfb.view(torch.uint8)))
+
+
+def device_status(device: Optional[torch.device] = None) -> None:
+    """Synchronise and raise NVFP4Error(NVFP4_ERR_TIMEOUT) if a kernel gave up a wait."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    check(lib().nvfp4_device_status(_stream(dev)), "device status")
+
+
+def set_wait_timeout_ns(ns: int) -> None:
+    lib().nvfp4_set_wait_timeout_ns(int(ns))
+
+
+def selftest_wait_timeout(ns: int = 1_000_000) -> int:
+    return lib().nvfp4_selftest_wait_timeout(int(ns))
+
+
+def launch_count() -> int:
+    return int(lib().nvfp4_launch_count())
+
+
+__all__ = ["NVFP4Error", "global_scale", "quantize", "gemm", "matmul_nvfp4", "create_tensors",
+           "device_status", "set_wait_timeout_ns", "selftest_wait_timeout", "launch_count"]

@@ -1,0 +1,141 @@
+/*
+ * nvfp4_b200.h — C ABI of the B200 (sm_100a) NVFP4 block-scaled GEMM and its
+ * bf16 -> NVFP4 quantizer (library: gpu-kernels_b200/nvfp4_b200/libnvfp4_b200.so).
+ *
+ * It is the drop-in boundary for the reference's plugin surface
+ * (Parth-Badgujar/gpu-kernels):
+ *   matmul/sm100_nvfp4/block_scaled_nvfp4.cuh:7-18   host launcher declarations
+ *       void matmul_nvfp4_vN(fp16 *c, const uint8_t *sfa, const uint8_t *sfb,
+ *                            const uint8_t *a, const uint8_t *b, int M, int N, int K);
+ *   matmul/sm100_nvfp4/runner.cu:61-96               the runner that calls them
+ *   matmul/sm100_nvfp4/main.py:9-34                  operand formats / oracle semantics
+ *
+ * Only plain pointers, sizes and status codes cross it: no CUDA, torch or C++
+ * types.  Streams are passed as `void*` (a cudaStream_t / CUstream handle;
+ * NULL = the legacy default stream).  All data pointers are DEVICE pointers of
+ * the current device unless a function says otherwise.
+ *
+ * Operand formats (identical to the reference's):
+ *   A  [M, K/2]  uint8: e2m1 codes, K-major, element 2i in the low nibble
+ *   B  [N, K/2]  uint8: same (B is the "weight", D = A . B^T)
+ *   SFA/SFB      uint8 e4m3 codes, one per 16 K-elements, in the 128x4 blocked
+ *                layout of [pad128(rows), K/16]:
+ *                off(r,k16) = ((r/128)*(K/64) + k16/4)*512 + (r%32)*16
+ *                             + ((r/32)%4)*4 + k16%4
+ *                (rows padded to a multiple of 128; padding scales must be finite)
+ *   D  [M, N]    bf16 (uint16 bit patterns) row-major, D = alpha * A . B^T
+ *
+ * Shape rules: M >= 1, N >= 8 with N % 8 == 0, K >= 64 with K % 64 == 0 (the bf16
+ * row pitch of D is a multiple of 16 bytes).  Pointers 16-byte aligned.
+ *
+ * Errors: every int-returning function returns NVFP4_OK (0) or a negative
+ * status; nothing exits or traps.  Kernel launches are asynchronous; a device
+ * side timeout (a bounded wait that gave up) is latched in a per-device status
+ * word that nvfp4_device_status() reads and clears.
+ */
+#ifndef NVFP4_B200_H
+#define NVFP4_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NVFP4_API __attribute__((visibility("default")))
+#else
+#define NVFP4_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    NVFP4_OK = 0,
+    NVFP4_ERR_INVALID = -1,      /* null pointer or bad argument            */
+    NVFP4_ERR_SHAPE = -2,        /* M/N/K violate the shape rules           */
+    NVFP4_ERR_ALIGN = -3,        /* pointer not 16-byte aligned             */
+    NVFP4_ERR_CUDA = -4,         /* CUDA runtime / driver error             */
+    NVFP4_ERR_TIMEOUT = -5,      /* a bounded device wait gave up           */
+    NVFP4_ERR_UNSUPPORTED = -6,  /* device is not sm_100 (B200/GB200)       */
+    NVFP4_ERR_WORKSPACE = -7     /* workspace missing or too small          */
+};
+
+/* Human-readable name of a status code. */
+NVFP4_API const char *nvfp4_status_string(int status);
+
+/* Library version as (major << 16) | minor. */
+NVFP4_API int nvfp4_version(void);
+
+/*
+ * bf16 -> NVFP4 quantizer.  Replaces: nothing in the reference (it has no
+ * quantizer; main.py:9-23 draws random codes instead).  Required by the
+ * reference path's operands.
+ *   X [M, K] bf16 row-major -> Q [M, K/2] e2m1 codes, SF blocked [pad128(M), K/16]
+ *   global_scale: DEVICE pointer to one fp32 gs (x ~= q * sf * gs).
+ * Per 16-element block: sf = e4m3_rn_sat((amax/6)/gs); q = e2m1_rn_sat(x * (1/(sf*gs))),
+ * every fp32 step a single IEEE round-to-nearest operation (bit-exact with the
+ * CPU specification).  SF padding rows are written as 0.
+ */
+NVFP4_API int nvfp4_quantize(const uint16_t *X, uint8_t *Q, uint8_t *SF, const float *global_scale,
+                   int M, int K, void *stream);
+
+/*
+ * Tensor amax and global scale: *amax_out = max |X|, *gs_out = amax / (6 * 448)
+ * (both DEVICE fp32 pointers; either may be NULL).  n = number of bf16 elements.
+ * Replaces: nothing in the reference; it is the first pass of the quantizer
+ * when gs is not known ahead of time.
+ */
+NVFP4_API int nvfp4_global_scale(const uint16_t *X, int64_t n, float *amax_out, float *gs_out,
+                       void *stream);
+
+/*
+ * NVFP4 GEMM, D = alpha * A . B^T, bf16 out.  Replaces the reference's best B200
+ * launcher matmul_nvfp4_v5 (matmul/sm100_nvfp4/nvfp4_v5.cu:287-309, declared at
+ * block_scaled_nvfp4.cuh:15-16), adding alpha, bf16 output, a stream, any
+ * M >= 1 / N % 8 / K % 64 shape and a status code.  Runs the persistent,
+ * warp-specialised tcgen05 kernel; allocates nothing.
+ */
+NVFP4_API int nvfp4_gemm(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+               float alpha, uint16_t *D, int M, int N, int K, void *stream);
+
+/* Same contract, fp16 output (the reference's output type). */
+NVFP4_API int nvfp4_gemm_f16(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+                   float alpha, uint16_t *D, int M, int N, int K, void *stream);
+
+/*
+ * Reference-signature shim: drop-in for matmul_nvfp4_vN in
+ * matmul/sm100_nvfp4/runner.cu:61-96 (fp16 D, alpha = 1, legacy default
+ * stream, no return value).  The status of the last call is kept for
+ * nvfp4_last_status().  `c` is a __half* in the reference; any 2-byte type works.
+ */
+NVFP4_API void matmul_nvfp4_b200(void *c, const uint8_t *sfa, const uint8_t *sfb, const uint8_t *a,
+                       const uint8_t *b, int M, int N, int K);
+NVFP4_API int nvfp4_last_status(void);
+
+/*
+ * Reads and clears the device-side status word of the current device after
+ * synchronising `stream`: NVFP4_OK, or NVFP4_ERR_TIMEOUT if any kernel of this
+ * library gave up a bounded wait since the last call.
+ */
+NVFP4_API int nvfp4_device_status(void *stream);
+
+/*
+ * Upper bound, in nanoseconds, of every device-side wait of this library's
+ * kernels (default 2e9).  A wait that exceeds it makes the kernel drain its
+ * in-flight copies, free its tensor memory, latch NVFP4_ERR_TIMEOUT and return.
+ */
+NVFP4_API void nvfp4_set_wait_timeout_ns(uint64_t ns);
+
+/*
+ * Self-test of the bounded wait: launches one block that waits on a barrier
+ * nothing arrives on, with the given limit, and returns the status read back
+ * (NVFP4_ERR_TIMEOUT when the limit works).  The context stays usable.
+ */
+NVFP4_API int nvfp4_selftest_wait_timeout(uint64_t timeout_ns);
+
+/* Number of kernel launches this library has issued in this process. */
+NVFP4_API uint64_t nvfp4_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
