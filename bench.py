@@ -22,7 +22,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -59,48 +58,71 @@ def committed_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock, power and clock-event (throttle) reasons sampled every 5 ms through
+    NVML on a background thread for the duration of the timed region."""
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
+    def __init__(self, device):
+        self.device = device
+        self.samples = []
+        self.max_mhz = None
+        self._stop = None
+
+    def _handle(self, nvml):
+        props = torch.cuda.get_device_properties(self.device)
+        uuid = str(getattr(props, "uuid", ""))
+        if uuid:
+            for cand in (uuid if uuid.startswith("GPU-") else "GPU-" + uuid, uuid):
+                try:
+                    return nvml.nvmlDeviceGetHandleByUUID(cand)
+                except Exception:
+                    pass
+        bus = "%08x:%02x:%02x.0" % (getattr(props, "pci_domain_id", 0), props.pci_bus_id, props.pci_device_id)
+        return nvml.nvmlDeviceGetHandleByPciBusId(bus)
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+            import pynvml as nvml
+            nvml.nvmlInit()
+            h = self._handle(nvml)
+            self.max_mhz = nvml.nvmlDeviceGetMaxClockInfo(h, nvml.NVML_CLOCK_SM)
+            get_reasons = getattr(nvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception as e:  # no NVML: report the gap instead of guessing
+            self.error = f"nvml unavailable: {e}"
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append((nvml.nvmlDeviceGetClockInfo(h, nvml.NVML_CLOCK_SM),
+                                         nvml.nvmlDeviceGetPowerUsage(h) / 1000.0, int(get_reasons(h))))
+                except Exception:
+                    pass
+                self._stop.wait(0.005)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        self.out = ""
-        if self.proc is not None:
-            time.sleep(0.25)
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except Exception:
-                self.proc.kill()
+        if self._stop is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        rows = []
-        for line in (self.out or "").strip().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        smax = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0,
+                    "note": getattr(self, "error", "no sample fell in the timed region")}
+        mask = 0
+        for _, _, r in self.samples:
+            mask |= r
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(v for k, v in self.REASONS.items() if mask & k), "samples": len(self.samples),
+                "power_w_max": max(s[1] for s in self.samples), "source": "nvml"}
 
 
 def dist_setup(args):
@@ -154,16 +176,18 @@ def cpu_reference_sample(a, sfa, b, sfb, alpha, M, N, K, target_s=12.0):
     from oracle import oracle as o
     an, sfan, bn, sfbn = (t.cpu().numpy() for t in (a, sfa, b, sfb))
     threads = o.max_threads()
-    rows = 16
-    t0 = time.perf_counter()
-    o.gemm(an, sfan, bn, sfbn, alpha, M, N, K, m0=0, mrows=rows, nthreads=threads)
-    t_small = time.perf_counter() - t0
-    # the call dequantises all of B (fixed cost) plus `rows` rows of A and their dot products
-    rows = int(max(16, min(M, rows * target_s / max(t_small, 1e-3))))
-    rows = max(16, rows // 16 * 16)
-    t0 = time.perf_counter()
-    o.gemm(an, sfan, bn, sfbn, alpha, M, N, K, m0=0, mrows=rows, nthreads=threads)
-    dt = time.perf_counter() - t0
+
+    def timed(rows):
+        t0 = time.perf_counter()
+        o.gemm(an, sfan, bn, sfbn, alpha, M, N, K, m0=0, mrows=rows, nthreads=threads)
+        return time.perf_counter() - t0
+
+    # t(rows) ~ fixed (dequantise all of B) + rows * per_row: fit two points, then size
+    # the sample so that it runs for about target_s seconds
+    t16, t64 = timed(16), timed(64)
+    per_row = max((t64 - t16) / 48.0, 1e-6)
+    rows = int(min(M, max(64, (target_s - t16) / per_row + 16))) // 16 * 16
+    dt = timed(rows)
     return {"value": 2.0 * rows * N * K / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"A rows 0..{rows} x N={N} x K={K} (dequantise A rows + all of B, fp32 GEMM, bf16 out); "
                       f"{dt:.1f} s"}, rows, dt
@@ -241,7 +265,7 @@ def run_ours(args):
     # ---- timed region: device time with CUDA events on the launching stream
     launches0 = nv.launch_count()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-    with ClockSampler(local) as clk:
+    with ClockSampler(dev) as clk:
         barrier(world)
         torch.cuda.synchronize()
         ev[0].record(stream)

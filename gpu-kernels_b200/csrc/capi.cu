@@ -2,23 +2,96 @@
 // include/nvfp4_b200.h).  Argument checking lives in gemm_validate; kernels in
 // gemm.cu, quantize.cu; shared plumbing in runtime.cu.
 #include <atomic>
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "common.cuh"
 
 namespace nvfp4 {
 int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                   int M, int N, int K, cudaStream_t stream, bool f16);
+size_t decode_workspace_bytes(int M, int N);
+int decode_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                    uint16_t *D, int M, int N, int K, void *ws, size_t ws_bytes, cudaStream_t stream);
 }  // namespace nvfp4
 
 using namespace nvfp4;
 
 static std::atomic<int> g_last_status{NVFP4_OK};
 
+// Largest M routed to the split-K decode kernel by nvfp4_gemm (env override
+// NVFP4_DECODE_MAX_M, 0 disables the decode path).
+static int decode_max_m() {
+    static int v = [] {
+        const char *e = std::getenv("NVFP4_DECODE_MAX_M");
+        int x = e ? std::atoi(e) : 128;
+        return x < 0 ? 0 : (x > 128 ? 128 : x);
+    }();
+    return v;
+}
+
+// nvfp4_gemm's own decode workspace: one zero-initialised buffer per (device,
+// stream), grown on demand and kept for the life of the process.  Calls on the
+// same stream are ordered, so they may share it.
+static int internal_workspace(int M, int N, cudaStream_t stream, void **ws, size_t *bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<int, cudaStream_t>, std::pair<void *, size_t>> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return NVFP4_ERR_CUDA;
+    const size_t need = decode_workspace_bytes(M, N);
+    if (!need) return NVFP4_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(mu);
+    auto &slot = cache[{dev, stream}];
+    if (slot.second < need) {
+        if (slot.first) {
+            cudaStreamSynchronize(stream);
+            cudaFree(slot.first);
+            slot = {nullptr, 0};
+        }
+        void *p = nullptr;
+        if (cudaMalloc(&p, need) != cudaSuccess) return NVFP4_ERR_CUDA;
+        if (cudaMemsetAsync(p, 0, need, stream) != cudaSuccess) {
+            cudaFree(p);
+            return NVFP4_ERR_CUDA;
+        }
+        slot = {p, need};
+    }
+    *ws = slot.first;
+    *bytes = slot.second;
+    return NVFP4_OK;
+}
+
 extern "C" {
 
 int nvfp4_gemm(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, uint16_t *D,
                int M, int N, int K, void *stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (M >= 1 && M <= decode_max_m() && A && SFA && B && SFB && D) {
+        void *ws = nullptr;
+        size_t bytes = 0;
+        int st = internal_workspace(M, N, s, &ws, &bytes);
+        if (st) return st;
+        return decode_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, ws, bytes, s);
+    }
+    return gemm_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, s, false);
+}
+
+int nvfp4_gemm_persistent(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                          uint16_t *D, int M, int N, int K, void *stream) {
     return gemm_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, static_cast<cudaStream_t>(stream), false);
+}
+
+size_t nvfp4_gemm_decode_workspace_size(int M, int N) {
+    if (M < 1 || M > 128 || N < 1) return 0;
+    return decode_workspace_bytes(M, N);
+}
+
+int nvfp4_gemm_decode(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                      uint16_t *D, int M, int N, int K, void *workspace, size_t workspace_bytes, void *stream) {
+    return decode_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, workspace, workspace_bytes,
+                           static_cast<cudaStream_t>(stream));
 }
 
 int nvfp4_gemm_f16(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,

@@ -1,0 +1,368 @@
+// gemm_decode.cu — stream-K, swap-AB NVFP4 GEMM for skinny M (decode shapes).
+//
+// For M <= 128, D = alpha * A . B^T is HBM-bound: the weight B (N x K/2 bytes plus
+// scales) is read once and dominates the traffic.  The reference cannot run these
+// shapes at all (M < 128 gives zero tiles, matmul/sm100_nvfp4/nvfp4_v5.cu:163-176).
+//
+// Design:
+//   * swap-AB: the MMA computes D^T tiles = B_tile[128 x K] . A[MPAD x K]^T with
+//     tcgen05 kind::mxf4nvf4 (M = 128 weight rows, N = MPAD activation rows, MPAD in
+//     {8,16,32,64,128}); weights stream from HBM (evict-first), the small activation
+//     matrix stays L2-resident (evict-last);
+//   * stream-K: the n_tiles x k_blocks iteration space is cut into one contiguous
+//     range per CTA (grid = #SMs), so every SM streams the same number of bytes;
+//   * a tile whose k-range is split across CTAs is finished by the last contributor,
+//     which adds the fp32 partials in CTA order (deterministic) — partials and
+//     per-tile arrival counters live in a caller-provided workspace that the kernel
+//     leaves zeroed again;
+//   * deep TMA ring (up to 10 stages) to keep enough bytes in flight per SM;
+//   * bounded waits as in gemm.cu.
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace nvfp4 {
+namespace decode {
+
+constexpr int kTileN = 128;          // weight rows per tile (MMA M)
+constexpr int kBlockKBytes = 128;    // 256 fp4 per stage row
+constexpr int kKGroups = 4;
+constexpr int kThreads = 32 * 6;     // producer, MMA, 4 epilogue warps
+constexpr int kSmemBudget = 225 * 1024;
+
+template <int MPAD>
+struct Layout {
+    static constexpr int kW = kTileN * kBlockKBytes;     // 16 KB
+    static constexpr int kX = MPAD * kBlockKBytes;       // 1..16 KB
+    static constexpr int kSfw = kKGroups * 512;          // 2 KB
+    static constexpr int kSfx = kKGroups * 512;          // 2 KB (one 128-row scale block)
+    static constexpr int kStage = kW + kX + kSfw + kSfx;
+    static constexpr int STAGES = (kSmemBudget - 2048) / kStage > 10 ? 10 : (kSmemBudget - 2048) / kStage;
+    static constexpr int kOffW = 0;
+    static constexpr int kOffX = kOffW + STAGES * kW;
+    static constexpr int kOffSfw = kOffX + STAGES * kX;
+    static constexpr int kOffSfx = kOffSfw + STAGES * kSfw;
+    static constexpr int kOffBar = kOffSfx + STAGES * kSfx;
+    static constexpr int kBarBytes = (2 * STAGES + 3) * 8 + 32;
+    static constexpr int kDynamicSmem = kOffBar + kBarBytes + 1024;
+    static constexpr int kSfColsPerStage = kKGroups * 8;  // SFw 4 + SFx 4 per k-group
+    static constexpr int kTmemCols = MPAD + 2 * kSfColsPerStage <= 128 ? 128 : 256;
+    static_assert(MPAD % 8 == 0 && MPAD <= 128, "MPAD");
+    static_assert(MPAD + 2 * kSfColsPerStage <= kTmemCols, "tensor memory budget");
+    static_assert(kDynamicSmem <= 232448, "shared memory budget");
+};
+
+struct Params {
+    const uint8_t *sfa;  // activations' scales (blocked, pad128(M) rows)
+    const uint8_t *sfb;  // weights' scales
+    uint16_t *d;         // [M, N] bf16
+    float *partials;     // [grid][2][MPAD][128] fp32
+    int *counters;       // [n_tiles], zero between calls
+    int M, N, K;
+    float alpha;
+    int n_tiles, num_kb, k_groups;
+    int64_t total_iters;
+    int grid;
+    KernelCtl ctl;
+};
+
+__device__ __forceinline__ int64_t range_begin(int64_t c, const Params &p) { return c * p.total_iters / p.grid; }
+
+// CTA whose range holds iteration `it` (ranges are [begin(c), begin(c+1))).
+__device__ __forceinline__ int owner_of(int64_t it, const Params &p) {
+    return (int)(((it + 1) * p.grid - 1) / p.total_iters);
+}
+
+template <int MPAD>
+__global__ void __launch_bounds__(kThreads, 1)
+    nvfp4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                        const Params p) {
+    using L = Layout<MPAD>;
+    constexpr int S = L::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    uint8_t *base_ptr = smem_raw + (base - smem_u32(smem_raw));
+    const uint32_t sW = base + L::kOffW, sX = base + L::kOffX, sSfw = base + L::kOffSfw, sSfx = base + L::kOffSfx;
+    const uint32_t bar_full = base + L::kOffBar, bar_empty = bar_full + 8 * S;
+    const uint32_t bar_acc_full = bar_empty + 8 * S, bar_acc_empty = bar_acc_full + 8, bar_drain = bar_acc_empty + 8;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(base_ptr + L::kOffBar + (2 * S + 3) * 8);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    volatile int *last_flag = reinterpret_cast<volatile int *>(tmem_slot + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        mbar_init(bar_acc_full, 1);
+        mbar_init(bar_acc_empty, 4);
+        mbar_init(bar_drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tmap(&tmap_w);
+        prefetch_tmap(&tmap_x);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint64_t tmo = p.ctl.wait_timeout_ns;
+    const int64_t it_begin = range_begin(blockIdx.x, p), it_end = range_begin(blockIdx.x + 1, p);
+    const int64_t rest_k = p.K >> 6;
+
+    if (warp == 0) {
+        if (elect_one()) {
+            const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
+            bool ok = true;
+            uint32_t issued_mask = 0, issued_parity = 0, i = 0;
+            for (int64_t it = it_begin; it < it_end; it++, i++) {
+                const int s = i % S;
+                const uint32_t ph = (i / S) & 1;
+                if (!wait_parity(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
+                    report_timeout(abort_flag, p.ctl.status);
+                    ok = false;
+                    break;
+                }
+                const int tile = (int)(it / p.num_kb), kb = (int)(it % p.num_kb);
+                const int kg = min(kKGroups, p.k_groups - kb * kKGroups);
+                mbar_arrive_expect_tx(bar_full + 8 * s, L::kW + L::kX + 2u * kg * 512u);
+                issued_mask |= 1u << s;
+                issued_parity = (issued_parity & ~(1u << s)) | (ph << s);
+                tma_load_2d_hint(sW + s * L::kW, &tmap_w, bar_full + 8 * s, kb * kBlockKBytes, tile * kTileN, pol_w);
+                tma_load_2d_hint(sX + s * L::kX, &tmap_x, bar_full + 8 * s, kb * kBlockKBytes, 0, pol_x);
+                bulk_load_hint(sSfw + s * L::kSfw, p.sfb + ((int64_t)tile * rest_k + kb * kKGroups) * 512, kg * 512u,
+                               bar_full + 8 * s, pol_w);
+                bulk_load_hint(sSfx + s * L::kSfx, p.sfa + (int64_t)kb * kKGroups * 512, kg * 512u, bar_full + 8 * s,
+                               pol_x);
+            }
+            if (!ok) {
+                volatile int never = 0;
+                for (int s = 0; s < S; s++)
+                    if (issued_mask & (1u << s))
+                        wait_parity(bar_full + 8 * s, (issued_parity >> s) & 1, p.ctl.drain_timeout_ns, &never);
+            }
+        }
+    } else if (warp == 1) {
+        if (elect_one()) {
+            constexpr uint32_t idesc = idesc_mxf4nvf4(kTileN, MPAD);
+            bool ok = true, any = false;
+            uint32_t i = 0;
+            int seg = 0;
+            for (int64_t it = it_begin; ok && it < it_end; seg++) {
+                const int tile = (int)(it / p.num_kb);
+                const int64_t seg_end = min(it_end, (int64_t)(tile + 1) * p.num_kb);
+                if (!wait_parity(bar_acc_empty, (seg & 1) ^ 1, tmo, abort_flag)) {
+                    report_timeout(abort_flag, p.ctl.status);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                bool first = true;
+                for (; it < seg_end; it++, i++) {
+                    const int s = i % S;
+                    if (!wait_parity(bar_full + 8 * s, (i / S) & 1, tmo, abort_flag)) {
+                        report_timeout(abort_flag, p.ctl.status);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const int kb = (int)(it % p.num_kb);
+                    const int kg = min(kKGroups, p.k_groups - kb * kKGroups);
+                    const uint32_t sf_cols = tmem_base + MPAD + (i & 1) * L::kSfColsPerStage;
+                    for (int j = 0; j < kg; j++) {
+                        const uint32_t col = sf_cols + j * 8;
+                        tmem_cp_32x128_x4(col, smem_desc(sSfw + s * L::kSfw + j * 512, 16, 128, 0));
+                        tmem_cp_32x128_x4(col + 4, smem_desc(sSfx + s * L::kSfx + j * 512, 16, 128, 0));
+                        mma_mxf4nvf4(tmem_base, smem_desc(sW + s * L::kW + j * 32, 16, 1024, 2),
+                                     smem_desc(sX + s * L::kX + j * 32, 16, 1024, 2), idesc, col, col + 4,
+                                     !(first && j == 0));
+                    }
+                    first = false;
+                    any = true;
+                    mma_commit(bar_empty + 8 * s);
+                }
+                if (!ok) break;
+                mma_commit(bar_acc_full);
+            }
+            if (!ok && any) {
+                volatile int never = 0;
+                mma_commit(bar_drain);
+                wait_parity(bar_drain, 0, p.ctl.drain_timeout_ns, &never);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (warps 2..5)
+        const int quarter = warp & 3;
+        const int nl = quarter * 32 + lane;  // row of the weight tile this thread owns
+        const int etid = threadIdx.x - 64;   // 0..127
+        int seg = 0;
+        for (int64_t it = it_begin; it < it_end; seg++) {
+            const int tile = (int)(it / p.num_kb);
+            const int64_t tile_first = (int64_t)tile * p.num_kb, tile_last = tile_first + p.num_kb - 1;
+            const int64_t seg_end = min(it_end, tile_last + 1);
+            const bool whole = (it == tile_first) && (seg_end == tile_last + 1);
+            const int slot = (it == it_begin) ? 0 : 1;
+            it = seg_end;
+
+            bool ok = true;
+            if (lane == 0) ok = wait_parity(bar_acc_full, seg & 1, tmo, abort_flag);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0) report_timeout(abort_flag, p.ctl.status);
+                break;
+            }
+            tc_fence_after();
+            uint32_t acc[MPAD];
+            tmem_ld_cols<MPAD>(tmem_base + ((uint32_t)(quarter * 32) << 16), acc);
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_acc_empty);
+
+            const int n = tile * kTileN + nl;
+            float sum[MPAD];
+            if (whole) {
+#pragma unroll
+                for (int m = 0; m < MPAD; m++) sum[m] = __uint_as_float(acc[m]);
+            } else {
+                // publish this CTA's partial, then count arrivals on the tile
+                float *mine = p.partials + ((int64_t)blockIdx.x * 2 + slot) * MPAD * kTileN;
+#pragma unroll
+                for (int m = 0; m < MPAD; m++) __stcg(mine + m * kTileN + nl, __uint_as_float(acc[m]));
+                __threadfence();
+                named_barrier(1, 128);
+                if (etid == 0) {
+                    const int c_lo = owner_of(tile_first, p), c_hi = owner_of(tile_last, p);
+                    const int prev = atomicAdd(p.counters + tile, 1);
+                    *last_flag = (prev + 1 == c_hi - c_lo + 1);
+                    __threadfence();
+                }
+                named_barrier(1, 128);
+                if (!*last_flag) continue;
+                // last contributor: add every partial (its own included, re-read from L2)
+                // in CTA order, so the result does not depend on who finished last
+                const int c_lo = owner_of(tile_first, p), c_hi = owner_of(tile_last, p);
+#pragma unroll
+                for (int m = 0; m < MPAD; m++) sum[m] = 0.0f;
+                for (int c = c_lo; c <= c_hi; c++) {
+                    const int cslot = ((int)(range_begin(c, p) / p.num_kb) == tile) ? 0 : 1;
+                    const float *part = p.partials + ((int64_t)c * 2 + cslot) * MPAD * kTileN;
+#pragma unroll
+                    for (int m = 0; m < MPAD; m++) sum[m] += __ldcg(part + m * kTileN + nl);
+                }
+                if (etid == 0) p.counters[tile] = 0;  // reusable by the next call
+            }
+            if (n < p.N) {
+#pragma unroll
+                for (int m = 0; m < MPAD; m++)
+                    if (m < p.M) {
+                        __nv_bfloat16 v = __float2bfloat16_rn(sum[m] * p.alpha);
+                        p.d[(int64_t)m * p.N + n] = *reinterpret_cast<uint16_t *>(&v);
+                    }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, L::kTmemCols);
+    }
+}
+
+static int act_map(const void *ptr, int64_t rows, int64_t K, int box_rows, CUtensorMap *out) {
+    return encode_tiled_2d(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, ptr, (uint64_t)(K / 2), (uint64_t)rows,
+                           (uint64_t)(K / 2), kBlockKBytes, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int mpad_for(int M) {
+    int m = 8;
+    while (m < M) m *= 2;
+    return m;
+}
+
+size_t workspace_bytes(int M, int N, int sm_count) {
+    const int mpad = mpad_for(M);
+    const size_t n_tiles = (size_t)(N + kTileN - 1) / kTileN;
+    const size_t counters = (n_tiles * sizeof(int) + 255) / 256 * 256;
+    return counters + (size_t)sm_count * 2 * mpad * kTileN * sizeof(float);
+}
+
+template <int MPAD>
+static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                  uint16_t *D, int M, int N, int K, void *ws, cudaStream_t stream, const DeviceInfo &di) {
+    using L = Layout<MPAD>;
+    auto kern = nvfp4_decode_kernel<MPAD>;
+    static int configured[64] = {};
+    if (!configured[di.device]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamicSmem) != cudaSuccess)
+            return NVFP4_ERR_CUDA;
+        configured[di.device] = 1;
+    }
+    CUtensorMap tw, tx;
+    int st = act_map(B, N, K, kTileN, &tw);
+    if (!st) st = act_map(A, M, K, MPAD, &tx);
+    if (st) return st;
+    Params p;
+    p.sfa = SFA;
+    p.sfb = SFB;
+    p.d = D;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.alpha = alpha;
+    p.n_tiles = (N + kTileN - 1) / kTileN;
+    p.num_kb = (K + 255) / 256;
+    p.k_groups = K / 64;
+    p.total_iters = (int64_t)p.n_tiles * p.num_kb;
+    p.grid = (int)std::min<int64_t>(di.sm_count, p.total_iters);
+    const size_t counters = ((size_t)p.n_tiles * sizeof(int) + 255) / 256 * 256;
+    p.counters = static_cast<int *>(ws);
+    p.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + counters);
+    if ((st = kernel_ctl(&p.ctl))) return st;
+    kern<<<p.grid, kThreads, L::kDynamicSmem, stream>>>(tw, tx, p);
+    count_launch();
+    return cuda_status(cudaGetLastError());
+}
+
+}  // namespace decode
+
+int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const void *D, int M,
+                  int N, int K);
+
+size_t decode_workspace_bytes(int M, int N) {
+    DeviceInfo di;
+    if (device_info(&di)) return 0;
+    return decode::workspace_bytes(M, N, di.sm_count);
+}
+
+int decode_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                    uint16_t *D, int M, int N, int K, void *ws, size_t ws_bytes, cudaStream_t stream) {
+    int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
+    if (st) return st;
+    if (M > 128) return NVFP4_ERR_SHAPE;
+    DeviceInfo di;
+    if ((st = device_info(&di))) return st;
+    if (!ws || ws_bytes < decode::workspace_bytes(M, N, di.sm_count) ||
+        (reinterpret_cast<uintptr_t>(ws) & 255u))
+        return NVFP4_ERR_WORKSPACE;
+    switch (decode::mpad_for(M)) {
+        case 8: return decode::launch<8>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
+        case 16: return decode::launch<16>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
+        case 32: return decode::launch<32>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
+        case 64: return decode::launch<64>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
+        default: return decode::launch<128>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
+    }
+}
+
+}  // namespace nvfp4

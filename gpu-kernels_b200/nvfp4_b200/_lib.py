@@ -19,6 +19,10 @@ SIGNATURES = {
     "nvfp4_global_scale": (C.c_int, [_u16p, C.c_int64, _f32p, _f32p, _vp]),
     "nvfp4_gemm": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp]),
     "nvfp4_gemm_f16": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp]),
+    "nvfp4_gemm_persistent": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp]),
+    "nvfp4_gemm_decode_workspace_size": (C.c_size_t, [C.c_int, C.c_int]),
+    "nvfp4_gemm_decode": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp,
+                                    C.c_size_t, _vp]),
     "matmul_nvfp4_b200": (None, [_vp, _u8p, _u8p, _u8p, _u8p, C.c_int, C.c_int, C.c_int]),
     "nvfp4_last_status": (C.c_int, []),
     "nvfp4_device_status": (C.c_int, [_vp]),

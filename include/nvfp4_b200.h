@@ -36,6 +36,7 @@
 #ifndef NVFP4_B200_H
 #define NVFP4_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -91,11 +92,32 @@ NVFP4_API int nvfp4_global_scale(const uint16_t *X, int64_t n, float *amax_out, 
  * NVFP4 GEMM, D = alpha * A . B^T, bf16 out.  Replaces the reference's best B200
  * launcher matmul_nvfp4_v5 (matmul/sm100_nvfp4/nvfp4_v5.cu:287-309, declared at
  * block_scaled_nvfp4.cuh:15-16), adding alpha, bf16 output, a stream, any
- * M >= 1 / N % 8 / K % 64 shape and a status code.  Runs the persistent,
- * warp-specialised tcgen05 kernel; allocates nothing.
+ * M >= 1 / N % 8 / K % 64 shape and a status code.  For M > 128 it runs the
+ * persistent, warp-specialised tcgen05 kernel (nvfp4_gemm_persistent).  For
+ * M <= 128 (decode shapes; env NVFP4_DECODE_MAX_M lowers the bound, 0 disables)
+ * it runs the stream-K decode kernel (nvfp4_gemm_decode) with a workspace that
+ * this function allocates with cudaMalloc on the first such call per (device,
+ * stream) and keeps; make that first call outside CUDA-graph capture.
  */
 NVFP4_API int nvfp4_gemm(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
                float alpha, uint16_t *D, int M, int N, int K, void *stream);
+
+/* The persistent tensor-core kernel alone (any M), no workspace, no allocation. */
+NVFP4_API int nvfp4_gemm_persistent(const uint8_t *A, const uint8_t *SFA, const uint8_t *B,
+               const uint8_t *SFB, float alpha, uint16_t *D, int M, int N, int K, void *stream);
+
+/*
+ * Skinny-M (1 <= M <= 128) split-K / stream-K GEMM, bf16 out, judged on HBM GB/s.
+ * Replaces nothing that runs in the reference: its launchers produce zero tiles
+ * for M < 128 (matmul/sm100_nvfp4/nvfp4_v5.cu:163-176, 287-309).
+ * `workspace` (256-byte aligned, >= nvfp4_gemm_decode_workspace_size(M, N) bytes)
+ * must be zero-filled before its first use; every call leaves it zeroed again.
+ * Calls that share a workspace must be ordered (same stream); overlapping calls race.
+ */
+NVFP4_API size_t nvfp4_gemm_decode_workspace_size(int M, int N);
+NVFP4_API int nvfp4_gemm_decode(const uint8_t *A, const uint8_t *SFA, const uint8_t *B,
+               const uint8_t *SFB, float alpha, uint16_t *D, int M, int N, int K, void *workspace,
+               size_t workspace_bytes, void *stream);
 
 /* Same contract, fp16 output (the reference's output type). */
 NVFP4_API int nvfp4_gemm_f16(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
