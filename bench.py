@@ -240,6 +240,81 @@ def run_reference(args):
     return 0
 
 
+def decode_section(nv, dev, pk, reps=20):
+    """skinny-M GEMMs against the two FFN weights, judged on HBM
+    GB/s.  Weights rotate over 3 sets (> 3x L2); bytes per call follow the algorithmic
+    count N*K/2 + N*K/16 + M*K/2 + M*K/16 + 2*M*N."""
+    out = []
+    g = torch.Generator(device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for (N, K) in ((28672, 8192), (8192, 28672)):
+        ws = []
+        for i in range(3):
+            g.manual_seed(77 + i)
+            w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            _, gs = nv.global_scale(w)
+            ws.append(nv.quantize(w, gs))
+            del w
+        for M in (1, 16, 64, 128):
+            g.manual_seed(5 + M)
+            x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+            _, gsx = nv.global_scale(x)
+            xq, xsf = nv.quantize(x, gsx)
+            d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            for i in range(3):
+                nv.gemm(xq, xsf, ws[i % 3][0], ws[i % 3][1], 1.0, out=d)
+            torch.cuda.synchronize()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+            ev[0].record(stream)
+            for i in range(reps):
+                nv.gemm(xq, xsf, ws[i % 3][0], ws[i % 3][1], 1.0, out=d)
+                ev[i + 1].record(stream)
+            torch.cuda.synchronize()
+            times = sorted(ev[i].elapsed_time(ev[i + 1]) for i in range(reps))
+            us = 1e3 * statistics.median(times)
+            nbytes = N * K // 2 + N * K // 16 + M * K // 2 + M * K // 16 + 2 * M * N
+            out.append({"M": M, "N": N, "K": K, "us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1),
+                        "frac_hbm": round(nbytes / us / 1e3 / pk["hbm_gbs"], 3)})
+        del ws
+    nv.device_status()
+    return {"unit": "GB/s", "peak_gbs": pk["hbm_gbs"], "peak_basis": pk["source"] + " HBM copy", "shapes": out}
+
+
+def run_decode_workload(args, M, N, K):
+    """One skinny-M shape alone (for profiling): weights rotate over 3 sets."""
+    import nvfp4_b200 as nv
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    ws = []
+    for i in range(3):
+        g.manual_seed(77 + i)
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        _, gs = nv.global_scale(w)
+        ws.append(nv.quantize(w, gs))
+        del w
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    _, gsx = nv.global_scale(x)
+    xq, xsf = nv.quantize(x, gsx)
+    d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    for i in range(args.warmup):
+        nv.gemm(xq, xsf, ws[i % 3][0], ws[i % 3][1], 1.0, out=d)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        nv.gemm(xq, xsf, ws[i % 3][0], ws[i % 3][1], 1.0, out=d)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    nv.device_status()
+    us = 1e3 * e0.elapsed_time(e1) / args.steps
+    nbytes = N * K // 2 + N * K // 16 + M * K // 2 + M * K // 16 + 2 * M * N
+    print(json.dumps({"metric": "decode NVFP4 GEMM HBM GB/s", "value": nbytes / us / 1e3, "unit": "GB/s",
+                      "us_per_call": us, "config": {"M": M, "N": N, "K": K}, "steps": args.steps}), flush=True)
+    return 0
+
+
 def run_ours(args):
     import nvfp4_b200 as nv
     world, rank, local = dist_setup(args)
@@ -318,6 +393,9 @@ def run_ours(args):
     fp4_peak_est = 4.0 * pk["bf16_tflops"]
     traffic = committed_traffic().get("gemm_8192", {}).get("dram_bytes_per_launch")
     cpu = None
+    decode = None
+    if not args.no_decode:
+        decode = decode_section(nv, dev, pk)
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu, _, _ = cpu_reference_sample(a, sfa, b, sfb, alpha, M, N, K, target_s=args.cpu_seconds)
 
@@ -344,6 +422,8 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if decode is not None:
+            line["decode"] = decode
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
@@ -360,11 +440,17 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--sets", type=int, default=0, help="operand sets to rotate (default: > 3x L2)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode-shape GB/s section")
+    ap.add_argument("--workload", default="square",
+                    help="square (default, the bench line) or decode:M:N:K (one skinny shape, for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload.startswith("decode:"):
+        M, N, K = (int(v) for v in args.workload.split(":")[1:])
+        return run_decode_workload(args, M, N, K)
     return run_ours(args)
 
 

@@ -13,6 +13,8 @@ namespace nvfp4 {
 int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                   int M, int N, int K, cudaStream_t stream, bool f16);
 size_t decode_workspace_bytes(int M, int N);
+int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const void *D, int M,
+                  int N, int K);
 int decode_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                     uint16_t *D, int M, int N, int K, void *ws, size_t ws_bytes, cudaStream_t stream);
 }  // namespace nvfp4
@@ -68,10 +70,12 @@ extern "C" {
 int nvfp4_gemm(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, uint16_t *D,
                int M, int N, int K, void *stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (M >= 1 && M <= decode_max_m() && A && SFA && B && SFB && D) {
+    int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
+    if (st) return st;
+    if (M <= decode_max_m()) {
         void *ws = nullptr;
         size_t bytes = 0;
-        int st = internal_workspace(M, N, s, &ws, &bytes);
+        st = internal_workspace(M, N, s, &ws, &bytes);
         if (st) return st;
         return decode_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, ws, bytes, s);
     }

@@ -20,6 +20,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -90,6 +92,39 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool f16) {
     }
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Convert this thread's kCols accumulator columns (one output row) with alpha and
+// store them to D[row, col0 .. col0+kCols), clipped to N.
+template <int kCols, bool F16>
+__device__ __forceinline__ void store_row(const uint32_t (&acc)[kCols], const Params &p, int row, int col0) {
+    if (row >= p.M) return;
+    uint8_t *drow = static_cast<uint8_t *>(p.d) + ((int64_t)row * p.N + col0) * 2;
+    if (p.vec32_store) {
+#pragma unroll
+        for (int c = 0; c < kCols / 16; c++) {
+            if (col0 + c * 16 < p.N) {
+                uint32_t v[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+                    v[i] = pack2(__uint_as_float(acc[c * 16 + 2 * i]) * p.alpha,
+                                 __uint_as_float(acc[c * 16 + 2 * i + 1]) * p.alpha, F16);
+                st_global_v8(drow + c * 32, v);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < kCols / 8; c++) {
+            if (col0 + c * 8 < p.N) {
+                uint4 v;
+                v.x = pack2(__uint_as_float(acc[c * 8 + 0]) * p.alpha, __uint_as_float(acc[c * 8 + 1]) * p.alpha, F16);
+                v.y = pack2(__uint_as_float(acc[c * 8 + 2]) * p.alpha, __uint_as_float(acc[c * 8 + 3]) * p.alpha, F16);
+                v.z = pack2(__uint_as_float(acc[c * 8 + 4]) * p.alpha, __uint_as_float(acc[c * 8 + 5]) * p.alpha, F16);
+                v.w = pack2(__uint_as_float(acc[c * 8 + 6]) * p.alpha, __uint_as_float(acc[c * 8 + 7]) * p.alpha, F16);
+                *reinterpret_cast<uint4 *>(drow + c * 16) = v;
+            }
+        }
+    }
 }
 
 template <int BN, int STAGES, bool F16>
@@ -256,40 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_acc_empty);  // accumulator may be overwritten now
 
-            const int row = tm * kBlockM + quarter * 32 + lane;
-            const int col0 = tn * BN + half * kCols;
-            if (row < p.M) {
-                uint8_t *drow = static_cast<uint8_t *>(p.d) + ((int64_t)row * p.N + col0) * 2;
-                if (p.vec32_store) {
-#pragma unroll
-                    for (int c = 0; c < kCols / 16; c++) {
-                        if (col0 + c * 16 < p.N) {
-                            uint32_t v[8];
-#pragma unroll
-                            for (int i = 0; i < 8; i++)
-                                v[i] = pack2(__uint_as_float(acc[c * 16 + 2 * i]) * p.alpha,
-                                             __uint_as_float(acc[c * 16 + 2 * i + 1]) * p.alpha, F16);
-                            st_global_v8(drow + c * 32, v);
-                        }
-                    }
-                } else {
-#pragma unroll
-                    for (int c = 0; c < kCols / 8; c++) {
-                        if (col0 + c * 8 < p.N) {
-                            uint4 v;
-                            v.x = pack2(__uint_as_float(acc[c * 8 + 0]) * p.alpha,
-                                        __uint_as_float(acc[c * 8 + 1]) * p.alpha, F16);
-                            v.y = pack2(__uint_as_float(acc[c * 8 + 2]) * p.alpha,
-                                        __uint_as_float(acc[c * 8 + 3]) * p.alpha, F16);
-                            v.z = pack2(__uint_as_float(acc[c * 8 + 4]) * p.alpha,
-                                        __uint_as_float(acc[c * 8 + 5]) * p.alpha, F16);
-                            v.w = pack2(__uint_as_float(acc[c * 8 + 6]) * p.alpha,
-                                        __uint_as_float(acc[c * 8 + 7]) * p.alpha, F16);
-                            *reinterpret_cast<uint4 *>(drow + c * 16) = v;
-                        }
-                    }
-                }
-            }
+            store_row<kCols, F16>(acc, p, tm * kBlockM + quarter * 32 + lane, tn * BN + half * kCols);
         }
     }
 
@@ -299,6 +301,233 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem_base, L::kTmemCols);
+    }
+}
+
+
+// ---------------------------------------------------------------------------
+// CTA-pair kernel: tcgen05 cta_group::2, one 256x256 output tile per pair.
+//
+// CTA rank r of the pair holds A rows [256*tm + 128*r, +128), B rows
+// [256*tn + 128*r, +128), the 128-row scale block of its A rows and both 128-row
+// scale blocks of the tile's B rows.  Its producer loads those into its own smem
+// with cta_group::2 TMA loads whose bytes complete on the LEADER's (rank 0) full
+// barrier; the leader's MMA thread issues the pair MMAs (M=256, N=256, K=64) and
+// the scale copies, and commits separately to each CTA's empty / acc_full
+// barriers.  Both CTAs' epilogues drain their own TMEM half and arrive on the
+// leader's acc_empty barrier.  Per CTA and stage: 16 + 16 + 2 + 4 KB.
+// ---------------------------------------------------------------------------
+template <int STAGES>
+struct PairLayout {
+    static constexpr int kA = kBlockM * kBlockKBytes;   // 16 KB: this CTA's 128 A rows
+    static constexpr int kB = 128 * kBlockKBytes;       // 16 KB: this CTA's 128 B rows
+    static constexpr int kSfa = kKGroups * 512;         // 2 KB
+    static constexpr int kSfb = 2 * kKGroups * 512;     // 4 KB: both 128-row blocks of the tile
+    static constexpr int kStage = kA + kB + kSfa + kSfb;
+    static constexpr int kOffA = 0;
+    static constexpr int kOffB = kOffA + STAGES * kA;
+    static constexpr int kOffSfa = kOffB + STAGES * kB;
+    static constexpr int kOffSfb = kOffSfa + STAGES * kSfa;
+    static constexpr int kOffBar = kOffSfb + STAGES * kSfb;
+    static constexpr int kBarBytes = (2 * STAGES + 3) * 8 + 16;
+    static constexpr int kDynamicSmem = kOffBar + kBarBytes + 1024;
+    static constexpr int kSfColsPerGroup = 12;           // SFA 4 + SFB 8
+    static constexpr int kSfColsPerStage = kKGroups * kSfColsPerGroup;
+    static constexpr int kTmemCols = 512;
+    static constexpr uint32_t kTxBytes = 2u * kStage;    // both CTAs complete on the leader's barrier
+    static_assert(256 + 2 * kSfColsPerStage <= kTmemCols, "tensor memory budget");
+    static_assert(kDynamicSmem <= 232448, "shared memory budget");
+};
+
+template <int STAGES, bool F16>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
+                           const Params p) {
+    using L = PairLayout<STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    uint8_t *base_ptr = smem_raw + (base - smem_u32(smem_raw));
+    const uint32_t sA = base + L::kOffA, sB = base + L::kOffB, sSfa = base + L::kOffSfa, sSfb = base + L::kOffSfb;
+    const uint32_t bar_full = base + L::kOffBar;
+    const uint32_t bar_empty = bar_full + 8 * STAGES;
+    const uint32_t bar_acc_full = bar_empty + 8 * STAGES;
+    const uint32_t bar_acc_empty = bar_acc_full + 8;
+    const uint32_t bar_drain = bar_acc_empty + 8;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(base_ptr + L::kOffBar + (2 * STAGES + 3) * 8);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+    const int n_m = (p.M + 255) / 256, n_n = (p.N + 255) / 256, n_tiles = n_m * n_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        mbar_init(bar_acc_full, 1);
+        mbar_init(bar_acc_empty, 2 * kEpiWarps);
+        mbar_init(bar_drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_b);
+        prefetch_tmap(&tmap_sfa);
+        prefetch_tmap(&tmap_sfb);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_slot), L::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint64_t tmo = p.ctl.wait_timeout_ns;
+    const uint32_t lead_full = map_to_cta(bar_full, 0);
+
+    // raster: groups of kGroupM/2 pair-rows of 256
+    auto coords = [&](int t, int &tm, int &tn) {
+        const int gm_max = kGroupM / 2;
+        const int per_group = gm_max * n_n;
+        const int g = t / per_group, first = g * gm_max, gm = min(n_m - first, gm_max), local = t - g * per_group;
+        tm = first + local % gm;
+        tn = local / gm;
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer (both CTAs)
+        if (elect_one()) {
+            const int rest_k = p.K >> 6;
+            uint32_t it = 0;
+            bool ok = true;
+            uint32_t issued_mask = 0, issued_parity = 0;
+            for (int t = pair; ok && t < n_tiles; t += num_pairs) {
+                int tm, tn;
+                coords(t, tm, tn);
+                const int arow = tm * 256 + rank * 128, brow = tn * 256 + rank * 128;
+                for (int kb = 0; kb < p.num_kb; kb++, it++) {
+                    const int s = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!wait_parity(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
+                        report_timeout(abort_flag, p.ctl.status);
+                        ok = false;
+                        break;
+                    }
+                    if (rank == 0) {
+                        mbar_arrive_expect_tx(bar_full + 8 * s, L::kTxBytes);
+                        issued_mask |= 1u << s;
+                        issued_parity = (issued_parity & ~(1u << s)) | (ph << s);
+                    }
+                    const uint32_t fb = lead_full + 8 * s;
+                    tma_load_2d_pair(sA + s * L::kA, &tmap_a, fb, kb * kBlockKBytes, arow);
+                    tma_load_2d_pair(sB + s * L::kB, &tmap_b, fb, kb * kBlockKBytes, brow);
+                    // scale tensors viewed as rows of 256 bytes: one (128-row block, k-stage) = 8 rows
+                    tma_load_2d_pair(sSfa + s * L::kSfa, &tmap_sfa, fb, 0,
+                                     ((tm * 2 + (int)rank) * rest_k + kb * kKGroups) * 2);
+                    tma_load_2d_pair(sSfb + s * L::kSfb, &tmap_sfb, fb, 0, ((tn * 2) * rest_k + kb * kKGroups) * 2);
+                    tma_load_2d_pair(sSfb + s * L::kSfb + kKGroups * 512, &tmap_sfb, fb, 0,
+                                     ((tn * 2 + 1) * rest_k + kb * kKGroups) * 2);
+                }
+            }
+            if (!ok && rank == 0) {
+                volatile int never = 0;
+                for (int s = 0; s < STAGES; s++)
+                    if (issued_mask & (1u << s))
+                        wait_parity(bar_full + 8 * s, (issued_parity >> s) & 1, p.ctl.drain_timeout_ns, &never);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer (leader only)
+        if (rank == 0 && elect_one()) {
+            constexpr uint32_t idesc = idesc_mxf4nvf4(256, 256);
+            const uint32_t empty0 = map_to_cta(bar_empty, 0), empty1 = map_to_cta(bar_empty, 1);
+            const uint32_t accf0 = map_to_cta(bar_acc_full, 0), accf1 = map_to_cta(bar_acc_full, 1);
+            uint32_t it = 0;
+            int local = 0;
+            bool ok = true, any_issued = false;
+            for (int t = pair; ok && t < n_tiles; t += num_pairs, local++) {
+                if (!wait_parity(bar_acc_empty, (local & 1) ^ 1, tmo, abort_flag)) {
+                    report_timeout(abort_flag, p.ctl.status);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int kb = 0; kb < p.num_kb; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!wait_parity(bar_full + 8 * s, (it / STAGES) & 1, tmo, abort_flag)) {
+                        report_timeout(abort_flag, p.ctl.status);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const int kg = min(kKGroups, p.k_groups - kb * kKGroups);
+                    const uint32_t sf_cols = tmem_base + 256 + (it & 1) * L::kSfColsPerStage;
+                    for (int j = 0; j < kg; j++) {
+                        const uint32_t col = sf_cols + j * L::kSfColsPerGroup;
+                        tmem_cp_32x128_x4_pair(col, smem_desc(sSfa + s * L::kSfa + j * 512, 16, 128, 0));
+                        tmem_cp_32x128_x4_pair(col + 4, smem_desc(sSfb + s * L::kSfb + j * 512, 16, 128, 0));
+                        tmem_cp_32x128_x4_pair(col + 8,
+                                               smem_desc(sSfb + s * L::kSfb + (kKGroups + j) * 512, 16, 128, 0));
+                        mma_mxf4nvf4_pair(tmem_base, smem_desc(sA + s * L::kA + j * 32, 16, 1024, 2),
+                                          smem_desc(sB + s * L::kB + j * 32, 16, 1024, 2), idesc, col, col + 4,
+                                          (kb | j) != 0);
+                    }
+                    any_issued = true;
+                    mma_commit_pair(empty0 + 8 * s);
+                    mma_commit_pair(empty1 + 8 * s);
+                }
+                if (!ok) break;
+                mma_commit_pair(accf0);
+                mma_commit_pair(accf1);
+            }
+            if (!ok && any_issued) {
+                volatile int never = 0;
+                mma_commit_pair(map_to_cta(bar_drain, 0));
+                wait_parity(bar_drain, 0, p.ctl.drain_timeout_ns, &never);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        constexpr int kCols = 128;
+        const uint32_t lead_acc_empty = map_to_cta(bar_acc_empty, 0);
+        int local = 0;
+        for (int t = pair; t < n_tiles; t += num_pairs, local++) {
+            int tm, tn;
+            coords(t, tm, tn);
+            bool ok = true;
+            if (lane == 0) ok = wait_parity(bar_acc_full, local & 1, tmo, abort_flag);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0) report_timeout(abort_flag, p.ctl.status);
+                break;
+            }
+            tc_fence_after();
+            uint32_t acc[kCols];
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * kCols;
+#pragma unroll
+            for (int c = 0; c < kCols / 32; c++)
+                tmem_ld_32x32b_x32(taddr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&acc[c * 32]));
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(lead_acc_empty);
+            store_row<kCols, F16>(acc, p, tm * 256 + (int)rank * 128 + quarter * 32 + lane, tn * 256 + half * kCols);
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();  // no CTA leaves while its peer may still signal it
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, L::kTmemCols);
     }
 }
 
@@ -384,6 +613,49 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     return cuda_status(cudaGetLastError());
 }
 
+template <int STAGES, bool F16>
+static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                       void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di) {
+    using L = PairLayout<STAGES>;
+    auto kern = nvfp4_gemm_pair_kernel<STAGES, F16>;
+    static int configured[64] = {};
+    if (!configured[di.device]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamicSmem) != cudaSuccess)
+            return NVFP4_ERR_CUDA;
+        configured[di.device] = 1;
+    }
+    CUtensorMap ta, tb, tsa, tsb;
+    int st = operand_map(A, M, K, kBlockM, &ta);
+    if (!st) st = operand_map(B, N, K, 128, &tb);
+    // scale tensors as [bytes/256, 256] so one (128-row block, 4 k-groups) chunk is an 8x256 box
+    const uint64_t sfa_rows = (uint64_t)((M + 127) / 128) * (K / 64) * 2;
+    const uint64_t sfb_rows = (uint64_t)((N + 127) / 128) * (K / 64) * 2;
+    if (!st) st = encode_tiled_2d(&tsa, CU_TENSOR_MAP_DATA_TYPE_UINT8, SFA, 256, sfa_rows, 256, 256, 8,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!st) st = encode_tiled_2d(&tsb, CU_TENSOR_MAP_DATA_TYPE_UINT8, SFB, 256, sfb_rows, 256, 256, 8,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    Params p;
+    p.sfa = SFA;
+    p.sfb = SFB;
+    p.d = D;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.alpha = alpha;
+    p.num_m_tiles = (M + 255) / 256;
+    p.num_n_tiles = (N + 255) / 256;
+    p.num_tiles = p.num_m_tiles * p.num_n_tiles;
+    p.num_kb = (K + 255) / 256;
+    p.k_groups = K / 64;
+    p.vec32_store = ((reinterpret_cast<uintptr_t>(D) & 31u) == 0) && (N % 16 == 0);
+    if ((st = kernel_ctl(&p.ctl))) return st;
+    const int pairs = std::min(p.num_tiles, di.sm_count / 2);
+    kern<<<2 * pairs, kThreads, L::kDynamicSmem, stream>>>(ta, tb, tsa, tsb, p);
+    count_launch();
+    return cuda_status(cudaGetLastError());
+}
+
 }  // namespace gemm
 
 int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const void *D, int M,
@@ -394,12 +666,30 @@ int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     return NVFP4_OK;
 }
 
+// Kernel choice for the persistent path: the CTA-pair kernel for M > 128, the
+// single-CTA kernel otherwise.  NVFP4_GEMM_VARIANT=single|pair forces one.
+static int gemm_variant(int M) {
+    static int forced = [] {
+        const char *e = std::getenv("NVFP4_GEMM_VARIANT");
+        if (!e) return 0;
+        if (!std::strcmp(e, "single")) return 1;
+        if (!std::strcmp(e, "pair")) return 2;
+        return 0;
+    }();
+    if (forced) return forced;
+    return M > 128 ? 2 : 1;
+}
+
 int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                   int M, int N, int K, cudaStream_t stream, bool f16) {
     int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
     if (st) return st;
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
+    if (gemm_variant(M) == 2) {
+        if (f16) return gemm::launch_pair<5, true>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di);
+        return gemm::launch_pair<5, false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di);
+    }
     if (f16) return gemm::launch<256, 4, true>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di);
     return gemm::launch<256, 4, false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di);
 }

@@ -144,3 +144,33 @@ def test_c2_full_size_sampled(nv, oracle, cuda_dev, N, K):
     check_against_oracle(oracle, d, a, sfa, b, sfb, alpha, M, N, K,
                          rows=[(0, 64), (4096 + 32, 64), (M - 64, 64)])
     assert not torch.isnan(d).any()
+
+
+@pytest.mark.parametrize("variant", ["single", "pair"])
+def test_forced_kernel_variant(variant, tmp_path):
+    """Both persistent kernels (single-CTA 128x256 and CTA-pair 256x256 tiles) on the
+    same ragged shape, each forced through NVFP4_GEMM_VARIANT in a fresh process."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = f"""
+import sys, numpy as np, torch
+sys.path[:0] = [{root!r}, {os.path.join(root, 'gpu-kernels_b200')!r}]
+import nvfp4_b200 as nv
+from oracle import oracle as o
+M, N, K = 520, 776, 1344
+a, sfa = o.random_codes(M, K, seed=1, sf_lo=0x30, sf_hi=0x40)
+b, sfb = o.random_codes(N, K, seed=2, sf_lo=0x30, sf_hi=0x40)
+t = lambda x: torch.from_numpy(x).cuda()
+d = nv.gemm(t(a), t(sfa), t(b), t(sfb), 0.5)
+torch.cuda.synchronize(); nv.device_status()
+_, d16 = o.gemm(a, sfa, b, sfb, 0.5, M, N, K)
+ref = o.bf16_bits_to_f32(d16).reshape(M, N)
+err = np.abs(d.float().cpu().numpy() - ref).max() / np.abs(ref).max()
+assert err <= 1e-2, err
+print("ok", err)
+"""
+    env = dict(os.environ, NVFP4_GEMM_VARIANT=variant)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
