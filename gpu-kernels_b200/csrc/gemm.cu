@@ -73,7 +73,13 @@ struct Params {
     int k_groups;     // K / 64
     int vec32_store;  // D 32-byte aligned and N % 16 == 0
     KernelCtl ctl;
+    // Optional per-CTA cycle trace (nullptr = off), kTraceSlots u64 per CTA:
+    // [0] MMA wait on full  [1] MMA wait on acc_empty  [2] producer wait on empty
+    // [3] epilogue wait on acc_full  [4] epilogue drain+store  [5] tiles
+    // [6] MMA-thread cycles from first issue to last commit  [7] unused
+    unsigned long long *trace;
 };
+constexpr int kTraceSlots = 8;
 
 __device__ __forceinline__ void tile_coords(int t, const Params &p, int &tm, int &tn) {
     const int per_group = kGroupM * p.num_n_tiles;
@@ -405,6 +411,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t it = 0;
             bool ok = true;
             uint32_t issued_mask = 0, issued_parity = 0;
+            long long t_wait = 0;
             for (int t = pair; ok && t < n_tiles; t += num_pairs) {
                 int tm, tn;
                 coords(t, tm, tn);
@@ -412,11 +419,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int kb = 0; kb < p.num_kb; kb++, it++) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
+                    const long long c0 = p.trace ? clock64() : 0;
                     if (!wait_parity(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
                         report_timeout(abort_flag, p.ctl.status);
                         ok = false;
                         break;
                     }
+                    if (p.trace) t_wait += clock64() - c0;
                     if (rank == 0) {
                         mbar_arrive_expect_tx(bar_full + 8 * s, L::kTxBytes);
                         issued_mask |= 1u << s;
@@ -439,6 +448,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     if (issued_mask & (1u << s))
                         wait_parity(bar_full + 8 * s, (issued_parity >> s) & 1, p.ctl.drain_timeout_ns, &never);
             }
+            if (p.trace) p.trace[blockIdx.x * kTraceSlots + 2] = t_wait;
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (leader only)
@@ -449,20 +459,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t it = 0;
             int local = 0;
             bool ok = true, any_issued = false;
+            long long t_full = 0, t_acc = 0, t_first = 0;
             for (int t = pair; ok && t < n_tiles; t += num_pairs, local++) {
+                long long c0 = p.trace ? clock64() : 0;
                 if (!wait_parity(bar_acc_empty, (local & 1) ^ 1, tmo, abort_flag)) {
                     report_timeout(abort_flag, p.ctl.status);
                     ok = false;
                     break;
                 }
+                if (p.trace) {
+                    const long long c1 = clock64();
+                    t_acc += c1 - c0;
+                    if (!t_first) t_first = c1;
+                }
                 tc_fence_after();
                 for (int kb = 0; kb < p.num_kb; kb++, it++) {
                     const int s = it % STAGES;
+                    c0 = p.trace ? clock64() : 0;
                     if (!wait_parity(bar_full + 8 * s, (it / STAGES) & 1, tmo, abort_flag)) {
                         report_timeout(abort_flag, p.ctl.status);
                         ok = false;
                         break;
                     }
+                    if (p.trace) t_full += clock64() - c0;
                     tc_fence_after();
                     const int kg = min(kKGroups, p.k_groups - kb * kKGroups);
                     const uint32_t sf_cols = tmem_base + 256 + (it & 1) * L::kSfColsPerStage;
@@ -489,6 +508,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 mma_commit_pair(map_to_cta(bar_drain, 0));
                 wait_parity(bar_drain, 0, p.ctl.drain_timeout_ns, &never);
             }
+            if (p.trace) {
+                unsigned long long *tr = p.trace + blockIdx.x * kTraceSlots;
+                tr[0] = t_full;
+                tr[1] = t_acc;
+                tr[5] = local;
+                tr[6] = clock64() - t_first;
+            }
         }
     } else {
         // ------------------------------------------------------------ epilogue (both CTAs)
@@ -497,12 +523,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         constexpr int kCols = 128;
         const uint32_t lead_acc_empty = map_to_cta(bar_acc_empty, 0);
         int local = 0;
+        long long t_accw = 0, t_store = 0, c_ready = 0;
         for (int t = pair; t < n_tiles; t += num_pairs, local++) {
             int tm, tn;
             coords(t, tm, tn);
             bool ok = true;
+            const long long c0 = p.trace ? clock64() : 0;
             if (lane == 0) ok = wait_parity(bar_acc_full, local & 1, tmo, abort_flag);
             ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (p.trace) {
+                c_ready = clock64();
+                t_accw += c_ready - c0;
+            }
             if (!ok) {
                 if (lane == 0) report_timeout(abort_flag, p.ctl.status);
                 break;
@@ -518,6 +550,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(lead_acc_empty);
             store_row<kCols, F16>(acc, p, tm * 256 + (int)rank * 128 + quarter * 32 + lane, tn * 256 + half * kCols);
+            if (p.trace && warp == 2 && lane == 0) t_store += clock64() - c_ready;
+        }
+        if (p.trace && warp == 2 && lane == 0) {
+            p.trace[blockIdx.x * kTraceSlots + 3] = t_accw;
+            p.trace[blockIdx.x * kTraceSlots + 4] = t_store;
         }
     }
 
@@ -606,6 +643,7 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     p.num_kb = (K + 255) / 256;
     p.k_groups = K / 64;
     p.vec32_store = ((reinterpret_cast<uintptr_t>(D) & 31u) == 0) && (N % 16 == 0);
+    p.trace = nullptr;
     if ((st = kernel_ctl(&p.ctl))) return st;
     const int grid = p.num_tiles < di.sm_count ? p.num_tiles : di.sm_count;
     kern<<<grid, kThreads, L::kDynamicSmem, stream>>>(ta, tb, p);
@@ -615,7 +653,8 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
 
 template <int STAGES, bool F16>
 static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
-                       void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di) {
+                       void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di,
+                       unsigned long long *trace = nullptr) {
     using L = PairLayout<STAGES>;
     auto kern = nvfp4_gemm_pair_kernel<STAGES, F16>;
     static int configured[64] = {};
@@ -649,6 +688,7 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     p.num_kb = (K + 255) / 256;
     p.k_groups = K / 64;
     p.vec32_store = ((reinterpret_cast<uintptr_t>(D) & 31u) == 0) && (N % 16 == 0);
+    p.trace = trace;
     if ((st = kernel_ctl(&p.ctl))) return st;
     const int pairs = std::min(p.num_tiles, di.sm_count / 2);
     kern<<<2 * pairs, kThreads, L::kDynamicSmem, stream>>>(ta, tb, tsa, tsb, p);
@@ -692,6 +732,17 @@ int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     }
     if (f16) return gemm::launch<256, 4, true>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di);
     return gemm::launch<256, 4, false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di);
+}
+
+// Pair kernel with the per-CTA cycle trace on (trace: 148 x kTraceSlots u64 on the device).
+int gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D, int M,
+               int N, int K, unsigned long long *trace, cudaStream_t stream) {
+    int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
+    if (st) return st;
+    if (!trace) return NVFP4_ERR_INVALID;
+    DeviceInfo di;
+    if ((st = device_info(&di))) return st;
+    return gemm::launch_pair<5, false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
 }
 
 }  // namespace nvfp4

@@ -1,0 +1,179 @@
+// probe.cu — measured tensor-core ceiling for kind::mxf4nvf4 on this GPU.
+//
+// No FP4 peak is published for this pool's B200s, so the roofline denominator is
+// measured here: every SM issues back-to-back tcgen05.mma kind::mxf4nvf4 MMAs on
+// operands already resident in shared memory (no HBM/L2 traffic), optionally with
+// the per-MMA scale-factor copies (tcgen05.cp) the GEMM kernels issue.  The result
+// (FLOP / elapsed device time) is the ceiling the GEMM's roofline.frac is taken
+// against, at whatever clock the GPU runs under this load.
+//
+// modes: 0 single-CTA M=128 N=256, MMA only
+//        1 single-CTA, 3 scale copies before each MMA (the GEMM kernels' order)
+//        2 CTA pair M=256 N=256, MMA only
+//        3 CTA pair, 3 scale copies before each MMA
+//        4 CTA pair, the 12 scale copies of a 4-MMA stage issued first, then 4 MMAs
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace nvfp4 {
+
+constexpr int kProbeSmem = 64 * 1024;
+
+template <int MODE>
+__global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, unsigned long long *cycles) {
+    constexpr bool kPair = MODE >= 2;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    __shared__ uint32_t tmem_slot;
+    __shared__ __align__(8) uint64_t bar;
+    const int warp = threadIdx.x >> 5;
+    // zero operands and scales: throughput does not depend on the values
+    for (int i = threadIdx.x * 16; i < kProbeSmem - 1024; i += blockDim.x * 16)
+        st_shared_v4(base + i, 0, 0, 0, 0);
+    fence_proxy_async_smem();
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        if (kPair) {
+            tmem_alloc_pair(smem_u32(&tmem_slot), 512);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(&tmem_slot), 512);
+            tmem_relinquish();
+        }
+    }
+    tc_fence_before();
+    if (kPair) cluster_sync(); else __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const uint32_t sA = base, sB = base + 16384, sSf = base + 49152;
+    const bool issuer = kPair ? (cluster_ctarank() == 0) : true;
+    if (warp == 0 && issuer && elect_one()) {
+        constexpr uint32_t idesc = idesc_mxf4nvf4(kPair ? 256 : 128, 256);
+        const unsigned long long t0 = clock64();
+        for (int i = 0; i < iters; i++) {
+            const int j = i & 3;
+            const uint32_t col = tmem + 256 + j * 12;
+            const uint64_t ad = smem_desc(sA + j * 32, 16, 1024, 2), bd = smem_desc(sB + j * 32, 16, 1024, 2);
+            if constexpr (MODE == 0) {
+                mma_mxf4nvf4(tmem, ad, bd, idesc, col, col + 4, i != 0);
+            } else if constexpr (MODE == 1) {
+                tmem_cp_32x128_x4(col, smem_desc(sSf + j * 512, 16, 128, 0));
+                tmem_cp_32x128_x4(col + 4, smem_desc(sSf + 2048 + j * 512, 16, 128, 0));
+                tmem_cp_32x128_x4(col + 8, smem_desc(sSf + 4096 + j * 512, 16, 128, 0));
+                mma_mxf4nvf4(tmem, ad, bd, idesc, col, col + 4, i != 0);
+            } else if constexpr (MODE == 2) {
+                mma_mxf4nvf4_pair(tmem, ad, bd, idesc, col, col + 4, i != 0);
+            } else if constexpr (MODE == 3) {
+                tmem_cp_32x128_x4_pair(col, smem_desc(sSf + j * 512, 16, 128, 0));
+                tmem_cp_32x128_x4_pair(col + 4, smem_desc(sSf + 2048 + j * 512, 16, 128, 0));
+                tmem_cp_32x128_x4_pair(col + 8, smem_desc(sSf + 4096 + j * 512, 16, 128, 0));
+                mma_mxf4nvf4_pair(tmem, ad, bd, idesc, col, col + 4, i != 0);
+            } else {
+                if (j == 0) {
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const uint32_t c = tmem + 256 + q * 12;
+                        tmem_cp_32x128_x4_pair(c, smem_desc(sSf + q * 512, 16, 128, 0));
+                        tmem_cp_32x128_x4_pair(c + 4, smem_desc(sSf + 2048 + q * 512, 16, 128, 0));
+                        tmem_cp_32x128_x4_pair(c + 8, smem_desc(sSf + 4096 + q * 512, 16, 128, 0));
+                    }
+                }
+                mma_mxf4nvf4_pair(tmem, ad, bd, idesc, col, col + 4, i != 0);
+            }
+        }
+        if (kPair) mma_commit_pair(smem_u32(&bar)); else mma_commit(smem_u32(&bar));
+        volatile int never = 0;
+        wait_parity(smem_u32(&bar), 0, 2000000000ull, &never);
+        const unsigned long long t1 = clock64();
+        atomicMax(cycles, t1 - t0);
+    }
+    __syncwarp();
+    tc_fence_before();
+    if (kPair) cluster_sync(); else __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        if (kPair) tmem_dealloc_pair(tmem, 512); else tmem_dealloc(tmem, 512);
+    }
+}
+
+template <int MODE>
+static int run_probe(int iters, int sms, cudaStream_t s, unsigned long long *cycles) {
+    auto kern = mma_probe_kernel<MODE>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kProbeSmem) != cudaSuccess)
+        return NVFP4_ERR_CUDA;
+    if (MODE >= 2) {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(sms / 2 * 2);
+        cfg.blockDim = dim3(128);
+        cfg.dynamicSmemBytes = kProbeSmem;
+        cfg.stream = s;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, kern, iters, cycles) != cudaSuccess) return NVFP4_ERR_CUDA;
+    } else {
+        kern<<<sms, 128, kProbeSmem, s>>>(iters, cycles);
+    }
+    count_launch();
+    return cuda_status(cudaGetLastError());
+}
+
+}  // namespace nvfp4
+
+using namespace nvfp4;
+
+// Runs the probe on every SM and returns the achieved dense FP4 rate in TFLOP/s
+// (FLOP of all MMAs / elapsed device time measured with CUDA events) and the
+// longest per-SM MMA-issue time in cycles.  Synchronous; allocates a few bytes.
+extern "C" NVFP4_API int nvfp4_probe_mma_rate(int mode, int iters, double *tflops, double *cycles_per_mma) {
+    if (mode < 0 || mode > 4 || iters < 16 || !tflops) return NVFP4_ERR_INVALID;
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    unsigned long long *dcyc = nullptr;
+    if (cudaMalloc(&dcyc, sizeof(*dcyc)) != cudaSuccess) return NVFP4_ERR_CUDA;
+    cudaMemset(dcyc, 0, sizeof(*dcyc));
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    auto go = [&](int it) {
+        switch (mode) {
+            case 0: return run_probe<0>(it, di.sm_count, nullptr, dcyc);
+            case 1: return run_probe<1>(it, di.sm_count, nullptr, dcyc);
+            case 2: return run_probe<2>(it, di.sm_count, nullptr, dcyc);
+            case 3: return run_probe<3>(it, di.sm_count, nullptr, dcyc);
+            default: return run_probe<4>(it, di.sm_count, nullptr, dcyc);
+        }
+    };
+    st = go(iters);  // warm-up (clocks ramp)
+    if (!st) {
+        cudaMemset(dcyc, 0, sizeof(*dcyc));
+        cudaEventRecord(e0);
+        st = go(iters);
+        cudaEventRecord(e1);
+    }
+    if (!st && cudaEventSynchronize(e1) != cudaSuccess) st = NVFP4_ERR_CUDA;
+    if (!st) {
+        float ms = 0;
+        cudaEventElapsedTime(&ms, e0, e1);
+        const bool pair = mode >= 2;
+        const int ctas = pair ? di.sm_count / 2 * 2 : di.sm_count;
+        // per MMA: 2 * M * N * K with M = 256 over a pair (128 per CTA), N = 256, K = 64
+        const double flop = (double)ctas * iters * 2.0 * 128 * 256 * 64;
+        *tflops = flop / (ms * 1e-3) / 1e12;
+        unsigned long long cyc = 0;
+        cudaMemcpy(&cyc, dcyc, sizeof(cyc), cudaMemcpyDeviceToHost);
+        if (cycles_per_mma) *cycles_per_mma = (double)cyc / iters;
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaFree(dcyc);
+    return st;
+}

@@ -1,0 +1,72 @@
+"""Diagnostics for the NVFP4 kernels on a B200.
+
+    python -m nvfp4_b200.diag probe [iters]        measured mxf4nvf4 tensor rate per issue mode
+    python -m nvfp4_b200.diag trace M N K           per-CTA cycle breakdown of the CTA-pair GEMM
+
+(run with gpu-kernels_b200/ on sys.path).  Each prints JSON lines.
+"""
+import ctypes as C
+import json
+import statistics
+import sys
+
+import torch
+
+from ._lib import check, lib
+
+PROBE_MODES = {0: "single-CTA MMA only", 1: "single-CTA MMA + 3 scale copies each",
+               2: "CTA-pair MMA only", 3: "CTA-pair MMA + 3 scale copies each",
+               4: "CTA-pair, 12 scale copies per 4-MMA stage first"}
+
+
+def probe(iters: int = 20000):
+    out = []
+    for mode, name in PROBE_MODES.items():
+        tf, cyc = C.c_double(), C.c_double()
+        check(lib().nvfp4_probe_mma_rate(mode, iters, C.byref(tf), C.byref(cyc)), "probe")
+        out.append({"mode": mode, "what": name, "tflops": round(tf.value, 1),
+                    "cycles_per_mma": round(cyc.value, 2)})
+    return out
+
+
+def trace(M: int, N: int, K: int):
+    from .ops import create_tensors
+    dev = torch.device("cuda", 0)
+    a, b, sfa, sfb = create_tensors(M, N, K, seed=1)
+    sfa = torch.full_like(sfa, 0x38)
+    sfb = torch.full_like(sfb, 0x38)
+    d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    tr = torch.zeros(148 * 8, dtype=torch.int64, device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    for _ in range(3):
+        check(lib().nvfp4_gemm_trace(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), 1.0, d.data_ptr(),
+                                     M, N, K, tr.data_ptr(), s), "trace")
+    torch.cuda.synchronize()
+    t = tr.view(148, 8).cpu()
+    leaders = t[0::2]
+    span = leaders[:, 6].double()
+    rows = {"mma_wait_full": leaders[:, 0], "mma_wait_acc": leaders[:, 1], "producer_wait_empty": t[:, 2],
+            "epi_wait_acc_full": t[:, 3], "epi_drain_store": t[:, 4]}
+    res = {"M": M, "N": N, "K": K, "tiles_per_pair": statistics.mean(leaders[:, 5].tolist()),
+           "mma_span_cycles": statistics.mean(span.tolist())}
+    for k, v in rows.items():
+        res[k + "_cycles"] = statistics.mean(v.double().tolist())
+        res[k + "_frac_of_span"] = res[k + "_cycles"] / res["mma_span_cycles"]
+    return res
+
+
+def main(argv):
+    if not argv or argv[0] not in ("probe", "trace"):
+        print(__doc__)
+        return 2
+    if argv[0] == "probe":
+        for r in probe(int(argv[1]) if len(argv) > 1 else 20000):
+            print(json.dumps(r))
+    else:
+        M, N, K = (int(x) for x in argv[1:4])
+        print(json.dumps(trace(M, N, K)))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main(sys.argv[1:]))

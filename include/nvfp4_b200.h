@@ -154,6 +154,24 @@ NVFP4_API void nvfp4_set_wait_timeout_ns(uint64_t ns);
  */
 NVFP4_API int nvfp4_selftest_wait_timeout(uint64_t timeout_ns);
 
+/*
+ * Diagnostics (no counterpart in the reference, which only has a host timer and
+ * an unused per-SM event recorder, matmul/sm100_nvfp4/profiler.cuh:4-72).
+ *
+ * nvfp4_gemm_trace: the CTA-pair GEMM with a per-CTA cycle trace written to
+ * `trace` (device, 148 x 8 uint64): [0] MMA wait on full stages, [1] MMA wait on
+ * a free accumulator, [2] producer wait on empty stages, [3] epilogue wait on a
+ * full accumulator, [4] epilogue drain + stores, [5] tiles, [6] MMA-thread span.
+ *
+ * nvfp4_probe_mma_rate: measured kind::mxf4nvf4 tensor rate on every SM with
+ * operands resident in shared memory (mode 0/1: single CTA without/with the
+ * scale copies; 2/3: CTA pair without/with; 4: pair, scale copies batched per
+ * 4-MMA stage).  Synchronous; returns TFLOP/s and cycles per MMA.
+ */
+NVFP4_API int nvfp4_gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+               float alpha, uint16_t *D, int M, int N, int K, uint64_t *trace, void *stream);
+NVFP4_API int nvfp4_probe_mma_rate(int mode, int iters, double *tflops, double *cycles_per_mma);
+
 /* Number of kernel launches this library has issued in this process. */
 NVFP4_API uint64_t nvfp4_launch_count(void);
 
