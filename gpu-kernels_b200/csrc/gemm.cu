@@ -341,11 +341,12 @@ struct PairLayout {
     static constexpr int kSfColsPerStage = kKGroups * kSfColsPerGroup;
     static constexpr int kTmemCols = 512;
     static constexpr uint32_t kTxBytes = 2u * kStage;    // both CTAs complete on the leader's barrier
-    static_assert(256 + 2 * kSfColsPerStage <= kTmemCols, "tensor memory budget");
+    // accumulator [0, 256), then one set of scale columns per ring stage
+    static_assert(256 + STAGES * kSfColsPerStage <= kTmemCols, "tensor memory budget");
     static_assert(kDynamicSmem <= 232448, "shared memory budget");
 };
 
-template <int STAGES, bool F16>
+template <int STAGES, bool F16, bool TRACE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                            const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
@@ -419,13 +420,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int kb = 0; kb < p.num_kb; kb++, it++) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
-                    const long long c0 = p.trace ? clock64() : 0;
+                    const long long c0 = TRACE ? clock64() : 0;
                     if (!wait_parity(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
                         report_timeout(abort_flag, p.ctl.status);
                         ok = false;
                         break;
                     }
-                    if (p.trace) t_wait += clock64() - c0;
+                    if (TRACE) t_wait += clock64() - c0;
                     if (rank == 0) {
                         mbar_arrive_expect_tx(bar_full + 8 * s, L::kTxBytes);
                         issued_mask |= 1u << s;
@@ -448,56 +449,101 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     if (issued_mask & (1u << s))
                         wait_parity(bar_full + 8 * s, (issued_parity >> s) & 1, p.ctl.drain_timeout_ns, &never);
             }
-            if (p.trace) p.trace[blockIdx.x * kTraceSlots + 2] = t_wait;
+            if (TRACE) p.trace[blockIdx.x * kTraceSlots + 2] = t_wait;
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (leader only)
+        // One thread issues every tcgen05 op of the pair, so its instruction count per
+        // stage bounds the tensor rate: descriptors are advanced by constant strides
+        // (never rebuilt), each ring stage owns a fixed set of scale columns in TMEM,
+        // and a stage's 12 scale copies go out before its 4 MMAs.
         if (rank == 0 && elect_one()) {
             constexpr uint32_t idesc = idesc_mxf4nvf4(256, 256);
             const uint32_t empty0 = map_to_cta(bar_empty, 0), empty1 = map_to_cta(bar_empty, 1);
             const uint32_t accf0 = map_to_cta(bar_acc_full, 0), accf1 = map_to_cta(bar_acc_full, 1);
-            uint32_t it = 0;
+            const uint64_t a_desc0 = smem_desc(sA, 16, 1024, 2), b_desc0 = smem_desc(sB, 16, 1024, 2);
+            const uint64_t sfa_desc0 = smem_desc(sSfa, 16, 128, 0), sfb_desc0 = smem_desc(sSfb, 16, 128, 0);
+            const uint32_t sf_col0 = tmem_base + 256;
+            uint32_t stage = 0, phase = 0;
+            uint64_t a_d = a_desc0, b_d = b_desc0, sfa_d = sfa_desc0, sfb_d = sfb_desc0;
+            uint32_t sf_col = sf_col0, full_bar = bar_full, e0 = empty0, e1 = empty1;
             int local = 0;
             bool ok = true, any_issued = false;
             long long t_full = 0, t_acc = 0, t_first = 0;
             for (int t = pair; ok && t < n_tiles; t += num_pairs, local++) {
-                long long c0 = p.trace ? clock64() : 0;
+                long long c0 = TRACE ? clock64() : 0;
                 if (!wait_parity(bar_acc_empty, (local & 1) ^ 1, tmo, abort_flag)) {
                     report_timeout(abort_flag, p.ctl.status);
                     ok = false;
                     break;
                 }
-                if (p.trace) {
+                if (TRACE) {
                     const long long c1 = clock64();
                     t_acc += c1 - c0;
                     if (!t_first) t_first = c1;
                 }
                 tc_fence_after();
-                for (int kb = 0; kb < p.num_kb; kb++, it++) {
-                    const int s = it % STAGES;
-                    c0 = p.trace ? clock64() : 0;
-                    if (!wait_parity(bar_full + 8 * s, (it / STAGES) & 1, tmo, abort_flag)) {
+                for (int kb = 0; kb < p.num_kb; kb++) {
+                    if (TRACE) c0 = clock64();
+                    if (!mbar_try_wait(full_bar, phase) && !wait_parity(full_bar, phase, tmo, abort_flag)) {
                         report_timeout(abort_flag, p.ctl.status);
                         ok = false;
                         break;
                     }
-                    if (p.trace) t_full += clock64() - c0;
+                    if (TRACE) t_full += clock64() - c0;
                     tc_fence_after();
-                    const int kg = min(kKGroups, p.k_groups - kb * kKGroups);
-                    const uint32_t sf_cols = tmem_base + 256 + (it & 1) * L::kSfColsPerStage;
-                    for (int j = 0; j < kg; j++) {
-                        const uint32_t col = sf_cols + j * L::kSfColsPerGroup;
-                        tmem_cp_32x128_x4_pair(col, smem_desc(sSfa + s * L::kSfa + j * 512, 16, 128, 0));
-                        tmem_cp_32x128_x4_pair(col + 4, smem_desc(sSfb + s * L::kSfb + j * 512, 16, 128, 0));
-                        tmem_cp_32x128_x4_pair(col + 8,
-                                               smem_desc(sSfb + s * L::kSfb + (kKGroups + j) * 512, 16, 128, 0));
-                        mma_mxf4nvf4_pair(tmem_base, smem_desc(sA + s * L::kA + j * 32, 16, 1024, 2),
-                                          smem_desc(sB + s * L::kB + j * 32, 16, 1024, 2), idesc, col, col + 4,
-                                          (kb | j) != 0);
+                    const uint32_t acc0 = kb != 0;
+                    if (kb * kKGroups + kKGroups <= p.k_groups) {
+                        // full stage: descriptor offsets are immediates (addr >> 4 units)
+#pragma unroll
+                        for (int j = 0; j < kKGroups; j++) {
+                            const uint32_t col = sf_col + j * L::kSfColsPerGroup;
+                            tmem_cp_32x128_x4_pair(col, sfa_d + j * 32);
+                            tmem_cp_32x128_x4_pair(col + 4, sfb_d + j * 32);
+                            tmem_cp_32x128_x4_pair(col + 8, sfb_d + (kKGroups + j) * 32);
+                        }
+#pragma unroll
+                        for (int j = 0; j < kKGroups; j++) {
+                            const uint32_t col = sf_col + j * L::kSfColsPerGroup;
+                            mma_mxf4nvf4_pair(tmem_base, a_d + j * 2, b_d + j * 2, idesc, col, col + 4,
+                                              j == 0 ? acc0 : 1u);
+                        }
+                    } else {
+                        const int kg = p.k_groups - kb * kKGroups;  // last, partial stage
+                        for (int j = 0; j < kg; j++) {
+                            const uint32_t col = sf_col + j * L::kSfColsPerGroup;
+                            tmem_cp_32x128_x4_pair(col, sfa_d + j * 32);
+                            tmem_cp_32x128_x4_pair(col + 4, sfb_d + j * 32);
+                            tmem_cp_32x128_x4_pair(col + 8, sfb_d + (kKGroups + j) * 32);
+                            mma_mxf4nvf4_pair(tmem_base, a_d + j * 2, b_d + j * 2, idesc, col, col + 4,
+                                              j == 0 ? acc0 : 1u);
+                        }
                     }
                     any_issued = true;
-                    mma_commit_pair(empty0 + 8 * s);
-                    mma_commit_pair(empty1 + 8 * s);
+                    mma_commit_pair(e0);  // frees the stage in both CTAs once these MMAs finish
+                    mma_commit_pair(e1);
+                    // advance the ring
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                        a_d = a_desc0;
+                        b_d = b_desc0;
+                        sfa_d = sfa_desc0;
+                        sfb_d = sfb_desc0;
+                        sf_col = sf_col0;
+                        full_bar = bar_full;
+                        e0 = empty0;
+                        e1 = empty1;
+                    } else {
+                        a_d += L::kA >> 4;
+                        b_d += L::kB >> 4;
+                        sfa_d += L::kSfa >> 4;
+                        sfb_d += L::kSfb >> 4;
+                        sf_col += L::kSfColsPerStage;
+                        full_bar += 8;
+                        e0 += 8;
+                        e1 += 8;
+                    }
                 }
                 if (!ok) break;
                 mma_commit_pair(accf0);
@@ -508,7 +554,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 mma_commit_pair(map_to_cta(bar_drain, 0));
                 wait_parity(bar_drain, 0, p.ctl.drain_timeout_ns, &never);
             }
-            if (p.trace) {
+            if (TRACE) {
                 unsigned long long *tr = p.trace + blockIdx.x * kTraceSlots;
                 tr[0] = t_full;
                 tr[1] = t_acc;
@@ -528,10 +574,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             int tm, tn;
             coords(t, tm, tn);
             bool ok = true;
-            const long long c0 = p.trace ? clock64() : 0;
+            const long long c0 = TRACE ? clock64() : 0;
             if (lane == 0) ok = wait_parity(bar_acc_full, local & 1, tmo, abort_flag);
             ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (p.trace) {
+            if (TRACE) {
                 c_ready = clock64();
                 t_accw += c_ready - c0;
             }
@@ -550,9 +596,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(lead_acc_empty);
             store_row<kCols, F16>(acc, p, tm * 256 + (int)rank * 128 + quarter * 32 + lane, tn * 256 + half * kCols);
-            if (p.trace && warp == 2 && lane == 0) t_store += clock64() - c_ready;
+            if (TRACE && warp == 2 && lane == 0) t_store += clock64() - c_ready;
         }
-        if (p.trace && warp == 2 && lane == 0) {
+        if (TRACE && warp == 2 && lane == 0) {
             p.trace[blockIdx.x * kTraceSlots + 3] = t_accw;
             p.trace[blockIdx.x * kTraceSlots + 4] = t_store;
         }
@@ -656,12 +702,12 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
                        void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di,
                        unsigned long long *trace = nullptr) {
     using L = PairLayout<STAGES>;
-    auto kern = nvfp4_gemm_pair_kernel<STAGES, F16>;
-    static int configured[64] = {};
-    if (!configured[di.device]) {
+    auto kern = trace ? nvfp4_gemm_pair_kernel<STAGES, F16, true> : nvfp4_gemm_pair_kernel<STAGES, F16, false>;
+    static int configured[2][64] = {};
+    if (!configured[trace != nullptr][di.device]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamicSmem) != cudaSuccess)
             return NVFP4_ERR_CUDA;
-        configured[di.device] = 1;
+        configured[trace != nullptr][di.device] = 1;
     }
     CUtensorMap ta, tb, tsa, tsb;
     int st = operand_map(A, M, K, kBlockM, &ta);
