@@ -78,6 +78,7 @@ struct Params {
     // [3] epilogue wait on acc_full  [4] epilogue drain+store  [5] tiles
     // [6] MMA-thread cycles from first issue to last commit  [7] unused
     unsigned long long *trace;
+    int group_m;  // pair kernel: 256-row tile rows per raster group
 };
 constexpr int kTraceSlots = 8;
 
@@ -398,7 +399,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     // raster: groups of kGroupM/2 pair-rows of 256
     auto coords = [&](int t, int &tm, int &tn) {
-        const int gm_max = kGroupM / 2;
+        const int gm_max = p.group_m;
         const int per_group = gm_max * n_n;
         const int g = t / per_group, first = g * gm_max, gm = min(n_m - first, gm_max), local = t - g * per_group;
         tm = first + local % gm;
@@ -409,7 +410,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ producer (both CTAs)
         if (elect_one()) {
             const int rest_k = p.K >> 6;
-            uint32_t it = 0;
+            uint32_t stage = 0, phase = 0;
+            uint32_t dA = sA, dB = sB, dSfa = sSfa, dSfb = sSfb, emp = bar_empty, fb = lead_full, own_full = bar_full;
             bool ok = true;
             uint32_t issued_mask = 0, issued_parity = 0;
             long long t_wait = 0;
@@ -417,30 +419,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 int tm, tn;
                 coords(t, tm, tn);
                 const int arow = tm * 256 + rank * 128, brow = tn * 256 + rank * 128;
-                for (int kb = 0; kb < p.num_kb; kb++, it++) {
-                    const int s = it % STAGES;
-                    const uint32_t ph = (it / STAGES) & 1;
+                // scale tensors viewed as rows of 256 bytes: one (128-row block, k-stage) = 8 rows
+                const int ysa = (tm * 2 + (int)rank) * rest_k * 2, ysb0 = tn * 2 * rest_k * 2,
+                          ysb1 = (tn * 2 + 1) * rest_k * 2;
+                for (int kb = 0; kb < p.num_kb; kb++) {
                     const long long c0 = TRACE ? clock64() : 0;
-                    if (!wait_parity(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
+                    if (!mbar_try_wait(emp, phase ^ 1) && !wait_parity(emp, phase ^ 1, tmo, abort_flag)) {
                         report_timeout(abort_flag, p.ctl.status);
                         ok = false;
                         break;
                     }
                     if (TRACE) t_wait += clock64() - c0;
                     if (rank == 0) {
-                        mbar_arrive_expect_tx(bar_full + 8 * s, L::kTxBytes);
-                        issued_mask |= 1u << s;
-                        issued_parity = (issued_parity & ~(1u << s)) | (ph << s);
+                        mbar_arrive_expect_tx(own_full, L::kTxBytes);
+                        issued_mask |= 1u << stage;
+                        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
                     }
-                    const uint32_t fb = lead_full + 8 * s;
-                    tma_load_2d_pair(sA + s * L::kA, &tmap_a, fb, kb * kBlockKBytes, arow);
-                    tma_load_2d_pair(sB + s * L::kB, &tmap_b, fb, kb * kBlockKBytes, brow);
-                    // scale tensors viewed as rows of 256 bytes: one (128-row block, k-stage) = 8 rows
-                    tma_load_2d_pair(sSfa + s * L::kSfa, &tmap_sfa, fb, 0,
-                                     ((tm * 2 + (int)rank) * rest_k + kb * kKGroups) * 2);
-                    tma_load_2d_pair(sSfb + s * L::kSfb, &tmap_sfb, fb, 0, ((tn * 2) * rest_k + kb * kKGroups) * 2);
-                    tma_load_2d_pair(sSfb + s * L::kSfb + kKGroups * 512, &tmap_sfb, fb, 0,
-                                     ((tn * 2 + 1) * rest_k + kb * kKGroups) * 2);
+                    const int x = kb * kBlockKBytes, ysf = kb * kKGroups * 2;
+                    tma_load_2d_pair(dA, &tmap_a, fb, x, arow);
+                    tma_load_2d_pair(dB, &tmap_b, fb, x, brow);
+                    tma_load_2d_pair(dSfa, &tmap_sfa, fb, 0, ysa + ysf);
+                    tma_load_2d_pair(dSfb, &tmap_sfb, fb, 0, ysb0 + ysf);
+                    tma_load_2d_pair(dSfb + kKGroups * 512, &tmap_sfb, fb, 0, ysb1 + ysf);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                        dA = sA;
+                        dB = sB;
+                        dSfa = sSfa;
+                        dSfb = sSfb;
+                        emp = bar_empty;
+                        fb = lead_full;
+                        own_full = bar_full;
+                    } else {
+                        dA += L::kA;
+                        dB += L::kB;
+                        dSfa += L::kSfa;
+                        dSfb += L::kSfb;
+                        emp += 8;
+                        fb += 8;
+                        own_full += 8;
+                    }
                 }
             }
             if (!ok && rank == 0) {
@@ -697,6 +716,17 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     return cuda_status(cudaGetLastError());
 }
 
+// Raster group (256-row tile rows sharing a sweep over N) of the pair kernel;
+// env NVFP4_GROUP_M overrides the default.
+static int pair_group_m() {
+    static int v = [] {
+        const char *e = std::getenv("NVFP4_GROUP_M");
+        int x = e ? std::atoi(e) : 8;
+        return x < 1 ? 1 : (x > 1024 ? 1024 : x);
+    }();
+    return v;
+}
+
 template <int STAGES, bool F16>
 static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                        void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di,
@@ -735,6 +765,7 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     p.k_groups = K / 64;
     p.vec32_store = ((reinterpret_cast<uintptr_t>(D) & 31u) == 0) && (N % 16 == 0);
     p.trace = trace;
+    p.group_m = pair_group_m();
     if ((st = kernel_ctl(&p.ctl))) return st;
     const int pairs = std::min(p.num_tiles, di.sm_count / 2);
     kern<<<2 * pairs, kThreads, L::kDynamicSmem, stream>>>(ta, tb, tsa, tsb, p);
