@@ -1,0 +1,458 @@
+// gemm_pair.cu — CTA-pair (tcgen05 cta_group::2) persistent NVFP4 GEMM, one 256x256
+// output tile per pair of SMs.  The kernel for M > 128.
+//
+// CTA rank r of the pair holds A rows [256*tm + 128*r, +128), B rows
+// [256*tn + 128*r, +128), the 128-row scale block of its A rows and both 128-row
+// scale blocks of the tile's B rows (the MMA reads B's scales from each CTA's own
+// TMEM).  Each CTA's producers load those with cta_group::2 TMA loads — no
+// multicast — whose bytes complete on the LEADER's (rank 0) full barrier; the
+// leader's MMA thread issues the pair MMAs (M=256, N=256, K=64) and the scale
+// copies, and commits separately to each CTA's empty / acc_full barriers.  Both
+// CTAs' epilogues drain their own 128x256 TMEM half and arrive on the leader's
+// acc_empty barrier.
+//
+// The ring is latency-bound, not bandwidth-bound: a slot is reloaded only after
+// the MMAs that read it have completed, so throughput = slots / (MMA time of the
+// queued slots + commit->producer wake-up + TMA issue + TMA latency).  Slot width
+// is therefore a template parameter: BKB = 128 bytes of K per row (256 fp4, 38 KB
+// per CTA, 5 slots) or BKB = 64 (128 fp4, 19 KB, 11 slots, 64-byte swizzle).  Two
+// producer warps issue each slot's loads (A/B and the scales) in parallel, and a
+// single MMA thread issues with strided (never rebuilt) descriptors.
+#include <cstdlib>
+#include <cstring>
+
+#include "gemm_common.cuh"
+
+namespace nvfp4 {
+namespace gemm {
+
+template <int STAGES, int BKB>
+struct PairLayout {
+    static_assert(BKB == 128 || BKB == 64, "slot width");
+    static constexpr int kKG = BKB / 32;                 // 64-element k-groups per slot
+    static constexpr int kA = 128 * BKB;                 // this CTA's 128 A rows
+    static constexpr int kB = 128 * BKB;                 // this CTA's 128 B rows
+    static constexpr int kSfa = kKG * 512;               // A scales (one 128-row block)
+    static constexpr int kSfb = 2 * kKG * 512;           // B scales (both 128-row blocks of the tile)
+    static constexpr int kStage = kA + kB + kSfa + kSfb;
+    static constexpr int kOffA = 0;
+    static constexpr int kOffB = kOffA + STAGES * kA;
+    static constexpr int kOffSfa = kOffB + STAGES * kB;
+    static constexpr int kOffSfb = kOffSfa + STAGES * kSfa;
+    static constexpr int kOffBar = kOffSfb + STAGES * kSfb;
+    static constexpr int kBarBytes = (2 * STAGES + 3) * 8 + 16;
+    static constexpr int kDynamicSmem = kOffBar + kBarBytes + 1024;
+    static constexpr uint32_t kTxBytes = 2u * kStage;    // both CTAs complete on the leader's barrier
+    // shared-memory matrix descriptor: 128B or 64B swizzle, 8-row core groups
+    static constexpr uint32_t kLayout = BKB == 128 ? 2 : 4;
+    static constexpr uint32_t kSbo = 8 * BKB;
+    // TMEM: accumulator [0, 256), then rotating sets of scale columns (SFA 4 + SFB 8
+    // per k-group); the tensor pipe executes copies and MMAs in issue order, so a set
+    // is rewritten only after the MMAs that read it
+    static constexpr int kSfColsPerGroup = 12;
+    static constexpr int kSfCols = kKG * kSfColsPerGroup;
+    static constexpr int kSfSets = (256 / kSfCols) < STAGES ? (256 / kSfCols) : STAGES;
+    static constexpr int kTmemCols = 512;
+    static_assert(256 + kSfSets * kSfCols <= kTmemCols, "tensor memory budget");
+    static_assert(kDynamicSmem <= 232448, "shared memory budget");
+};
+
+constexpr int kPairThreads = 32 * (3 + kEpiWarps);  // A/B producer, MMA, 8 epilogue, scale producer
+constexpr int kSfProducerWarp = 2 + kEpiWarps;
+
+template <int STAGES, int BKB, bool F16, bool TRACE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+    nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                           const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
+                           const Params p) {
+    using L = PairLayout<STAGES, BKB>;
+    constexpr int KG = L::kKG;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    uint8_t *base_ptr = smem_raw + (base - smem_u32(smem_raw));
+    const uint32_t sA = base + L::kOffA, sB = base + L::kOffB, sSfa = base + L::kOffSfa, sSfb = base + L::kOffSfb;
+    const uint32_t bar_full = base + L::kOffBar;
+    const uint32_t bar_empty = bar_full + 8 * STAGES;
+    const uint32_t bar_acc_full = bar_empty + 8 * STAGES;
+    const uint32_t bar_acc_empty = bar_acc_full + 8;
+    const uint32_t bar_drain = bar_acc_empty + 8;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(base_ptr + L::kOffBar + (2 * STAGES + 3) * 8);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+    const int n_m = (p.M + 255) / 256, n_n = (p.N + 255) / 256, n_tiles = n_m * n_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        mbar_init(bar_acc_full, 1);
+        mbar_init(bar_acc_empty, 2 * kEpiWarps);
+        mbar_init(bar_drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_b);
+        prefetch_tmap(&tmap_sfa);
+        prefetch_tmap(&tmap_sfb);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_slot), L::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint64_t tmo = p.ctl.wait_timeout_ns;
+    const uint32_t lead_full = map_to_cta(bar_full, 0);
+
+    // raster: groups of p.group_m 256-row tile rows sweep N together (L2 reuse of A)
+    auto coords = [&](int t, int &tm, int &tn) {
+        const int gm_max = p.group_m;
+        const int per_group = gm_max * n_n;
+        const int g = t / per_group, first = g * gm_max, gm = min(n_m - first, gm_max), local = t - g * per_group;
+        tm = first + local % gm;
+        tn = local / gm;
+    };
+
+    if (warp == 0 || warp == kSfProducerWarp) {
+        // ------------------------------------------------------------ producers (both CTAs)
+        // warp 0: the A and B tiles (and, on the leader, the slot's expected bytes);
+        // the last warp: the scale tiles.  Both wait on the same empty barrier.
+        if (elect_one()) {
+            const bool ab = warp == 0;
+            const int rest_k = p.K >> 6;
+            uint32_t stage = 0, phase = 0;
+            uint32_t d0 = ab ? sA : sSfa, d1 = ab ? sB : sSfb, emp = bar_empty, fb = lead_full, own_full = bar_full;
+            bool ok = true;
+            uint32_t issued_mask = 0, issued_parity = 0;
+            long long t_wait = 0;
+            for (int t = pair; ok && t < n_tiles; t += num_pairs) {
+                int tm, tn;
+                coords(t, tm, tn);
+                const int arow = tm * 256 + rank * 128, brow = tn * 256 + rank * 128;
+                // scale tensors viewed as rows of 256 bytes: one (128-row block, 64-K group) = 2 rows
+                const int ysa = (tm * 2 + (int)rank) * rest_k * 2, ysb0 = tn * 2 * rest_k * 2,
+                          ysb1 = (tn * 2 + 1) * rest_k * 2;
+                for (int kb = 0; kb < p.num_kb; kb++) {
+                    const long long c0 = TRACE ? clock64() : 0;
+                    if (!mbar_try_wait(emp, phase ^ 1) && !wait_parity(emp, phase ^ 1, tmo, abort_flag)) {
+                        report_timeout(abort_flag, p.ctl.status);
+                        ok = false;
+                        break;
+                    }
+                    if (TRACE) t_wait += clock64() - c0;
+                    if (ab) {
+                        if (rank == 0) {
+                            mbar_arrive_expect_tx(own_full, L::kTxBytes);
+                            issued_mask |= 1u << stage;
+                            issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                        }
+                        const int x = kb * BKB;
+                        tma_load_2d_pair(d0, &tmap_a, fb, x, arow);
+                        tma_load_2d_pair(d1, &tmap_b, fb, x, brow);
+                    } else {
+                        const int ysf = kb * KG * 2;
+                        tma_load_2d_pair(d0, &tmap_sfa, fb, 0, ysa + ysf);
+                        tma_load_2d_pair(d1, &tmap_sfb, fb, 0, ysb0 + ysf);
+                        tma_load_2d_pair(d1 + KG * 512, &tmap_sfb, fb, 0, ysb1 + ysf);
+                    }
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                        d0 = ab ? sA : sSfa;
+                        d1 = ab ? sB : sSfb;
+                        emp = bar_empty;
+                        fb = lead_full;
+                        own_full = bar_full;
+                    } else {
+                        d0 += ab ? L::kA : L::kSfa;
+                        d1 += ab ? L::kB : L::kSfb;
+                        emp += 8;
+                        fb += 8;
+                        own_full += 8;
+                    }
+                }
+            }
+            if (!ok && ab && rank == 0) {
+                volatile int never = 0;
+                for (int s = 0; s < STAGES; s++)
+                    if (issued_mask & (1u << s))
+                        wait_parity(bar_full + 8 * s, (issued_parity >> s) & 1, p.ctl.drain_timeout_ns, &never);
+            }
+            if (TRACE && ab) p.trace[blockIdx.x * kTraceSlots + 2] = t_wait;
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer (leader only)
+        // One thread issues every tcgen05 op of the pair, so its instruction count per
+        // slot bounds the tensor rate: descriptors advance by constant strides, scale
+        // columns rotate through kSfSets sets, and a slot's scale copies go out before
+        // its MMAs.
+        if (rank == 0 && elect_one()) {
+            constexpr uint32_t idesc = idesc_mxf4nvf4(256, 256);
+            const uint32_t empty0 = map_to_cta(bar_empty, 0), empty1 = map_to_cta(bar_empty, 1);
+            const uint32_t accf0 = map_to_cta(bar_acc_full, 0), accf1 = map_to_cta(bar_acc_full, 1);
+            const uint64_t a_desc0 = smem_desc(sA, 16, L::kSbo, L::kLayout);
+            const uint64_t b_desc0 = smem_desc(sB, 16, L::kSbo, L::kLayout);
+            const uint64_t sfa_desc0 = smem_desc(sSfa, 16, 128, 0), sfb_desc0 = smem_desc(sSfb, 16, 128, 0);
+            const uint32_t sf_col0 = tmem_base + 256;
+            uint32_t stage = 0, phase = 0, sf_set = 0;
+            uint64_t a_d = a_desc0, b_d = b_desc0, sfa_d = sfa_desc0, sfb_d = sfb_desc0;
+            uint32_t sf_col = sf_col0, full_bar = bar_full, e0 = empty0, e1 = empty1;
+            int local = 0;
+            bool ok = true, any_issued = false;
+            long long t_full = 0, t_acc = 0, t_first = 0;
+            uint64_t ns_first = 0;
+            for (int t = pair; ok && t < n_tiles; t += num_pairs, local++) {
+                long long c0 = TRACE ? clock64() : 0;
+                if (!wait_parity(bar_acc_empty, (local & 1) ^ 1, tmo, abort_flag)) {
+                    report_timeout(abort_flag, p.ctl.status);
+                    ok = false;
+                    break;
+                }
+                if (TRACE) {
+                    const long long c1 = clock64();
+                    t_acc += c1 - c0;
+                    if (!t_first) {
+                        t_first = c1;
+                        ns_first = global_timer_ns();
+                    }
+                }
+                tc_fence_after();
+                for (int kb = 0; kb < p.num_kb; kb++) {
+                    if (TRACE) c0 = clock64();
+                    if (!mbar_try_wait(full_bar, phase) && !wait_parity(full_bar, phase, tmo, abort_flag)) {
+                        report_timeout(abort_flag, p.ctl.status);
+                        ok = false;
+                        break;
+                    }
+                    if (TRACE) t_full += clock64() - c0;
+                    tc_fence_after();
+                    const uint32_t acc0 = kb != 0;
+                    if ((kb + 1) * KG <= p.k_groups) {
+                        // full slot: descriptor offsets are immediates (addr >> 4 units)
+#pragma unroll
+                        for (int j = 0; j < KG; j++) {
+                            const uint32_t col = sf_col + j * L::kSfColsPerGroup;
+                            tmem_cp_32x128_x4_pair(col, sfa_d + j * 32);
+                            tmem_cp_32x128_x4_pair(col + 4, sfb_d + j * 32);
+                            tmem_cp_32x128_x4_pair(col + 8, sfb_d + (KG + j) * 32);
+                        }
+#pragma unroll
+                        for (int j = 0; j < KG; j++) {
+                            const uint32_t col = sf_col + j * L::kSfColsPerGroup;
+                            mma_mxf4nvf4_pair(tmem_base, a_d + j * 2, b_d + j * 2, idesc, col, col + 4,
+                                              j == 0 ? acc0 : 1u);
+                        }
+                    } else {
+                        const int kg = p.k_groups - kb * KG;  // last, partial slot
+                        for (int j = 0; j < kg; j++) {
+                            const uint32_t col = sf_col + j * L::kSfColsPerGroup;
+                            tmem_cp_32x128_x4_pair(col, sfa_d + j * 32);
+                            tmem_cp_32x128_x4_pair(col + 4, sfb_d + j * 32);
+                            tmem_cp_32x128_x4_pair(col + 8, sfb_d + (KG + j) * 32);
+                            mma_mxf4nvf4_pair(tmem_base, a_d + j * 2, b_d + j * 2, idesc, col, col + 4,
+                                              j == 0 ? acc0 : 1u);
+                        }
+                    }
+                    any_issued = true;
+                    mma_commit_pair(e0);  // frees the slot in both CTAs once these MMAs finish
+                    mma_commit_pair(e1);
+                    if (++sf_set == L::kSfSets) {
+                        sf_set = 0;
+                        sf_col = sf_col0;
+                    } else {
+                        sf_col += L::kSfCols;
+                    }
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                        a_d = a_desc0;
+                        b_d = b_desc0;
+                        sfa_d = sfa_desc0;
+                        sfb_d = sfb_desc0;
+                        full_bar = bar_full;
+                        e0 = empty0;
+                        e1 = empty1;
+                    } else {
+                        a_d += L::kA >> 4;
+                        b_d += L::kB >> 4;
+                        sfa_d += L::kSfa >> 4;
+                        sfb_d += L::kSfb >> 4;
+                        full_bar += 8;
+                        e0 += 8;
+                        e1 += 8;
+                    }
+                }
+                if (!ok) break;
+                mma_commit_pair(accf0);
+                mma_commit_pair(accf1);
+            }
+            if (!ok && any_issued) {
+                volatile int never = 0;
+                mma_commit_pair(map_to_cta(bar_drain, 0));
+                wait_parity(bar_drain, 0, p.ctl.drain_timeout_ns, &never);
+            }
+            if (TRACE) {
+                unsigned long long *tr = p.trace + blockIdx.x * kTraceSlots;
+                tr[0] = t_full;
+                tr[1] = t_acc;
+                tr[5] = local;
+                tr[6] = clock64() - t_first;
+                tr[7] = global_timer_ns() - ns_first;
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (warps 2..9, both CTAs)
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        constexpr int kCols = 128;
+        const uint32_t lead_acc_empty = map_to_cta(bar_acc_empty, 0);
+        int local = 0;
+        long long t_accw = 0, t_store = 0, c_ready = 0;
+        for (int t = pair; t < n_tiles; t += num_pairs, local++) {
+            int tm, tn;
+            coords(t, tm, tn);
+            bool ok = true;
+            const long long c0 = TRACE ? clock64() : 0;
+            if (lane == 0) ok = wait_parity(bar_acc_full, local & 1, tmo, abort_flag);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (TRACE) {
+                c_ready = clock64();
+                t_accw += c_ready - c0;
+            }
+            if (!ok) {
+                if (lane == 0) report_timeout(abort_flag, p.ctl.status);
+                break;
+            }
+            tc_fence_after();
+            uint32_t acc[kCols];
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * kCols;
+#pragma unroll
+            for (int c = 0; c < kCols / 32; c++)
+                tmem_ld_32x32b_x32(taddr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&acc[c * 32]));
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(lead_acc_empty);
+            store_row<kCols, F16>(acc, p, tm * 256 + (int)rank * 128 + quarter * 32 + lane, tn * 256 + half * kCols);
+            if (TRACE && warp == 2 && lane == 0) t_store += clock64() - c_ready;
+        }
+        if (TRACE && warp == 2 && lane == 0) {
+            p.trace[blockIdx.x * kTraceSlots + 3] = t_accw;
+            p.trace[blockIdx.x * kTraceSlots + 4] = t_store;
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();  // no CTA leaves while its peer may still signal it
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, L::kTmemCols);
+    }
+}
+
+// Raster group (256-row tile rows sharing a sweep over N); env NVFP4_GROUP_M overrides.
+static int pair_group_m() {
+    static int v = [] {
+        const char *e = std::getenv("NVFP4_GROUP_M");
+        int x = e ? std::atoi(e) : 32;
+        return x < 1 ? 1 : (x > 1024 ? 1024 : x);
+    }();
+    return v;
+}
+
+template <int STAGES, int BKB, bool F16>
+static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                       void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di,
+                       unsigned long long *trace) {
+    using L = PairLayout<STAGES, BKB>;
+    auto kern = trace ? nvfp4_gemm_pair_kernel<STAGES, BKB, F16, true> : nvfp4_gemm_pair_kernel<STAGES, BKB, F16, false>;
+    static int configured[2][64] = {};
+    if (!configured[trace != nullptr][di.device]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamicSmem) != cudaSuccess)
+            return NVFP4_ERR_CUDA;
+        configured[trace != nullptr][di.device] = 1;
+    }
+    CUtensorMap ta, tb, tsa, tsb;
+    int st = operand_map(A, M, K, 128, BKB, &ta);
+    if (!st) st = operand_map(B, N, K, 128, BKB, &tb);
+    // scale tensors as [bytes/256, 256]: one (128-row block, 64-K group) chunk is two rows
+    const uint64_t sfa_rows = (uint64_t)((M + 127) / 128) * (K / 64) * 2;
+    const uint64_t sfb_rows = (uint64_t)((N + 127) / 128) * (K / 64) * 2;
+    if (!st) st = encode_tiled_2d(&tsa, CU_TENSOR_MAP_DATA_TYPE_UINT8, SFA, 256, sfa_rows, 256, 256, 2 * L::kKG,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!st) st = encode_tiled_2d(&tsb, CU_TENSOR_MAP_DATA_TYPE_UINT8, SFB, 256, sfb_rows, 256, 256, 2 * L::kKG,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    Params p;
+    p.sfa = SFA;
+    p.sfb = SFB;
+    p.d = D;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.alpha = alpha;
+    p.num_m_tiles = (M + 255) / 256;
+    p.num_n_tiles = (N + 255) / 256;
+    p.num_tiles = p.num_m_tiles * p.num_n_tiles;
+    p.num_kb = (K + 2 * BKB - 1) / (2 * BKB);
+    p.k_groups = K / 64;
+    p.vec32_store = ((reinterpret_cast<uintptr_t>(D) & 31u) == 0) && (N % 16 == 0);
+    p.trace = trace;
+    p.group_m = pair_group_m();
+    if ((st = kernel_ctl(&p.ctl))) return st;
+    const int pairs = std::min(p.num_tiles, di.sm_count / 2);
+    kern<<<2 * pairs, kPairThreads, L::kDynamicSmem, stream>>>(ta, tb, tsa, tsb, p);
+    count_launch();
+    return cuda_status(cudaGetLastError());
+}
+
+// Ring shape of the pair kernel: 11 slots of 64 bytes of K (default) or 5 of 128;
+// env NVFP4_PAIR_RING=5x128|11x64 overrides.
+static int pair_ring() {
+    static int v = [] {
+        const char *e = std::getenv("NVFP4_PAIR_RING");
+        return (e && !std::strcmp(e, "5x128")) ? 128 : 64;
+    }();
+    return v;
+}
+
+template <bool F16>
+static int launch_pair_cfg(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                           void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di,
+                           unsigned long long *trace) {
+    if (pair_ring() == 128) return launch_pair<5, 128, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
+    return launch_pair<11, 64, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
+}
+
+}  // namespace gemm
+
+int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const void *D, int M,
+                  int N, int K);
+
+int pair_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
+                  int M, int N, int K, cudaStream_t stream, bool f16, const DeviceInfo &di) {
+    if (f16) return gemm::launch_pair_cfg<true>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, nullptr);
+    return gemm::launch_pair_cfg<false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, nullptr);
+}
+
+// Pair kernel with the per-CTA cycle trace on (trace: 148 x kTraceSlots u64 on the device).
+int gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D, int M,
+               int N, int K, unsigned long long *trace, cudaStream_t stream) {
+    int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
+    if (st) return st;
+    if (!trace) return NVFP4_ERR_INVALID;
+    DeviceInfo di;
+    if ((st = device_info(&di))) return st;
+    return gemm::launch_pair_cfg<false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
+}
+
+}  // namespace nvfp4

@@ -1,7 +1,7 @@
 """Diagnostics for the NVFP4 kernels on a B200.
 
     python -m nvfp4_b200.diag probe [iters]        measured mxf4nvf4 tensor rate per issue mode
-    python -m nvfp4_b200.diag trace M N K           per-CTA cycle breakdown of the CTA-pair GEMM
+    python -m nvfp4_b200.diag trace M N K [reps]    per-CTA cycle breakdown of the CTA-pair GEMM (last of reps)
 
 (run with gpu-kernels_b200/ on sys.path).  Each prints JSON lines.
 """
@@ -29,7 +29,7 @@ def probe(iters: int = 20000):
     return out
 
 
-def trace(M: int, N: int, K: int):
+def trace(M: int, N: int, K: int, reps: int = 3):
     from .ops import create_tensors
     dev = torch.device("cuda", 0)
     a, b, sfa, sfb = create_tensors(M, N, K, seed=1)
@@ -38,7 +38,7 @@ def trace(M: int, N: int, K: int):
     d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
     tr = torch.zeros(148 * 8, dtype=torch.int64, device=dev)
     s = torch.cuda.current_stream().cuda_stream
-    for _ in range(3):
+    for _ in range(reps):
         check(lib().nvfp4_gemm_trace(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), 1.0, d.data_ptr(),
                                      M, N, K, tr.data_ptr(), s), "trace")
     torch.cuda.synchronize()
@@ -48,7 +48,8 @@ def trace(M: int, N: int, K: int):
     rows = {"mma_wait_full": leaders[:, 0], "mma_wait_acc": leaders[:, 1], "producer_wait_empty": t[:, 2],
             "epi_wait_acc_full": t[:, 3], "epi_drain_store": t[:, 4]}
     res = {"M": M, "N": N, "K": K, "tiles_per_pair": statistics.mean(leaders[:, 5].tolist()),
-           "mma_span_cycles": statistics.mean(span.tolist())}
+           "mma_span_cycles": statistics.mean(span.tolist()),
+           "sm_clock_mhz": statistics.mean((leaders[:, 6].double() / leaders[:, 7].double() * 1e3).tolist())}
     for k, v in rows.items():
         res[k + "_cycles"] = statistics.mean(v.double().tolist())
         res[k + "_frac_of_span"] = res[k + "_cycles"] / res["mma_span_cycles"]
@@ -64,7 +65,8 @@ def main(argv):
             print(json.dumps(r))
     else:
         M, N, K = (int(x) for x in argv[1:4])
-        print(json.dumps(trace(M, N, K)))
+        reps = int(argv[4]) if len(argv) > 4 else 3
+        print(json.dumps(trace(M, N, K, reps)))
     return 0
 
 

@@ -146,10 +146,11 @@ def test_c2_full_size_sampled(nv, oracle, cuda_dev, N, K):
     assert not torch.isnan(d).any()
 
 
-@pytest.mark.parametrize("variant", ["single", "pair"])
-def test_forced_kernel_variant(variant, tmp_path):
-    """Both persistent kernels (single-CTA 128x256 and CTA-pair 256x256 tiles) on the
-    same ragged shape, each forced through NVFP4_GEMM_VARIANT in a fresh process."""
+@pytest.mark.parametrize("variant,ring", [("single", "11x64"), ("pair", "11x64"), ("pair", "5x128")])
+def test_forced_kernel_variant(variant, ring, tmp_path):
+    """Both persistent kernels (single-CTA 128x256 and CTA-pair 256x256 tiles, the
+    latter with both ring shapes) on the same ragged shape, each forced through
+    NVFP4_GEMM_VARIANT / NVFP4_PAIR_RING in a fresh process."""
     import os
     import subprocess
     import sys
@@ -171,6 +172,6 @@ err = np.abs(d.float().cpu().numpy() - ref).max() / np.abs(ref).max()
 assert err <= 1e-2, err
 print("ok", err)
 """
-    env = dict(os.environ, NVFP4_GEMM_VARIANT=variant)
+    env = dict(os.environ, NVFP4_GEMM_VARIANT=variant, NVFP4_PAIR_RING=ring)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
