@@ -11,13 +11,13 @@
 // CTAs' epilogues drain their own 128x256 TMEM half and arrive on the leader's
 // acc_empty barrier.
 //
-// The ring is latency-bound, not bandwidth-bound: a slot is reloaded only after
-// the MMAs that read it have completed, so throughput = slots / (MMA time of the
-// queued slots + commit->producer wake-up + TMA issue + TMA latency).  Slot width
-// is therefore a template parameter: BKB = 128 bytes of K per row (256 fp4, 38 KB
-// per CTA, 5 slots) or BKB = 64 (128 fp4, 19 KB, 11 slots, 64-byte swizzle).  Two
-// producer warps issue each slot's loads (A/B and the scales) in parallel, and a
-// single MMA thread issues with strided (never rebuilt) descriptors.
+// The ring is latency-bound: a slot is reloaded only after the MMAs that read it
+// have completed, so throughput = slots / (queued MMA time + commit->producer
+// wake-up + TMA issue + TMA latency, ~1.9K + 0.3K + 1.5K cycles measured).  Slot
+// width is a template parameter: BKB = 128 bytes of K per row (256 fp4, 38 KB per
+// CTA, 5 slots, the default) or BKB = 64 (128 fp4, 19 KB, 11 slots, 64-byte
+// swizzle).  Two producer warps issue each slot's loads (A/B and the scales) in
+// parallel, and a single MMA thread issues with strided (never rebuilt) descriptors.
 #include <cstdlib>
 #include <cstring>
 
@@ -415,12 +415,14 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     return cuda_status(cudaGetLastError());
 }
 
-// Ring shape of the pair kernel: 11 slots of 64 bytes of K (default) or 5 of 128;
-// env NVFP4_PAIR_RING=5x128|11x64 overrides.
+// Ring shape of the pair kernel: 5 slots of 128 bytes of K (default) or 11 of 64;
+// env NVFP4_PAIR_RING=5x128|11x64 overrides.  Measured at M=N=K=8192: 5x128 spends
+// 268K MMA-thread cycles per CTA pair, 11x64 405K — the single issuing thread's
+// fixed cost per slot (wait, fence, two commits) outweighs the deeper ring.
 static int pair_ring() {
     static int v = [] {
         const char *e = std::getenv("NVFP4_PAIR_RING");
-        return (e && !std::strcmp(e, "5x128")) ? 128 : 64;
+        return (e && !std::strcmp(e, "11x64")) ? 64 : 128;
     }();
     return v;
 }
