@@ -13,6 +13,8 @@ namespace nvfp4 {
 int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                   int M, int N, int K, cudaStream_t stream, bool f16);
 size_t decode_workspace_bytes(int M, int N);
+int decode_noalloc_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                            uint16_t *D, int M, int N, int K, cudaStream_t stream);
 int gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D, int M,
                int N, int K, unsigned long long *trace, cudaStream_t stream);
 int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const void *D, int M,
@@ -113,6 +115,11 @@ void matmul_nvfp4_b200(void *c, const uint8_t *sfa, const uint8_t *sfb, const ui
 }
 
 int nvfp4_last_status(void) { return g_last_status.load(); }
+
+int nvfp4_gemm_decode_noalloc(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+                              float alpha, uint16_t *D, int M, int N, int K, void *stream) {
+    return decode_noalloc_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, static_cast<cudaStream_t>(stream));
+}
 
 int nvfp4_gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                      uint16_t *D, int M, int N, int K, uint64_t *trace, void *stream) {

@@ -365,4 +365,60 @@ int decode_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, cons
     }
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the decode GEMM.
+//
+// Some callers cannot let a kernel library allocate device memory: hosts that own
+// all device memory themselves (memory-budgeted inference servers, plugin
+// interfaces of other frameworks that hand a library only its inputs and outputs),
+// and latency-critical loops in which a cudaMalloc — which may synchronise the
+// whole device — is not acceptable.  For them the split-K scratch (per-tile arrival
+// counters and fp32 partial tiles) lives in this fixed, file-scope device array
+// instead of a caller- or library-allocated workspace.  Every GPU that loads the
+// library holds these kNoAllocScratchBytes until the process exits.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB: M <= 16 on a 148-SM B200
+static __device__ __align__(256) uint8_t g_decode_scratch[kNoAllocScratchBytes];
+
+// Device address of g_decode_scratch on the current device, looked up once per
+// device (host code must not use the symbol itself as a device pointer).
+static int noalloc_scratch(void **out) {
+    static std::mutex mu;
+    static void *addr[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return NVFP4_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || !p) return NVFP4_ERR_CUDA;
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return NVFP4_OK;
+}
+
+int decode_noalloc_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                            uint16_t *D, int M, int N, int K, cudaStream_t stream) {
+    int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
+    if (st) return st;
+    if (M > 128) return NVFP4_ERR_SHAPE;
+    DeviceInfo di;
+    if ((st = device_info(&di))) return st;
+    const size_t need = decode::workspace_bytes(M, N, di.sm_count);
+    if (need > kNoAllocScratchBytes) return NVFP4_ERR_WORKSPACE;  // problem too large for the fixed scratch
+    void *ws = nullptr;
+    if ((st = noalloc_scratch(&ws))) return st;
+    // The array keeps whatever the previous call left; the arrival counters must
+    // start at zero, so clear them (a memset, not an allocation).
+    const size_t counters = ((size_t)((N + decode::kTileN - 1) / decode::kTileN) * sizeof(int) + 255) / 256 * 256;
+    if ((st = cuda_status(cudaMemsetAsync(ws, 0, counters, stream)))) return st;
+    switch (decode::mpad_for(M)) {
+        case 8: return decode::launch<8>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
+        case 16: return decode::launch<16>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
+        case 32: return decode::launch<32>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
+        case 64: return decode::launch<64>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
+        default: return decode::launch<128>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
+    }
+}
+
 }  // namespace nvfp4

@@ -155,6 +155,26 @@ NVFP4_API void nvfp4_set_wait_timeout_ns(uint64_t ns);
 NVFP4_API int nvfp4_selftest_wait_timeout(uint64_t timeout_ns);
 
 /*
+ * Allocation-free decode GEMM.  No counterpart in the reference: it exists for
+ * callers that cannot let a library allocate device memory — hosts that own all
+ * device memory (memory-budgeted servers, plugin interfaces that pass a library
+ * only its inputs and outputs) and latency-critical paths where a cudaMalloc,
+ * which may synchronise the device, is not acceptable.
+ *
+ * Same contract and result as nvfp4_gemm_decode, but the split-K scratch is a
+ * fixed 4 MiB device array inside the library (held by every GPU that loads the
+ * library until exit), so the call allocates nothing; the caller still passes A,
+ * SFA, B, SFB and D.  Shapes whose
+ * scratch need (nvfp4_gemm_decode_workspace_size) exceeds it are refused with
+ * NVFP4_ERR_WORKSPACE — on a 148-SM B200 that admits M <= 16.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress), so make that
+ * first call before any stream capture.  All calls on a device share the one array:
+ * calls whose kernels overlap on the GPU (different streams, no ordering) race.
+ */
+NVFP4_API int nvfp4_gemm_decode_noalloc(const uint8_t *A, const uint8_t *SFA, const uint8_t *B,
+               const uint8_t *SFB, float alpha, uint16_t *D, int M, int N, int K, void *stream);
+
+/*
  * Diagnostics (no counterpart in the reference, which only has a host timer and
  * an unused per-SM event recorder, matmul/sm100_nvfp4/profiler.cuh:4-72).
  *
