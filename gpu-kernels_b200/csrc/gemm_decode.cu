@@ -21,8 +21,7 @@
 
 #include <mutex>
 
-#include "common.cuh"
-#include "ptx.cuh"
+#include "gemm_common.cuh"
 
 namespace nvfp4 {
 namespace decode {
@@ -118,6 +117,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t it_begin = range_begin(blockIdx.x, p), it_end = range_begin(blockIdx.x + 1, p);
     const int64_t rest_k = p.K >> 6;
 
+    // Launched as a programmatic dependent of the previous kernel in the stream:
+    // everything above overlapped that kernel's tail.  Warm L2 with this CTA's first
+    // weight tiles (a prefetch only fills L2, which stays coherent with any write the
+    // previous kernel still makes), then wait for the previous kernel before touching
+    // any input or output.
+    if (warp == 0 && lane == 0) {
+        for (int64_t it = it_begin; it < it_end && it < it_begin + L::STAGES; it++)
+            tma_prefetch_2d(&tmap_w, (int)(it % p.num_kb) * kBlockKBytes, (int)(it / p.num_kb) * kTileN);
+    }
+    grid_dependency_wait();
+
     if (warp == 0) {
         if (elect_one()) {
             const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
@@ -143,6 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bulk_load_hint(sSfx + s * L::kSfx, p.sfa + (int64_t)kb * kKGroups * 512, kg * 512u, bar_full + 8 * s,
                                pol_x);
             }
+            grid_launch_dependents();  // all loads issued: the next kernel may start its prologue
             if (!ok) {
                 volatile int never = 0;
                 for (int s = 0; s < S; s++)
@@ -280,11 +291,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-static int act_map(const void *ptr, int64_t rows, int64_t K, int box_rows, CUtensorMap *out) {
-    return encode_tiled_2d(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, ptr, (uint64_t)(K / 2), (uint64_t)rows,
-                           (uint64_t)(K / 2), kBlockKBytes, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
-}
-
 int mpad_for(int M) {
     int m = 8;
     while (m < M) m *= 2;
@@ -310,8 +316,8 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
         configured[di.device] = 1;
     }
     CUtensorMap tw, tx;
-    int st = act_map(B, N, K, kTileN, &tw);
-    if (!st) st = act_map(A, M, K, MPAD, &tx);
+    int st = gemm::operand_map(B, N, K, kTileN, kBlockKBytes, &tw);  // cached tensor maps
+    if (!st) st = gemm::operand_map(A, M, K, MPAD, kBlockKBytes, &tx);
     if (st) return st;
     Params p;
     p.sfa = SFA;
@@ -330,7 +336,17 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     p.counters = static_cast<int *>(ws);
     p.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + counters);
     if ((st = kernel_ctl(&p.ctl))) return st;
-    kern<<<p.grid, kThreads, L::kDynamicSmem, stream>>>(tw, tx, p);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::kDynamicSmem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, tw, tx, p) != cudaSuccess) return NVFP4_ERR_CUDA;
     count_launch();
     return cuda_status(cudaGetLastError());
 }
