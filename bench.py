@@ -302,6 +302,95 @@ def decode_section(nv, dev, pk, reps=30):
             "timing": "CUDA-graph replay of 30 back-to-back calls, weights rotating over 3 sets", "shapes": out}
 
 
+def quantize_section(nv, dev, pk, reps=20):
+    """Row a9-Q (bf16 -> NVFP4) and BASELINE configs[4] (fused quantize + GEMM on
+    heavy-tailed activations): the quantizer's HBM rate on the 8192x8192 operand and
+    the 4096x4096 activation, and the end-to-end device time of amax -> quantize ->
+    GEMM against a pre-quantized W[14336, 4096].  Timed from CUDA-graph replays."""
+    g = torch.Generator(device=dev)
+    stream = torch.cuda.Stream(dev)
+    res = {"unit": "GB/s", "peak_gbs": pk["hbm_gbs"]}
+    for (M, K) in ((8192, 8192), (4096, 4096)):
+        g.manual_seed(3)
+        xs = [torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16) for _ in range(3)]
+        gs = torch.full((1,), 1e-3, dtype=torch.float32, device=dev)
+        q = torch.empty(M, K // 2, dtype=torch.uint8, device=dev)
+        sf = torch.empty(nv.sf_bytes(M, K), dtype=torch.uint8, device=dev)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                nv.quantize(xs[i % 3], gs, q_out=q, sf_out=sf)
+            stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(reps):
+                nv.quantize(xs[i % 3], gs, q_out=q, sf_out=sf)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        us = 1e3 * e0.elapsed_time(e1) / reps
+        nbytes = M * K * 2 + M * K // 2 + M * K // 16
+        res[f"quantize_{M}x{K}"] = {"us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1),
+                                    "frac_hbm": round(nbytes / us / 1e3 / pk["hbm_gbs"], 3)}
+        del graph, xs
+    # configs[4]: X[4096,4096] Student-t(3) with 4 outlier channels x50, W[14336,4096] N(0, 0.02)
+    M, N, K = 4096, 14336, 4096
+    g.manual_seed(9)
+    z = torch.randn(M, K, device=dev, generator=g)
+    chi = (torch.randn(3, M, K, device=dev, generator=g) ** 2).sum(0) / 3
+    x = z / chi.sqrt()
+    cols = torch.randperm(K, device=dev, generator=g)[:4]
+    x[:, cols] *= 50
+    x = x.to(torch.bfloat16)
+    del z, chi
+    w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    _, gsw = nv.global_scale(w)
+    wq, wsf = nv.quantize(w, gsw)
+    del w
+    amax, gsx = torch.empty(1, device=dev), torch.empty(1, device=dev)
+    xq = torch.empty(M, K // 2, dtype=torch.uint8, device=dev)
+    xsf = torch.empty(nv.sf_bytes(M, K), dtype=torch.uint8, device=dev)
+    d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    L = nv.lib()
+
+    def fused():
+        s = torch.cuda.current_stream(dev).cuda_stream
+        L.nvfp4_global_scale(x.data_ptr(), x.numel(), amax.data_ptr(), gsx.data_ptr(), s)
+        L.nvfp4_quantize(x.data_ptr(), xq.data_ptr(), xsf.data_ptr(), gsx.data_ptr(), M, K, s)
+        # the GEMM's alpha would be gs_x * gs_w; gs_x lives on the device here and the
+        # timing does not depend on alpha's value, so alpha = 1 is passed
+        nv.gemm(xq, xsf, wq, wsf, 1.0, out=d)
+
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        fused()
+        stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(reps):
+            fused()
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    us = 1e3 * e0.elapsed_time(e1) / reps
+    del graph
+    res["fused_quantize_gemm_4096x14336x4096"] = {
+        "us": round(us, 2), "tflops": round(2.0 * M * N * K / us / 1e6, 1),
+        "steps": "amax + quantize of X (bf16 Student-t, 4 outlier channels x50) + GEMM vs pre-quantized W"}
+    nv.device_status()
+    return res
+
+
 def run_decode_workload(args, M, N, K):
     """One skinny-M shape alone (for profiling): weights rotate over 3 sets."""
     import nvfp4_b200 as nv
@@ -334,6 +423,34 @@ def run_decode_workload(args, M, N, K):
     nbytes = N * K // 2 + N * K // 16 + M * K // 2 + M * K // 16 + 2 * M * N
     print(json.dumps({"metric": "decode NVFP4 GEMM HBM GB/s", "value": nbytes / us / 1e3, "unit": "GB/s",
                       "us_per_call": us, "config": {"M": M, "N": N, "K": K}, "steps": args.steps}), flush=True)
+    return 0
+
+
+def run_quantize_workload(args, M, K):
+    """The quantizer alone (for profiling): bf16 N(0,1) X [M, K], 3 rotating inputs."""
+    import nvfp4_b200 as nv
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    xs = [torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16) for _ in range(3)]
+    gs = torch.full((1,), 1e-3, dtype=torch.float32, device=dev)
+    q = torch.empty(M, K // 2, dtype=torch.uint8, device=dev)
+    sf = torch.empty(nv.sf_bytes(M, K), dtype=torch.uint8, device=dev)
+    for i in range(args.warmup):
+        nv.quantize(xs[i % 3], gs, q_out=q, sf_out=sf)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        nv.quantize(xs[i % 3], gs, q_out=q, sf_out=sf)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = 1e3 * e0.elapsed_time(e1) / args.steps
+    nbytes = M * K * 2 + M * K // 2 + M * K // 16
+    print(json.dumps({"metric": "bf16 -> NVFP4 quantize HBM GB/s", "value": nbytes / us / 1e3, "unit": "GB/s",
+                      "us_per_call": us, "config": {"M": M, "K": K}, "steps": args.steps}), flush=True)
     return 0
 
 
@@ -415,9 +532,10 @@ def run_ours(args):
     fp4_peak_est = 4.0 * pk["bf16_tflops"]
     traffic = committed_traffic().get("gemm_8192", {}).get("dram_bytes_per_launch")
     cpu = None
-    decode = None
+    decode = quant = None
     if not args.no_decode:
         decode = decode_section(nv, dev, pk)
+        quant = quantize_section(nv, dev, pk)
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu, _, _ = cpu_reference_sample(a, sfa, b, sfb, alpha, M, N, K, target_s=args.cpu_seconds)
 
@@ -446,6 +564,8 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         if decode is not None:
             line["decode"] = decode
+        if quant is not None:
+            line["quantize"] = quant
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
@@ -464,7 +584,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-shape GB/s section")
     ap.add_argument("--workload", default="square",
-                    help="square (default, the bench line) or decode:M:N:K (one skinny shape, for profiling)")
+                    help="square (default, the bench line), decode:M:N:K or quantize:M:K (one kernel, for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -473,6 +593,9 @@ def main():
     if args.workload.startswith("decode:"):
         M, N, K = (int(v) for v in args.workload.split(":")[1:])
         return run_decode_workload(args, M, N, K)
+    if args.workload.startswith("quantize:"):
+        M, K = (int(v) for v in args.workload.split(":")[1:])
+        return run_quantize_workload(args, M, K)
     return run_ours(args)
 
 

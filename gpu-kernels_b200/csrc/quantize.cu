@@ -7,11 +7,12 @@
 //   q  = e2m1_rn_sat(x*inv), each fp32 step one IEEE round-to-nearest op
 //   (a gs outside [2^-100, FLT_MAX] gives sf = 0, inv = 0).
 //
-// Work split: a lane owns 8 consecutive bf16 (one 16-byte load); two lanes form
-// a 16-element scale block (amax via one shuffle); eight lanes form one 64-element
-// k-group of one row, whose 4 scale bytes are contiguous in the blocked layout and
-// leave as one 32-bit store.  A warp therefore reads 512 contiguous bytes, writes
-// 128 contiguous bytes of codes and 4 x 4 bytes of scales per step.
+// Work split: a lane owns one 16-element scale block (one 32-byte load, 8 bytes of
+// codes out); four lanes form one 64-element k-group of one row, whose 4 scale
+// bytes are contiguous in the blocked layout and leave as one 32-bit store.  A warp
+// reads 1 KB contiguous and writes 256 contiguous bytes of codes per step.  The
+// kernel is instruction-bound before it is HBM-bound (IEEE divisions), so the
+// per-block reciprocal comes from a 256-entry table.
 #include <cuda_bf16.h>
 #include <cuda_fp4.h>
 #include <cuda_fp8.h>
@@ -37,68 +38,87 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
     return v;
 }
 
-constexpr int kQuantUnroll = 4;
+constexpr int kQuantUnroll = 2;
 
-// X: [M, K] bf16, Q: [M, K/2], SF: blocked [pad128(M), K/16].  n_groups8 = M*K/8.
+__device__ __forceinline__ void ld_stream_v8(const void *p, uint32_t (&w)[8]) {
+    asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+                 : "l"(p));
+}
+
+// X: [M, K] bf16, Q: [M, K/2], SF: blocked [pad128(M), K/16].  n_blocks = M*K/16.
+// A lane owns one 16-element scale block (one 32-byte load, one 8-byte store of
+// codes); four consecutive lanes own one 64-element k-group, whose 4 scale bytes
+// are contiguous in the blocked layout and leave as one 32-bit store.  The
+// reciprocal 1/(float(sf)*gs) takes only 256 values per launch, so each CTA
+// tabulates it once in shared memory with the same IEEE operations.
 __global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16 *__restrict__ X, uint8_t *__restrict__ Q,
                                                        uint8_t *__restrict__ SF, const float *__restrict__ gs_ptr,
-                                                       int64_t n_groups8, int64_t K) {
+                                                       int64_t n_blocks, int64_t K) {
+    __shared__ float inv_table[256];
     const float gs = *gs_ptr;
     // Same usability rule as the CPU specification: outside [2^-100, FLT_MAX]
     // every block quantizes to sf = 0, q = e2m1(x * 0).
     const bool gs_ok = gs >= 0x1p-100f && gs <= 0x1.fffffep127f;
+    {
+        const int c = threadIdx.x;  // blockDim.x == 256
+        const float denom = __fmul_rn(e4m3_to_float((uint8_t)c), gs);
+        inv_table[c] = (!gs_ok || denom == 0.0f) ? 0.0f : __fdiv_rn(1.0f, denom);
+    }
+    __syncthreads();
     const int lane = threadIdx.x & 31;
     const int64_t rest_k = K >> 6;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    // All lanes of a warp iterate together (the trip count is warp-uniform because
-    // every warp covers 32 consecutive groups and n_groups8 % 8 == 0).
-    for (; g - lane < n_groups8; g += stride * kQuantUnroll) {
-        uint4 raw[kQuantUnroll];
+    // The trip count is warp-uniform: every warp covers 32 consecutive blocks and
+    // n_blocks % 4 == 0 (K % 64 == 0), so whole 4-lane k-groups are active or not.
+    for (; g - lane < n_blocks; g += stride * kQuantUnroll) {
+        uint32_t raw[kQuantUnroll][8];
 #pragma unroll
         for (int u = 0; u < kQuantUnroll; u++) {
-            int64_t gi = g + u * stride;
-            raw[u] = gi < n_groups8 ? ld_stream_u4(X + gi * 8) : make_uint4(0, 0, 0, 0);
+            const int64_t gi = g + u * stride;
+            if (gi < n_blocks) {
+                ld_stream_v8(X + gi * 16, raw[u]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; i++) raw[u][i] = 0;
+            }
         }
 #pragma unroll
         for (int u = 0; u < kQuantUnroll; u++) {
-            int64_t gi = g + u * stride;
-            const bool active = gi < n_groups8;
-            float v[8];
-            const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+            const int64_t gi = g + u * stride;
+            float v[16];
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                v[2 * i] = __uint_as_float(w[i] << 16);
-                v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+            for (int i = 0; i < 8; i++) {
+                v[2 * i] = __uint_as_float(raw[u][i] << 16);
+                v[2 * i + 1] = __uint_as_float(raw[u][i] & 0xFFFF0000u);
             }
             float amax = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-            uint8_t code = 0;
-            float inv = 0.0f;
+            for (int i = 0; i < 16; i++) amax = fmaxf(amax, fabsf(v[i]));
+            uint32_t code = 0;
             if (gs_ok) {
                 const float sfv = __fdiv_rn(__fdiv_rn(amax, 6.0f), gs);
-                code = static_cast<uint8_t>(__nv_cvt_float_to_fp8(sfv, __NV_SATFINITE, __NV_E4M3));
-                const float denom = __fmul_rn(e4m3_to_float(code), gs);
-                inv = denom == 0.0f ? 0.0f : __fdiv_rn(1.0f, denom);
+                code = static_cast<uint32_t>(__nv_cvt_float_to_fp8(sfv, __NV_SATFINITE, __NV_E4M3));
             }
-            uint32_t packed = 0;
+            const float inv = inv_table[code];
+            uint32_t lo = 0, hi = 0;
 #pragma unroll
-            for (int i = 0; i < 4; i++)
-                packed |= e2m1x2(__fmul_rn(v[2 * i], inv), __fmul_rn(v[2 * i + 1], inv)) << (8 * i);
-            // Gather the 4 scale codes of this 8-lane k-group into its first lane.
-            uint32_t c = code;
-            const uint32_t c1 = __shfl_down_sync(0xffffffffu, c, 2);
-            const uint32_t c2 = __shfl_down_sync(0xffffffffu, c, 4);
-            const uint32_t c3 = __shfl_down_sync(0xffffffffu, c, 6);
-            if (active) {
-                reinterpret_cast<uint32_t *>(Q)[gi] = packed;
-                if ((lane & 7) == 0) {
-                    const int64_t e = gi * 8;  // first element of the k-group
+            for (int i = 0; i < 4; i++) {
+                lo |= e2m1x2(__fmul_rn(v[2 * i], inv), __fmul_rn(v[2 * i + 1], inv)) << (8 * i);
+                hi |= e2m1x2(__fmul_rn(v[8 + 2 * i], inv), __fmul_rn(v[8 + 2 * i + 1], inv)) << (8 * i);
+            }
+            // gather the 4 scale codes of this lane's k-group into its first lane
+            const uint32_t c1 = __shfl_down_sync(0xffffffffu, code, 1);
+            const uint32_t c2 = __shfl_down_sync(0xffffffffu, code, 2);
+            const uint32_t c3 = __shfl_down_sync(0xffffffffu, code, 3);
+            if (gi < n_blocks) {
+                *reinterpret_cast<uint2 *>(Q + gi * 8) = make_uint2(lo, hi);
+                if ((lane & 3) == 0) {
+                    const int64_t e = gi * 16;  // first element of the k-group
                     const int64_t r = e / K, kg = (e - r * K) >> 6;
                     const int64_t off = ((r >> 7) * rest_k + kg) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4;
-                    *reinterpret_cast<uint32_t *>(SF + off) = c | (c1 << 8) | (c2 << 16) | (c3 << 24);
+                    *reinterpret_cast<uint32_t *>(SF + off) = code | (c1 << 8) | (c2 << 16) | (c3 << 24);
                 }
             }
         }
@@ -159,20 +179,20 @@ extern "C" int nvfp4_quantize(const uint16_t *X, uint8_t *Q, uint8_t *SF, const 
                               void *stream) {
     if (!X || !Q || !SF || !global_scale) return NVFP4_ERR_INVALID;
     if (M < 1 || K < 64 || K % 64) return NVFP4_ERR_SHAPE;
-    if (!aligned16(X) || !aligned16(Q) || (reinterpret_cast<uintptr_t>(SF) & 3u) ||
+    if ((reinterpret_cast<uintptr_t>(X) & 31u) || !aligned16(Q) || (reinterpret_cast<uintptr_t>(SF) & 3u) ||
         (reinterpret_cast<uintptr_t>(global_scale) & 3u))
         return NVFP4_ERR_ALIGN;
     DeviceInfo di;
     int st = device_info(&di);
     if (st) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int64_t n_groups8 = (int64_t)M * K / 8;
+    const int64_t n_blocks = (int64_t)M * K / 16;
     const int threads = 256;
-    int64_t blocks = (n_groups8 + threads - 1) / threads;
+    int64_t blocks = (n_blocks + threads - 1) / threads;
     const int64_t cap = (int64_t)di.sm_count * 8;  // 8 x 256 threads resident per SM
     if (blocks > cap) blocks = cap;
     quantize_kernel<<<(unsigned)blocks, threads, 0, s>>>(reinterpret_cast<const __nv_bfloat16 *>(X), Q, SF,
-                                                         global_scale, n_groups8, K);
+                                                         global_scale, n_blocks, K);
     count_launch();
     if (M % 128) {
         sf_pad_zero_kernel<<<(unsigned)std::min<int64_t>(di.sm_count, (128 * (int64_t)K / 16 + 255) / 256), 256, 0,

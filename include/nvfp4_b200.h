@@ -74,7 +74,8 @@ NVFP4_API int nvfp4_version(void);
  *   global_scale: DEVICE pointer to one fp32 gs (x ~= q * sf * gs).
  * Per 16-element block: sf = e4m3_rn_sat((amax/6)/gs); q = e2m1_rn_sat(x * (1/(sf*gs))),
  * every fp32 step a single IEEE round-to-nearest operation (bit-exact with the
- * CPU specification).  SF padding rows are written as 0.
+ * CPU specification).  SF padding rows are written as 0.  X must be 32-byte
+ * aligned (one 256-bit load per 16-element block), Q 16-byte, SF 4-byte.
  */
 NVFP4_API int nvfp4_quantize(const uint16_t *X, uint8_t *Q, uint8_t *SF, const float *global_scale,
                    int M, int K, void *stream);
