@@ -4,8 +4,8 @@
 // CTA rank r of the pair holds A rows [256*tm + 128*r, +128), B rows
 // [256*tn + 128*r, +128), the 128-row scale block of its A rows and both 128-row
 // scale blocks of the tile's B rows (the MMA reads B's scales from each CTA's own
-// TMEM).  Each CTA's producers load those with cta_group::2 TMA loads — no
-// multicast — whose bytes complete on the LEADER's (rank 0) full barrier; the
+// TMEM).  Each CTA's producers load those with cta_group::2 TMA loads — each CTA
+// fetches only its own tiles — whose bytes complete on the LEADER's (rank 0) full barrier; the
 // leader's MMA thread issues the pair MMAs (M=256, N=256, K=64) and the scale
 // copies, and commits separately to each CTA's empty / acc_full barriers.  Both
 // CTAs' epilogues drain their own 128x256 TMEM half and arrive on the leader's

@@ -94,8 +94,8 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // ---------------------------------------------------------------------------
-// TMA / bulk copies.  No load here uses .multicast::cluster: each CTA fetches its
-// own tiles, so the same code is safe in multi-GPU runs.
+// TMA / bulk copies.  Every load here has exactly one destination CTA: each CTA
+// fetches its own tiles, so the same code is safe in multi-GPU runs.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -319,8 +319,8 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 }
 
 // 2-D tiled load into this CTA's smem whose transaction bytes complete on an
-// mbarrier that may live in either CTA of the pair (cta_group::2).  Not a
-// multicast load: each CTA fetches only its own tile.
+// mbarrier that may live in either CTA of the pair (cta_group::2).  It has one
+// destination CTA: each CTA fetches only its own tile.
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *tmap, uint32_t bar_cluster,
                                                  int32_t x, int32_t y) {
     asm volatile(

@@ -1,0 +1,80 @@
+"""GPU, 2+ devices: the column-parallel NVFP4 GEMM over NCCL.
+
+Each rank computes its 128-row-block shard of B with the CTA-pair kernel and the
+bf16 shards are all-gathered; the gathered D must equal the unsharded GEMM on one
+GPU bit for bit (every output element is accumulated by one CTA over the same K
+order however N is split).  Skipped when fewer than two GPUs are visible."""
+import datetime
+import os
+import socket
+import sys
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _operands(M, N, K, dev):
+    sys.path[:0] = [os.path.join(ROOT, "gpu-kernels_b200")]
+    import nvfp4_b200 as nv
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    xa = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    xb = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    _, ga = nv.global_scale(xa)
+    _, gb = nv.global_scale(xb)
+    a, sfa = nv.quantize(xa, ga)
+    b, sfb = nv.quantize(xb, gb)
+    return nv, a, sfa, b, sfb
+
+
+def _rank(rank, world, port, M, N, K, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import torch.distributed as dist
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        nv, a, sfa, b, sfb = _operands(M, N, K, dev)
+        from nvfp4_b200.dist import column_parallel_gemm, shard_weight
+        bs, ss = shard_weight(b, sfb, K, world, rank)
+        d = column_parallel_gemm(a, sfa, bs.contiguous(), ss.contiguous(), 0.5, N, gather=True)
+        torch.cuda.synchronize()
+        nv.device_status()
+        if rank == 0:
+            full = nv.gemm(a, sfa, b, sfb, 0.5)
+            torch.cuda.synchronize()
+            q.put(bool(torch.equal(d, full)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 3072, 1024), (300, 1288, 2048)])
+def test_column_parallel_nccl_matches_single_gpu(M, N, K):
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs at least two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_rank, args=(r, world, port, M, N, K, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert q.get(timeout=5) is True
