@@ -313,6 +313,26 @@ static void sgemm_nt(const float *A, const float *B, float *C, int64_t mrows, in
     }
 }
 
+void nvfp4o_sgemm_nt(const float *A, const float *B, float alpha, int64_t mrows, int64_t ncols, int64_t K,
+                     float *D32, uint16_t *D16, int nthreads) {
+    float *C = (float *)malloc((size_t)mrows * (size_t)ncols * sizeof(float));
+    if (!C) return;
+    sgemm_nt(A, B, C, mrows, ncols, K, nthreads);
+    int64_t total = mrows * ncols;
+#pragma omp parallel for schedule(static) num_threads(pick_threads(nthreads))
+    for (int64_t i = 0; i < total; i++) {
+        float v = alpha * C[i];
+        if (D32) D32[i] = v;
+        if (D16) D16[i] = nvfp4o_f32_to_bf16(v);
+    }
+    free(C);
+}
+
+void nvfp4o_dequant_rows(const uint8_t *Q, const uint8_t *SF, float *out, int64_t r0, int64_t nrows, int64_t K,
+                         int nthreads) {
+    dequant_rows(Q, SF, out, r0, nrows, K, nthreads);
+}
+
 void nvfp4o_gemm_rows(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
                       float alpha, int64_t M, int64_t N, int64_t K, int64_t m0, int64_t mrows,
                       float *D32, uint16_t *D16, int nthreads) {

@@ -64,6 +64,14 @@ void    nvfp4o_gemm_rows(const uint8_t *A, const uint8_t *SFA, const uint8_t *B,
                          const uint8_t *SFB, float alpha, int64_t M, int64_t N, int64_t K,
                          int64_t m0, int64_t mrows, float *D32, uint16_t *D16, int nthreads);
 
+/* The two halves of nvfp4o_gemm_rows, for callers that dequantise B once:
+ * rows [r0, r0+nrows) of a quantized matrix -> fp32, and D = alpha * A . B^T on fp32
+ * row-major A [mrows, K], B [ncols, K] (fp32 and/or bf16 out). */
+void    nvfp4o_dequant_rows(const uint8_t *Q, const uint8_t *SF, float *out, int64_t r0, int64_t nrows,
+                            int64_t K, int nthreads);
+void    nvfp4o_sgemm_nt(const float *A, const float *B, float alpha, int64_t mrows, int64_t ncols,
+                        int64_t K, float *D32, uint16_t *D16, int nthreads);
+
 /* ---- deterministic synthetic inputs -------------------------------------- */
 /* Counter-based (splitmix64) so that any slice can be generated alone. */
 void    nvfp4o_fill_normal_bf16(uint16_t *X, int64_t n, uint64_t seed, float stddev,

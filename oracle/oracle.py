@@ -50,6 +50,8 @@ def lib():
         L.nvfp4o_dequant.argtypes = [u8p, u8p, f32p, i64, i64, C.c_int]
         L.nvfp4o_gemm_rows.argtypes = [u8p, u8p, u8p, u8p, C.c_float, i64, i64, i64, i64, i64,
                                        f32p, u16p, C.c_int]
+        L.nvfp4o_dequant_rows.argtypes = [u8p, u8p, f32p, i64, i64, i64, C.c_int]
+        L.nvfp4o_sgemm_nt.argtypes = [f32p, f32p, C.c_float, i64, i64, i64, f32p, u16p, C.c_int]
         L.nvfp4o_fill_normal_bf16.argtypes = [u16p, i64, C.c_uint64, C.c_float, C.c_int]
         L.nvfp4o_fill_student_t3_bf16.argtypes = [u16p, i64, i64, C.c_uint64, C.c_int, C.c_float,
                                                    C.c_int]
@@ -158,6 +160,27 @@ def gemm(a, sfa, b, sfb, alpha, M, N, K, m0=0, mrows=None, nthreads=0):
     d16 = np.empty((mrows, N), dtype=np.uint16)
     lib().nvfp4o_gemm_rows(*[_p(t, C.c_uint8) for t in arrs], float(alpha), M, N, K, m0, mrows,
                            _p(d32, C.c_float), _p(d16, C.c_uint16), nthreads)
+    return d32, d16
+
+
+def dequant_rows(q, sf, r0: int, nrows: int, K: int, nthreads: int = 0) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.uint8)
+    sf = np.ascontiguousarray(sf, dtype=np.uint8)
+    out = np.empty((nrows, K), dtype=np.float32)
+    lib().nvfp4o_dequant_rows(_p(q, C.c_uint8), _p(sf, C.c_uint8), _p(out, C.c_float), r0, nrows, K, nthreads)
+    return out
+
+
+def sgemm_nt(af: np.ndarray, bf: np.ndarray, alpha: float, nthreads: int = 0):
+    """fp32 D = alpha * af . bf^T -> (D32, D_bf16_bits)."""
+    af = np.ascontiguousarray(af, dtype=np.float32)
+    bf = np.ascontiguousarray(bf, dtype=np.float32)
+    mrows, K = af.shape
+    ncols = bf.shape[0]
+    d32 = np.empty((mrows, ncols), dtype=np.float32)
+    d16 = np.empty((mrows, ncols), dtype=np.uint16)
+    lib().nvfp4o_sgemm_nt(_p(af, C.c_float), _p(bf, C.c_float), float(alpha), mrows, ncols, K,
+                          _p(d32, C.c_float), _p(d16, C.c_uint16), nthreads)
     return d32, d16
 
 
