@@ -256,6 +256,31 @@ def run_reference(args):
     return 0
 
 
+def vendor_scaled_mm(sets, M, N, K, reps=50):
+    """Comparison point only (never used by the product): torch._scaled_mm, the
+    reference's own oracle (matmul/sm100_nvfp4/main.py:25-34, cuBLASLt block-scaled
+    FP4), on the same rotating operand sets, bf16 out."""
+    try:
+        args = [(a.view(torch.float4_e2m1fn_x2), b.view(torch.float4_e2m1fn_x2).t(),
+                 sfa.view(torch.float8_e4m3fn), sfb.view(torch.float8_e4m3fn)) for a, sfa, b, sfb, _ in sets]
+        for i in range(3):
+            x = args[i % len(args)]
+            torch._scaled_mm(x[0], x[1], x[2], x[3], out_dtype=torch.bfloat16)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            x = args[i % len(args)]
+            torch._scaled_mm(x[0], x[1], x[2], x[3], out_dtype=torch.bfloat16)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        return {"tflops": 2.0 * M * N * K / ms / 1e9, "ms": ms,
+                "what": "torch._scaled_mm (cuBLASLt) NVFP4, same operands, bf16 out; comparison only"}
+    except Exception as e:  # pragma: no cover - depends on the torch build
+        return {"unavailable": f"{type(e).__name__}: {str(e)[:120]}"}
+
+
 def decode_section(nv, dev, pk, reps=30):
     """skinny-M GEMMs against the two FFN weights, judged on HBM
     GB/s.  Weights rotate over 3 sets (> 3x L2).  Bytes per call follow the
@@ -548,6 +573,7 @@ def run_ours(args):
     fp4_peak_est = 4.0 * pk["bf16_tflops"]
     traffic = committed_traffic().get("gemm_8192", {}).get("dram_bytes_per_launch")
     cpu = None
+    vendor = vendor_scaled_mm(sets, M, N, K) if rank == 0 else None
     decode = quant = None
     if not args.no_decode:
         decode = decode_section(nv, dev, pk)
@@ -578,6 +604,8 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if vendor is not None:
+            line["vendor_scaled_mm"] = vendor
         if decode is not None:
             line["decode"] = decode
         if quant is not None:
