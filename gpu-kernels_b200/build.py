@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 OUT = os.path.join(HERE, "nvfp4_b200", "libnvfp4_b200.so")
-SOURCES = ["runtime.cu", "quantize.cu", "gemm.cu", "gemm_pair.cu", "gemm_decode.cu", "probe.cu", "capi.cu"]
+SOURCES = ["runtime.cu", "quantize.cu", "gemm.cu", "gemm_pair.cu", "gemm_decode.cu", "probe.cu", "host_pipeline.cu", "capi.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
          "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden", "-shared", "-cudart", "static"]

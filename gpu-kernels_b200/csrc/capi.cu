@@ -15,6 +15,8 @@ int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
 size_t decode_workspace_bytes(int M, int N);
 int decode_noalloc_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                             uint16_t *D, int M, int N, int K, cudaStream_t stream);
+int gemm_host(const uint8_t *hA, const uint8_t *hSFA, const uint8_t *hB, const uint8_t *hSFB, float alpha,
+              uint16_t *hD, int M, int N, int K, cudaStream_t stream);
 int gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D, int M,
                int N, int K, unsigned long long *trace, cudaStream_t stream);
 int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const void *D, int M,
@@ -119,6 +121,11 @@ int nvfp4_last_status(void) { return g_last_status.load(); }
 int nvfp4_gemm_decode_noalloc(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
                               float alpha, uint16_t *D, int M, int N, int K, void *stream) {
     return decode_noalloc_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+int nvfp4_gemm_host(const uint8_t *hA, const uint8_t *hSFA, const uint8_t *hB, const uint8_t *hSFB, float alpha,
+                    uint16_t *hD, int M, int N, int K, void *stream) {
+    return gemm_host(hA, hSFA, hB, hSFB, alpha, hD, M, N, K, static_cast<cudaStream_t>(stream));
 }
 
 int nvfp4_gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,

@@ -30,6 +30,7 @@ SIGNATURES = {
     "nvfp4_selftest_wait_timeout": (C.c_int, [C.c_uint64]),
     "nvfp4_launch_count": (C.c_uint64, []),
     "nvfp4_gemm_trace": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp, _vp]),
+    "nvfp4_gemm_host": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp]),
     "nvfp4_gemm_decode_noalloc": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int,
                                             _vp]),
     "nvfp4_probe_mma_rate": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]),

@@ -84,6 +84,23 @@ def gemm(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor,
     return d
 
 
+def gemm_host(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, alpha: float,
+              out: torch.Tensor, device: Optional[torch.device] = None) -> torch.Tensor:
+    """D = alpha * A . B^T from and to HOST tensors (pin them for overlap): uploads,
+    per-block GEMMs and the copy of D back are pipelined inside the library.
+    Asynchronous on the device's current stream; synchronise before reading `out`."""
+    for t, n in ((a, "a"), (sfa, "sfa"), (b, "b"), (sfb, "sfb")):
+        if t.is_cuda or t.element_size() != 1 or not t.is_contiguous():
+            raise ValueError(f"{n} must be a contiguous 1-byte host tensor")
+    M, K, N = a.shape[0], a.shape[1] * 2, b.shape[0]
+    if out.is_cuda or out.dtype != torch.bfloat16 or out.shape != (M, N) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 [M, N] host tensor")
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    check(lib().nvfp4_gemm_host(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), float(alpha),
+                                out.data_ptr(), M, N, K, _stream(dev)), "nvfp4_gemm_host")
+    return out
+
+
 def matmul_nvfp4(c: torch.Tensor, sfa: torch.Tensor, sfb: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
                  M: int, N: int, K: int) -> None:
     """Reference launcher signature (matmul/sm100_nvfp4/block_scaled_nvfp4.cuh:7-18):
@@ -124,5 +141,5 @@ def launch_count() -> int:
     return int(lib().nvfp4_launch_count())
 
 
-__all__ = ["NVFP4Error", "global_scale", "quantize", "gemm", "matmul_nvfp4", "create_tensors",
+__all__ = ["NVFP4Error", "global_scale", "quantize", "gemm", "gemm_host", "matmul_nvfp4", "create_tensors",
            "device_status", "set_wait_timeout_ns", "selftest_wait_timeout", "launch_count"]

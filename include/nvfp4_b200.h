@@ -156,6 +156,19 @@ NVFP4_API void nvfp4_set_wait_timeout_ns(uint64_t ns);
 NVFP4_API int nvfp4_selftest_wait_timeout(uint64_t timeout_ns);
 
 /*
+ * The GEMM on HOST buffers (A, SFA, B, SFB in, D out; pinned memory for overlap):
+ * the device-side counterpart of the reference runner's copy-in / GEMM / copy-out
+ * (matmul/sm100_nvfp4/runner.cu:45-59, 78-90), pipelined.  D is cut into up to 4x4
+ * blocks; operand uploads, per-block GEMMs and 2-D copies of D back to the host run
+ * on three internal streams, so the transfers overlap each other and the compute.
+ * Asynchronous: `stream` (the caller's) is made to wait for D to reach the host;
+ * synchronise it before reading hD.  Device buffers are allocated on first use per
+ * device and kept; calls on one device are serialised.
+ */
+NVFP4_API int nvfp4_gemm_host(const uint8_t *hA, const uint8_t *hSFA, const uint8_t *hB,
+               const uint8_t *hSFB, float alpha, uint16_t *hD, int M, int N, int K, void *stream);
+
+/*
  * Allocation-free decode GEMM.  No counterpart in the reference: it exists for
  * callers that cannot let a library allocate device memory — hosts that own all
  * device memory (memory-budgeted servers, plugin interfaces that pass a library
