@@ -1,0 +1,41 @@
+"""PyTorch custom operators over the C ABI: torch.ops.nvfp4_b200.gemm and
+torch.ops.nvfp4_b200.quantize.
+
+Registered with torch.library, so they carry schemas, run under torch.compile /
+FX tracing as opaque ops (fake implementations give output shapes without a GPU)
+and can be called from TorchScript-free model code the way the reference's
+harness calls torch._scaled_mm (matmul/sm100_nvfp4/main.py:25-34).  The CUDA
+implementations are the library's kernels; there is no CPU implementation.
+"""
+from typing import Tuple
+
+import torch
+
+from .layout import sf_bytes
+from .ops import gemm as _gemm
+from .ops import quantize as _quantize
+
+
+@torch.library.custom_op("nvfp4_b200::gemm", mutates_args=(), device_types="cuda")
+def gemm(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, alpha: float,
+         fp16_out: bool = False) -> torch.Tensor:
+    """D = alpha * A . B^T; A [M, K/2] and B [N, K/2] e2m1 codes, blocked e4m3 scales;
+    bf16 (or fp16) [M, N]."""
+    return _gemm(a, sfa, b, sfb, alpha, out_dtype=torch.float16 if fp16_out else torch.bfloat16)
+
+
+@gemm.register_fake
+def _gemm_fake(a, sfa, b, sfb, alpha, fp16_out=False):
+    return a.new_empty((a.shape[0], b.shape[0]), dtype=torch.float16 if fp16_out else torch.bfloat16)
+
+
+@torch.library.custom_op("nvfp4_b200::quantize", mutates_args=(), device_types="cuda")
+def quantize(x: torch.Tensor, global_scale: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [M, K] -> (e2m1 codes uint8 [M, K/2], blocked e4m3 scales uint8 [pad128(M)*K/16])."""
+    return _quantize(x, global_scale)
+
+
+@quantize.register_fake
+def _quantize_fake(x, global_scale):
+    M, K = x.shape
+    return (x.new_empty((M, K // 2), dtype=torch.uint8), x.new_empty((sf_bytes(M, K),), dtype=torch.uint8))
