@@ -31,10 +31,12 @@ struct Params {
     // [0] MMA wait on full  [1] MMA wait on acc_empty  [2] producer wait on empty
     // [3] epilogue wait on acc_full  [4] epilogue drain+store  [5] tiles
     // [6] MMA-thread cycles from first issue to last commit  [7] the same span in ns
+    // [8] %globaltimer at CTA entry  [9] at CTA exit  [10] at the first MMA issue
+    // [11] at the last accumulator commit
     unsigned long long *trace;
     int group_m;  // pair kernel: 256-row tile rows per raster group
 };
-constexpr int kTraceSlots = 8;
+constexpr int kTraceSlots = 12;
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool f16) {
     if (f16) {

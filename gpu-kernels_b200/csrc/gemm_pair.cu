@@ -1,23 +1,29 @@
-// gemm_pair.cu — CTA-pair (tcgen05 cta_group::2) persistent NVFP4 GEMM, one 256x256
+// gemm_pair.cu — CTA-pair (tcgen05 cta_group::2) persistent NVFP4 GEMM, one 256 x BN
 // output tile per pair of SMs.  The kernel for M > 128.
 //
 // CTA rank r of the pair holds A rows [256*tm + 128*r, +128), B rows
-// [256*tn + 128*r, +128), the 128-row scale block of its A rows and both 128-row
-// scale blocks of the tile's B rows (the MMA reads B's scales from each CTA's own
-// TMEM).  Each CTA's producers load those with cta_group::2 TMA loads — each CTA
-// fetches only its own tiles — whose bytes complete on the LEADER's (rank 0) full barrier; the
-// leader's MMA thread issues the pair MMAs (M=256, N=256, K=64) and the scale
-// copies, and commits separately to each CTA's empty / acc_full barriers.  Both
-// CTAs' epilogues drain their own 128x256 TMEM half and arrive on the leader's
-// acc_empty barrier.
+// [BN*tn + BN/2*r, +BN/2), the 128-row scale block of its A rows and the two
+// 128-row scale blocks that cover the tile's BN B rows (the MMA reads B's scales
+// from each CTA's own TMEM).  Each CTA's producers load those with cta_group::2 TMA
+// loads — each CTA fetches only its own tiles — whose bytes complete on the LEADER's
+// (rank 0) full barrier; the leader's MMA thread issues the pair MMAs (M=256, N=BN,
+// K=64) and the scale copies, and commits separately to each CTA's empty / acc_full
+// barriers.  Both CTAs' epilogues drain their own 128 x BN TMEM half and arrive on
+// the leader's acc_empty barrier.
+//
+// BN = 256 (one accumulator: the next tile's MMAs wait for the epilogue to read the
+// previous one out of TMEM) or BN = 192 (two accumulators of 192 columns, so the
+// MMAs of tile i+1 run while the epilogue drains tile i).  A 192-row B tile starts
+// 64 rows into a 128-row scale block on odd tn; its scales are then read from the
+// scale columns shifted by 2 (each TMEM scale column holds 32 rows).
 //
 // The ring is latency-bound: a slot is reloaded only after the MMAs that read it
 // have completed, so throughput = slots / (queued MMA time + commit->producer
 // wake-up + TMA issue + TMA latency, ~1.9K + 0.3K + 1.5K cycles measured).  Slot
-// width is a template parameter: BKB = 128 bytes of K per row (256 fp4, 38 KB per
-// CTA, 5 slots, the default) or BKB = 64 (128 fp4, 19 KB, 11 slots, 64-byte
-// swizzle).  Two producer warps issue each slot's loads (A/B and the scales) in
-// parallel, and a single MMA thread issues with strided (never rebuilt) descriptors.
+// width is a template parameter: BKB = 128 bytes of K per row (256 fp4, the
+// default) or BKB = 64 (128 fp4, 64-byte swizzle).  Two producer warps issue each
+// slot's loads (A/B and the scales) in parallel, and a single MMA thread issues
+// with strided (never rebuilt) descriptors.
 #include <cstdlib>
 #include <cstring>
 
@@ -26,46 +32,52 @@
 namespace nvfp4 {
 namespace gemm {
 
-template <int STAGES, int BKB>
+template <int STAGES, int BKB, int BN>
 struct PairLayout {
     static_assert(BKB == 128 || BKB == 64, "slot width");
+    static_assert(BN == 256 || BN == 192, "tile width");
     static constexpr int kKG = BKB / 32;                 // 64-element k-groups per slot
+    static constexpr int kBRows = BN / 2;                // B rows held by each CTA
     static constexpr int kA = 128 * BKB;                 // this CTA's 128 A rows
-    static constexpr int kB = 128 * BKB;                 // this CTA's 128 B rows
+    static constexpr int kB = kBRows * BKB;              // this CTA's BN/2 B rows
     static constexpr int kSfa = kKG * 512;               // A scales (one 128-row block)
-    static constexpr int kSfb = 2 * kKG * 512;           // B scales (both 128-row blocks of the tile)
+    static constexpr int kSfb = 2 * kKG * 512;           // B scales (the two 128-row blocks covering the tile)
     static constexpr int kStage = kA + kB + kSfa + kSfb;
     static constexpr int kOffA = 0;
     static constexpr int kOffB = kOffA + STAGES * kA;
     static constexpr int kOffSfa = kOffB + STAGES * kB;
     static constexpr int kOffSfb = kOffSfa + STAGES * kSfa;
     static constexpr int kOffBar = kOffSfb + STAGES * kSfb;
-    static constexpr int kBarBytes = (2 * STAGES + 3) * 8 + 16;
+    static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 16;  // full, empty, acc_full x2, acc_empty x2, drain
     static constexpr int kDynamicSmem = kOffBar + kBarBytes + 1024;
     static constexpr uint32_t kTxBytes = 2u * kStage;    // both CTAs complete on the leader's barrier
     // shared-memory matrix descriptor: 128B or 64B swizzle, 8-row core groups
     static constexpr uint32_t kLayout = BKB == 128 ? 2 : 4;
     static constexpr uint32_t kSbo = 8 * BKB;
-    // TMEM: accumulator [0, 256), then rotating sets of scale columns (SFA 4 + SFB 8
-    // per k-group); the tensor pipe executes copies and MMAs in issue order, so a set
-    // is rewritten only after the MMAs that read it
+    // TMEM: kAccBufs accumulators of BN columns, then rotating sets of scale columns
+    // (SFA 4 + SFB 8 per k-group); the tensor pipe executes copies and MMAs in issue
+    // order, so a set is rewritten only after the MMAs that read it
     static constexpr int kSfColsPerGroup = 12;
     static constexpr int kSfCols = kKG * kSfColsPerGroup;
-    static constexpr int kSfSets = (256 / kSfCols) < STAGES ? (256 / kSfCols) : STAGES;
     static constexpr int kTmemCols = 512;
-    static_assert(256 + kSfSets * kSfCols <= kTmemCols, "tensor memory budget");
+    static constexpr int kAccBufs = (2 * BN + kSfCols <= kTmemCols) ? 2 : 1;
+    static constexpr int kSfBase = kAccBufs * BN;
+    static constexpr int kSfSetsFit = (kTmemCols - kSfBase) / kSfCols;
+    static constexpr int kSfSets = kSfSetsFit < STAGES ? kSfSetsFit : STAGES;
+    static_assert(kSfSets >= 1 && kSfBase + kSfSets * kSfCols <= kTmemCols, "tensor memory budget");
+    static_assert(kB % 1024 == 0, "B slot must keep 1024-byte alignment for the swizzle");
     static_assert(kDynamicSmem <= 232448, "shared memory budget");
 };
 
 constexpr int kPairThreads = 32 * (3 + kEpiWarps);  // A/B producer, MMA, 8 epilogue, scale producer
 constexpr int kSfProducerWarp = 2 + kEpiWarps;
 
-template <int STAGES, int BKB, bool F16, bool TRACE>
+template <int STAGES, int BKB, int BN, bool F16, bool TRACE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                            const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                            const Params p) {
-    using L = PairLayout<STAGES, BKB>;
+    using L = PairLayout<STAGES, BKB, BN>;
     constexpr int KG = L::kKG;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -74,24 +86,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     const uint32_t bar_full = base + L::kOffBar;
     const uint32_t bar_empty = bar_full + 8 * STAGES;
     const uint32_t bar_acc_full = bar_empty + 8 * STAGES;
-    const uint32_t bar_acc_empty = bar_acc_full + 8;
-    const uint32_t bar_drain = bar_acc_empty + 8;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(base_ptr + L::kOffBar + (2 * STAGES + 3) * 8);
+    const uint32_t bar_acc_empty = bar_acc_full + 16;  // [2] each; buffer b at +8*b
+    const uint32_t bar_drain = bar_acc_empty + 16;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(base_ptr + L::kOffBar + (2 * STAGES + 5) * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
+    if (TRACE && threadIdx.x == 0) p.trace[blockIdx.x * kTraceSlots + 8] = global_timer_ns();
     const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
-    const int n_m = (p.M + 255) / 256, n_n = (p.N + 255) / 256, n_tiles = n_m * n_n;
+    const int n_m = (p.M + 255) / 256, n_n = (p.N + BN - 1) / BN, n_tiles = n_m * n_n;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(bar_full + 8 * s, 1);
             mbar_init(bar_empty + 8 * s, 1);
         }
-        mbar_init(bar_acc_full, 1);
-        mbar_init(bar_acc_empty, 2 * kEpiWarps);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(bar_acc_full + 8 * b, 1);
+            mbar_init(bar_acc_empty + 8 * b, 2 * kEpiWarps);
+        }
         mbar_init(bar_drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -135,10 +150,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             for (int t = pair; ok && t < n_tiles; t += num_pairs) {
                 int tm, tn;
                 coords(t, tm, tn);
-                const int arow = tm * 256 + rank * 128, brow = tn * 256 + rank * 128;
-                // scale tensors viewed as rows of 256 bytes: one (128-row block, 64-K group) = 2 rows
-                const int ysa = (tm * 2 + (int)rank) * rest_k * 2, ysb0 = tn * 2 * rest_k * 2,
-                          ysb1 = (tn * 2 + 1) * rest_k * 2;
+                const int arow = tm * 256 + rank * 128, brow = tn * BN + rank * L::kBRows;
+                // scale tensors viewed as rows of 256 bytes: one (128-row block, 64-K group) =
+                // 2 rows; the tile's B rows lie in 128-row blocks sb and sb + 1
+                const int sb = (tn * BN) >> 7;
+                const int ysa = (tm * 2 + (int)rank) * rest_k * 2, ysb0 = sb * rest_k * 2,
+                          ysb1 = (sb + 1) * rest_k * 2;
                 for (int kb = 0; kb < p.num_kb; kb++) {
                     const long long c0 = TRACE ? clock64() : 0;
                     if (!mbar_try_wait(emp, phase ^ 1) && !wait_parity(emp, phase ^ 1, tmo, abort_flag)) {
@@ -194,13 +211,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         // columns rotate through kSfSets sets, and a slot's scale copies go out before
         // its MMAs.
         if (rank == 0 && elect_one()) {
-            constexpr uint32_t idesc = idesc_mxf4nvf4(256, 256);
+            constexpr uint32_t idesc = idesc_mxf4nvf4(256, BN);
             const uint32_t empty0 = map_to_cta(bar_empty, 0), empty1 = map_to_cta(bar_empty, 1);
             const uint32_t accf0 = map_to_cta(bar_acc_full, 0), accf1 = map_to_cta(bar_acc_full, 1);
             const uint64_t a_desc0 = smem_desc(sA, 16, L::kSbo, L::kLayout);
             const uint64_t b_desc0 = smem_desc(sB, 16, L::kSbo, L::kLayout);
             const uint64_t sfa_desc0 = smem_desc(sSfa, 16, 128, 0), sfb_desc0 = smem_desc(sSfb, 16, 128, 0);
-            const uint32_t sf_col0 = tmem_base + 256;
+            const uint32_t sf_col0 = tmem_base + L::kSfBase;
             uint32_t stage = 0, phase = 0, sf_set = 0;
             uint64_t a_d = a_desc0, b_d = b_desc0, sfa_d = sfa_desc0, sfb_d = sfb_desc0;
             uint32_t sf_col = sf_col0, full_bar = bar_full, e0 = empty0, e1 = empty1;
@@ -209,8 +226,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             long long t_full = 0, t_acc = 0, t_first = 0;
             uint64_t ns_first = 0;
             for (int t = pair; ok && t < n_tiles; t += num_pairs, local++) {
+                int tm, tn;
+                coords(t, tm, tn);
+                // accumulator buffer and its use count; B-scale column shift of this tile
+                const uint32_t buf = L::kAccBufs == 2 ? (uint32_t)(local & 1) : 0u;
+                const uint32_t use = L::kAccBufs == 2 ? (uint32_t)(local >> 1) : (uint32_t)local;
+                const uint32_t d_tmem = tmem_base + buf * BN;
+                const uint32_t sfb_shift = (uint32_t)(((tn * BN) & 127) >> 5);
                 long long c0 = TRACE ? clock64() : 0;
-                if (!wait_parity(bar_acc_empty, (local & 1) ^ 1, tmo, abort_flag)) {
+                if (!wait_parity(bar_acc_empty + 8 * buf, (use & 1) ^ 1, tmo, abort_flag)) {
                     report_timeout(abort_flag, p.ctl.status);
                     ok = false;
                     break;
@@ -246,7 +270,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
 #pragma unroll
                         for (int j = 0; j < KG; j++) {
                             const uint32_t col = sf_col + j * L::kSfColsPerGroup;
-                            mma_mxf4nvf4_pair(tmem_base, a_d + j * 2, b_d + j * 2, idesc, col, col + 4,
+                            mma_mxf4nvf4_pair(d_tmem, a_d + j * 2, b_d + j * 2, idesc, col, col + 4 + sfb_shift,
                                               j == 0 ? acc0 : 1u);
                         }
                     } else {
@@ -256,7 +280,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                             tmem_cp_32x128_x4_pair(col, sfa_d + j * 32);
                             tmem_cp_32x128_x4_pair(col + 4, sfb_d + j * 32);
                             tmem_cp_32x128_x4_pair(col + 8, sfb_d + (KG + j) * 32);
-                            mma_mxf4nvf4_pair(tmem_base, a_d + j * 2, b_d + j * 2, idesc, col, col + 4,
+                            mma_mxf4nvf4_pair(d_tmem, a_d + j * 2, b_d + j * 2, idesc, col, col + 4 + sfb_shift,
                                               j == 0 ? acc0 : 1u);
                         }
                     }
@@ -290,8 +314,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     }
                 }
                 if (!ok) break;
-                mma_commit_pair(accf0);
-                mma_commit_pair(accf1);
+                mma_commit_pair(accf0 + 8 * buf);
+                mma_commit_pair(accf1 + 8 * buf);
             }
             if (!ok && any_issued) {
                 volatile int never = 0;
@@ -304,23 +328,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 tr[1] = t_acc;
                 tr[5] = local;
                 tr[6] = clock64() - t_first;
-                tr[7] = global_timer_ns() - ns_first;
+                const uint64_t ns_last = global_timer_ns();
+                tr[7] = ns_last - ns_first;
+                tr[10] = ns_first;
+                tr[11] = ns_last;
             }
         }
     } else {
         // ------------------------------------------------------------ epilogue (warps 2..9, both CTAs)
         const int quarter = warp & 3;
         const int half = (warp - 2) >> 2;
-        constexpr int kCols = 128;
+        constexpr int kCols = BN / 2;
         const uint32_t lead_acc_empty = map_to_cta(bar_acc_empty, 0);
         int local = 0;
         long long t_accw = 0, t_store = 0, c_ready = 0;
         for (int t = pair; t < n_tiles; t += num_pairs, local++) {
             int tm, tn;
             coords(t, tm, tn);
+            const uint32_t buf = L::kAccBufs == 2 ? (uint32_t)(local & 1) : 0u;
+            const uint32_t use = L::kAccBufs == 2 ? (uint32_t)(local >> 1) : (uint32_t)local;
             bool ok = true;
             const long long c0 = TRACE ? clock64() : 0;
-            if (lane == 0) ok = wait_parity(bar_acc_full, local & 1, tmo, abort_flag);
+            if (lane == 0) ok = wait_parity(bar_acc_full + 8 * buf, use & 1, tmo, abort_flag);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (TRACE) {
                 c_ready = clock64();
@@ -332,15 +361,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             }
             tc_fence_after();
             uint32_t acc[kCols];
-            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * kCols;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN + half * kCols;
 #pragma unroll
             for (int c = 0; c < kCols / 32; c++)
                 tmem_ld_32x32b_x32(taddr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&acc[c * 32]));
             tmem_ld_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(lead_acc_empty);
-            store_row<kCols, F16>(acc, p, tm * 256 + (int)rank * 128 + quarter * 32 + lane, tn * 256 + half * kCols);
+            if (lane == 0) mbar_arrive_cluster(lead_acc_empty + 8 * buf);
+            store_row<kCols, F16>(acc, p, tm * 256 + (int)rank * 128 + quarter * 32 + lane, tn * BN + half * kCols);
             if (TRACE && warp == 2 && lane == 0) t_store += clock64() - c_ready;
         }
         if (TRACE && warp == 2 && lane == 0) {
@@ -357,6 +386,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         tc_fence_after();
         tmem_dealloc_pair(tmem_base, L::kTmemCols);
     }
+    if (TRACE && threadIdx.x == 0) p.trace[blockIdx.x * kTraceSlots + 9] = global_timer_ns();
 }
 
 // Raster group (256-row tile rows sharing a sweep over N); env NVFP4_GROUP_M overrides.
@@ -369,12 +399,13 @@ static int pair_group_m() {
     return v;
 }
 
-template <int STAGES, int BKB, bool F16>
+template <int STAGES, int BKB, int BN, bool F16>
 static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                        void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di,
                        unsigned long long *trace) {
-    using L = PairLayout<STAGES, BKB>;
-    auto kern = trace ? nvfp4_gemm_pair_kernel<STAGES, BKB, F16, true> : nvfp4_gemm_pair_kernel<STAGES, BKB, F16, false>;
+    using L = PairLayout<STAGES, BKB, BN>;
+    auto kern = trace ? nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, true>
+                      : nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, false>;
     static int configured[2][64] = {};
     if (!configured[trace != nullptr][di.device]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamicSmem) != cudaSuccess)
@@ -383,7 +414,7 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     }
     CUtensorMap ta, tb, tsa, tsb;
     int st = operand_map(A, M, K, 128, BKB, &ta);
-    if (!st) st = operand_map(B, N, K, 128, BKB, &tb);
+    if (!st) st = operand_map(B, N, K, L::kBRows, BKB, &tb);
     // scale tensors as [bytes/256, 256]: one (128-row block, 64-K group) chunk is two rows
     const uint64_t sfa_rows = (uint64_t)((M + 127) / 128) * (K / 64) * 2;
     const uint64_t sfb_rows = (uint64_t)((N + 127) / 128) * (K / 64) * 2;
@@ -401,7 +432,7 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     p.K = K;
     p.alpha = alpha;
     p.num_m_tiles = (M + 255) / 256;
-    p.num_n_tiles = (N + 255) / 256;
+    p.num_n_tiles = (N + BN - 1) / BN;
     p.num_tiles = p.num_m_tiles * p.num_n_tiles;
     p.num_kb = (K + 2 * BKB - 1) / (2 * BKB);
     p.k_groups = K / 64;
@@ -415,14 +446,31 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     return cuda_status(cudaGetLastError());
 }
 
-// Ring shape of the pair kernel: 5 slots of 128 bytes of K (default) or 11 of 64;
-// env NVFP4_PAIR_RING=5x128|11x64 overrides.  Measured at M=N=K=8192: 5x128 spends
-// 268K MMA-thread cycles per CTA pair, 11x64 405K — the single issuing thread's
-// fixed cost per slot (wait, fence, two commits) outweighs the deeper ring.
-static int pair_ring() {
+// Tile and ring shape of the pair kernel (env NVFP4_PAIR_RING overrides):
+//   "6x128n192"  256x192 tiles, two TMEM accumulators, 6 slots of 128 bytes of K
+//   "5x128"      256x256 tiles, one accumulator, 5 slots of 128 bytes of K
+//   "11x64"      256x256 tiles, one accumulator, 11 slots of 64 bytes of K
+// Measured at M=N=K=8192: 5x128 spends 268K MMA-thread cycles per CTA pair, 11x64
+// 405K — the single issuing thread's fixed cost per slot (wait, fence, two commits)
+// outweighs the deeper ring.  6x128n192 (trace: 0.4 % waiting for an accumulator)
+// runs 213 us against 5x128's 200 us: the issuing thread needs ~455 cycles per slot
+// whatever the tile width, more than a 192-wide slot's 384 cycles of MMA work.
+// Writing the scales into TMEM from other warps (tcgen05.st) instead of tcgen05.cp
+// was measured 2.4-3x slower: those stores complete only behind the MMAs already
+// queued, so the scale path serialises with the tensor pipe.
+enum PairCfg {
+    kCfg5x128 = 0,
+    kCfg11x64 = 1,
+    kCfg6x128n192 = 2,
+    kCfgDefault = kCfg5x128
+};
+static int pair_cfg() {
     static int v = [] {
         const char *e = std::getenv("NVFP4_PAIR_RING");
-        return (e && !std::strcmp(e, "11x64")) ? 64 : 128;
+        if (e && !std::strcmp(e, "11x64")) return (int)kCfg11x64;
+        if (e && !std::strcmp(e, "5x128")) return (int)kCfg5x128;
+        if (e && !std::strcmp(e, "6x128n192")) return (int)kCfg6x128n192;
+        return (int)kCfgDefault;
     }();
     return v;
 }
@@ -431,8 +479,12 @@ template <bool F16>
 static int launch_pair_cfg(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                            void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di,
                            unsigned long long *trace) {
-    if (pair_ring() == 128) return launch_pair<5, 128, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
-    return launch_pair<11, 64, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
+    switch (pair_cfg()) {
+        case kCfg11x64: return launch_pair<11, 64, 256, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
+        case kCfg6x128n192:
+            return launch_pair<6, 128, 192, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
+        default: return launch_pair<5, 128, 256, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
+    }
 }
 
 }  // namespace gemm

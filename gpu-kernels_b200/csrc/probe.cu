@@ -12,6 +12,13 @@
 //        2 CTA pair M=256 N=256, MMA only
 //        3 CTA pair, 3 scale copies before each MMA
 //        4 CTA pair, the 12 scale copies of a 4-MMA stage issued first, then 4 MMAs
+//        5 CTA pair M=256 N=192, 3 scale copies before each MMA
+// Issue-cost modes (the iteration is shorter than its tensor work would allow, so
+// cycles per iteration measure the issuing thread):
+//        6 CTA pair, 3 scale copies per iteration, no MMA
+//        7 CTA pair M=256 N=64 MMA only (32 cycles of tensor work each)
+//        8 CTA pair N=64 MMA + 2 commits (one per CTA's barrier) per iteration
+//        9 CTA pair, 3 scale copies + N=64 MMA + 2 commits per iteration
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -26,6 +33,7 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, unsigned l
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     __shared__ uint32_t tmem_slot;
     __shared__ __align__(8) uint64_t bar;
+    __shared__ __align__(8) uint64_t bar2;  // per-iteration commits of modes 8 and 9 (never waited on)
     const int warp = threadIdx.x >> 5;
     // zero operands and scales: throughput does not depend on the values
     for (int i = threadIdx.x * 16; i < kProbeSmem - 1024; i += blockDim.x * 16)
@@ -33,6 +41,7 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, unsigned l
     fence_proxy_async_smem();
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(&bar), 1);
+        mbar_init(smem_u32(&bar2), 1);
         fence_barrier_init();
     }
     if (warp == 0) {
@@ -51,7 +60,8 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, unsigned l
     const uint32_t sA = base, sB = base + 16384, sSf = base + 49152;
     const bool issuer = kPair ? (cluster_ctarank() == 0) : true;
     if (warp == 0 && issuer && elect_one()) {
-        constexpr uint32_t idesc = idesc_mxf4nvf4(kPair ? 256 : 128, 256);
+        constexpr uint32_t idesc = idesc_mxf4nvf4(kPair ? 256 : 128, MODE == 5 ? 192 : (MODE >= 7 ? 64 : 256));
+        const uint32_t c0 = map_to_cta(smem_u32(&bar2), 0), c1 = map_to_cta(smem_u32(&bar2), 1);
         const unsigned long long t0 = clock64();
         for (int i = 0; i < iters; i++) {
             const int j = i & 3;
@@ -66,11 +76,28 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, unsigned l
                 mma_mxf4nvf4(tmem, ad, bd, idesc, col, col + 4, i != 0);
             } else if constexpr (MODE == 2) {
                 mma_mxf4nvf4_pair(tmem, ad, bd, idesc, col, col + 4, i != 0);
-            } else if constexpr (MODE == 3) {
+            } else if constexpr (MODE == 3 || MODE == 5) {
                 tmem_cp_32x128_x4_pair(col, smem_desc(sSf + j * 512, 16, 128, 0));
                 tmem_cp_32x128_x4_pair(col + 4, smem_desc(sSf + 2048 + j * 512, 16, 128, 0));
                 tmem_cp_32x128_x4_pair(col + 8, smem_desc(sSf + 4096 + j * 512, 16, 128, 0));
                 mma_mxf4nvf4_pair(tmem, ad, bd, idesc, col, col + 4, i != 0);
+            } else if constexpr (MODE == 6) {
+                tmem_cp_32x128_x4_pair(col, smem_desc(sSf + j * 512, 16, 128, 0));
+                tmem_cp_32x128_x4_pair(col + 4, smem_desc(sSf + 2048 + j * 512, 16, 128, 0));
+                tmem_cp_32x128_x4_pair(col + 8, smem_desc(sSf + 4096 + j * 512, 16, 128, 0));
+            } else if constexpr (MODE == 7) {
+                mma_mxf4nvf4_pair(tmem, ad, bd, idesc, col, col + 4, i != 0);
+            } else if constexpr (MODE == 8) {
+                mma_mxf4nvf4_pair(tmem, ad, bd, idesc, col, col + 4, i != 0);
+                mma_commit_pair(c0);
+                mma_commit_pair(c1);
+            } else if constexpr (MODE == 9) {
+                tmem_cp_32x128_x4_pair(col, smem_desc(sSf + j * 512, 16, 128, 0));
+                tmem_cp_32x128_x4_pair(col + 4, smem_desc(sSf + 2048 + j * 512, 16, 128, 0));
+                tmem_cp_32x128_x4_pair(col + 8, smem_desc(sSf + 4096 + j * 512, 16, 128, 0));
+                mma_mxf4nvf4_pair(tmem, ad, bd, idesc, col, col + 4, i != 0);
+                mma_commit_pair(c0);
+                mma_commit_pair(c1);
             } else {
                 if (j == 0) {
 #pragma unroll
@@ -133,7 +160,7 @@ using namespace nvfp4;
 // (FLOP of all MMAs / elapsed device time measured with CUDA events) and the
 // longest per-SM MMA-issue time in cycles.  Synchronous; allocates a few bytes.
 extern "C" NVFP4_API int nvfp4_probe_mma_rate(int mode, int iters, double *tflops, double *cycles_per_mma) {
-    if (mode < 0 || mode > 4 || iters < 16 || !tflops) return NVFP4_ERR_INVALID;
+    if (mode < 0 || mode > 9 || iters < 16 || !tflops) return NVFP4_ERR_INVALID;
     DeviceInfo di;
     int st = device_info(&di);
     if (st) return st;
@@ -149,7 +176,12 @@ extern "C" NVFP4_API int nvfp4_probe_mma_rate(int mode, int iters, double *tflop
             case 1: return run_probe<1>(it, di.sm_count, nullptr, dcyc);
             case 2: return run_probe<2>(it, di.sm_count, nullptr, dcyc);
             case 3: return run_probe<3>(it, di.sm_count, nullptr, dcyc);
-            default: return run_probe<4>(it, di.sm_count, nullptr, dcyc);
+            case 4: return run_probe<4>(it, di.sm_count, nullptr, dcyc);
+            case 5: return run_probe<5>(it, di.sm_count, nullptr, dcyc);
+            case 6: return run_probe<6>(it, di.sm_count, nullptr, dcyc);
+            case 7: return run_probe<7>(it, di.sm_count, nullptr, dcyc);
+            case 8: return run_probe<8>(it, di.sm_count, nullptr, dcyc);
+            default: return run_probe<9>(it, di.sm_count, nullptr, dcyc);
         }
     };
     st = go(iters);  // warm-up (clocks ramp)
@@ -165,8 +197,10 @@ extern "C" NVFP4_API int nvfp4_probe_mma_rate(int mode, int iters, double *tflop
         cudaEventElapsedTime(&ms, e0, e1);
         const bool pair = mode >= 2;
         const int ctas = pair ? di.sm_count / 2 * 2 : di.sm_count;
-        // per MMA: 2 * M * N * K with M = 256 over a pair (128 per CTA), N = 256, K = 64
-        const double flop = (double)ctas * iters * 2.0 * 128 * 256 * 64;
+        // per MMA: 2 * M * N * K with M = 256 over a pair (128 per CTA), N = 256 (192 in
+        // mode 5, 64 in modes 7-9, no MMA in mode 6), K = 64
+        const int n = mode == 5 ? 192 : (mode >= 7 ? 64 : (mode == 6 ? 0 : 256));
+        const double flop = (double)ctas * iters * 2.0 * 128 * n * 64;
         *tflops = flop / (ms * 1e-3) / 1e12;
         unsigned long long cyc = 0;
         cudaMemcpy(&cyc, dcyc, sizeof(cyc), cudaMemcpyDeviceToHost);

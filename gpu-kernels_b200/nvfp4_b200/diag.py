@@ -16,7 +16,12 @@ from ._lib import check, lib
 
 PROBE_MODES = {0: "single-CTA MMA only", 1: "single-CTA MMA + 3 scale copies each",
                2: "CTA-pair MMA only", 3: "CTA-pair MMA + 3 scale copies each",
-               4: "CTA-pair, 12 scale copies per 4-MMA stage first"}
+               4: "CTA-pair, 12 scale copies per 4-MMA stage first",
+               5: "CTA-pair N=192 + 3 scale copies each",
+               6: "CTA-pair, 3 scale copies per iteration, no MMA (issue cost)",
+               7: "CTA-pair N=64 MMA only (issue cost)",
+               8: "CTA-pair N=64 MMA + 2 commits (issue cost)",
+               9: "CTA-pair 3 copies + N=64 MMA + 2 commits (issue cost)"}
 
 
 def probe(iters: int = 20000):
@@ -30,29 +35,51 @@ def probe(iters: int = 20000):
 
 
 def trace(M: int, N: int, K: int, reps: int = 3):
+    """Per-CTA cycle breakdown of the CTA-pair kernel (the last of `reps` launches),
+    plus the kernel's event time and where the time outside the MMA span goes."""
+    from ._lib import lib as _l
     from .ops import create_tensors
+    slots = 12
     dev = torch.device("cuda", 0)
     a, b, sfa, sfb = create_tensors(M, N, K, seed=1)
     sfa = torch.full_like(sfa, 0x38)
     sfb = torch.full_like(sfb, 0x38)
     d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
-    tr = torch.zeros(148 * 8, dtype=torch.int64, device=dev)
+    tr = torch.zeros(148 * slots, dtype=torch.int64, device=dev)
     s = torch.cuda.current_stream().cuda_stream
-    for _ in range(reps):
-        check(lib().nvfp4_gemm_trace(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), 1.0, d.data_ptr(),
-                                     M, N, K, tr.data_ptr(), s), "trace")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(reps):
+        if i == reps - 1:
+            e0.record()
+        check(_l().nvfp4_gemm_trace(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), 1.0, d.data_ptr(),
+                                    M, N, K, tr.data_ptr(), s), "trace")
+    e1.record()
     torch.cuda.synchronize()
-    t = tr.view(148, 8).cpu()
+    t = tr.view(148, slots).cpu()
+    ctas = int((t[:, 8] > 0).sum())
+    t = t[:ctas]
     leaders = t[0::2]
     span = leaders[:, 6].double()
     rows = {"mma_wait_full": leaders[:, 0], "mma_wait_acc": leaders[:, 1], "producer_wait_empty": t[:, 2],
             "epi_wait_acc_full": t[:, 3], "epi_drain_store": t[:, 4]}
-    res = {"M": M, "N": N, "K": K, "tiles_per_pair": statistics.mean(leaders[:, 5].tolist()),
+    res = {"M": M, "N": N, "K": K, "event_us": e0.elapsed_time(e1) * 1e3,
+           "tiles_per_pair": statistics.mean(leaders[:, 5].tolist()),
            "mma_span_cycles": statistics.mean(span.tolist()),
            "sm_clock_mhz": statistics.mean((leaders[:, 6].double() / leaders[:, 7].double() * 1e3).tolist())}
     for k, v in rows.items():
         res[k + "_cycles"] = statistics.mean(v.double().tolist())
         res[k + "_frac_of_span"] = res[k + "_cycles"] / res["mma_span_cycles"]
+    t0 = int(t[:, 8].min())
+    us = lambda x: float(x) / 1e3  # noqa: E731
+    res.update({
+        "cta_span_us": us(t[:, 9].max() - t0),                      # first CTA entry -> last CTA exit
+        "entry_spread_us": us(t[:, 8].max() - t0),                  # launch skew across CTAs
+        "prologue_us": us((leaders[:, 10] - leaders[:, 8]).double().mean()),  # entry -> first MMA issue
+        "mma_span_us_mean": us(leaders[:, 7].double().mean()),
+        "last_commit_min_us": us(leaders[:, 11].min() - t0),         # tail imbalance across pairs
+        "last_commit_max_us": us(leaders[:, 11].max() - t0),
+        "epilogue_tail_us": us((leaders[:, 9] - leaders[:, 11]).double().mean()),  # last commit -> CTA exit
+    })
     return res
 
 

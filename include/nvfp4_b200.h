@@ -193,14 +193,19 @@ NVFP4_API int nvfp4_gemm_decode_noalloc(const uint8_t *A, const uint8_t *SFA, co
  * an unused per-SM event recorder, matmul/sm100_nvfp4/profiler.cuh:4-72).
  *
  * nvfp4_gemm_trace: the CTA-pair GEMM with a per-CTA cycle trace written to
- * `trace` (device, 148 x 8 uint64): [0] MMA wait on full stages, [1] MMA wait on
+ * `trace` (device, 148 x 12 uint64): [0] MMA wait on full stages, [1] MMA wait on
  * a free accumulator, [2] producer wait on empty stages, [3] epilogue wait on a
- * full accumulator, [4] epilogue drain + stores, [5] tiles, [6] MMA-thread span.
+ * full accumulator, [4] epilogue drain + stores, [5] tiles, [6] MMA-thread span
+ * in cycles, [7] the same in ns, [8]/[9] %globaltimer at CTA entry/exit,
+ * [10]/[11] at the first MMA issue / last accumulator commit.
  *
  * nvfp4_probe_mma_rate: measured kind::mxf4nvf4 tensor rate on every SM with
  * operands resident in shared memory (mode 0/1: single CTA without/with the
  * scale copies; 2/3: CTA pair without/with; 4: pair, scale copies batched per
- * 4-MMA stage).  Synchronous; returns TFLOP/s and cycles per MMA.
+ * 4-MMA stage; 5: pair with N = 192 and the scale copies; 6-9 measure the issuing
+ * thread: 6 scale copies alone, 7 N = 64 MMAs, 8 N = 64 MMA + 2 commits, 9 copies +
+ * N = 64 MMA + 2 commits).  Synchronous; returns TFLOP/s and cycles per iteration
+ * (one MMA, or one group of copies in mode 6).
  */
 NVFP4_API int nvfp4_gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
                float alpha, uint16_t *D, int M, int N, int K, uint64_t *trace, void *stream);

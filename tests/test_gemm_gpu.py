@@ -146,10 +146,18 @@ def test_c2_full_size_sampled(nv, oracle, cuda_dev, N, K):
     assert not torch.isnan(d).any()
 
 
-@pytest.mark.parametrize("variant,ring", [("single", "11x64"), ("pair", "11x64"), ("pair", "5x128")])
-def test_forced_kernel_variant(variant, ring, tmp_path):
-    """Both persistent kernels (single-CTA 128x256 and CTA-pair 256x256 tiles, the
-    latter with both ring shapes) on the same ragged shape, each forced through
+@pytest.mark.parametrize("variant,ring,shape", [
+    ("single", "11x64", (520, 776, 1344)),
+    ("pair", "11x64", (520, 776, 1344)),
+    ("pair", "5x128", (520, 776, 1344)),
+    ("pair", "6x128n192", (520, 776, 1344)),
+    # 16 x 22 tiles of 256x192 over 74 pairs: each TMEM accumulator is reused 2-3 times
+    ("pair", "6x128n192", (4096, 4224, 512)),
+])
+def test_forced_kernel_variant(variant, ring, shape, tmp_path):
+    """The persistent kernels (single-CTA 128x256 tiles; CTA-pair 256x256 tiles with
+    both ring shapes; CTA-pair 256x192 tiles with two accumulators, whose odd column
+    tiles read shifted B-scale columns) on ragged shapes, each forced through
     NVFP4_GEMM_VARIANT / NVFP4_PAIR_RING in a fresh process."""
     import os
     import subprocess
@@ -160,7 +168,7 @@ import sys, numpy as np, torch
 sys.path[:0] = [{root!r}, {os.path.join(root, 'gpu-kernels_b200')!r}]
 import nvfp4_b200 as nv
 from oracle import oracle as o
-M, N, K = 520, 776, 1344
+M, N, K = {shape!r}
 a, sfa = o.random_codes(M, K, seed=1, sf_lo=0x30, sf_hi=0x40)
 b, sfb = o.random_codes(N, K, seed=2, sf_lo=0x30, sf_hi=0x40)
 t = lambda x: torch.from_numpy(x).cuda()
@@ -168,7 +176,9 @@ d = nv.gemm(t(a), t(sfa), t(b), t(sfb), 0.5)
 torch.cuda.synchronize(); nv.device_status()
 _, d16 = o.gemm(a, sfa, b, sfb, 0.5, M, N, K)
 ref = o.bf16_bits_to_f32(d16).reshape(M, N)
-err = np.abs(d.float().cpu().numpy() - ref).max() / np.abs(ref).max()
+got = d.float().cpu().numpy()
+assert np.isfinite(got).all()
+err = np.abs(got - ref).max() / np.abs(ref).max()
 assert err <= 1e-2, err
 print("ok", err)
 """
