@@ -8,8 +8,12 @@
 #include <utility>
 
 #include "common.cuh"
+#include "epilogue.cuh"
 
 namespace nvfp4 {
+int gemm_dispatch_epi(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
+                      int M, int N, int K, cudaStream_t stream, bool f16, const Epi &epi);
+int sf_pad_zero(uint8_t *SF, int M, int K, cudaStream_t s, const DeviceInfo &di);
 int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                   int M, int N, int K, cudaStream_t stream, bool f16);
 size_t decode_workspace_bytes(int M, int N);
@@ -22,7 +26,8 @@ int gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uin
 int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const void *D, int M,
                   int N, int K);
 int decode_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
-                    uint16_t *D, int M, int N, int K, void *ws, size_t ws_bytes, cudaStream_t stream);
+                    uint16_t *D, int M, int N, int K, void *ws, size_t ws_bytes, cudaStream_t stream,
+                    const Epi &epi = Epi());
 }  // namespace nvfp4
 
 using namespace nvfp4;
@@ -86,6 +91,39 @@ int nvfp4_gemm(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uin
         return decode_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, ws, bytes, s);
     }
     return gemm_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, s, false);
+}
+
+int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                        uint16_t *D, int M, int N, int K, const nvfp4_epilogue *epi, void *stream) {
+    if (!epi) return nvfp4_gemm(A, SFA, B, SFB, alpha, D, M, N, K, stream);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    Epi e;
+    e.bias = epi->bias;
+    e.act = epi->activation;
+    e.q = epi->q_out;
+    e.sf = epi->sf_out;
+    e.gs = epi->out_global_scale;
+    if (e.act < NVFP4_ACT_NONE || e.act > NVFP4_ACT_GELU_TANH) return NVFP4_ERR_INVALID;
+    if (e.bias && (reinterpret_cast<uintptr_t>(e.bias) & 1u)) return NVFP4_ERR_ALIGN;
+    if (e.q) {
+        if (!e.sf || !e.gs) return NVFP4_ERR_INVALID;
+        if (N % 64) return NVFP4_ERR_SHAPE;
+        if ((reinterpret_cast<uintptr_t>(e.sf) & 3u) || (reinterpret_cast<uintptr_t>(e.gs) & 3u)) return NVFP4_ERR_ALIGN;
+    }
+    int st = gemm_validate(A, SFA, B, SFB, e.q ? static_cast<const void *>(e.q) : D, M, N, K);
+    if (st) return st;
+    if (M <= decode_max_m()) {
+        void *ws = nullptr;
+        size_t bytes = 0;
+        if ((st = internal_workspace(M, N, s, &ws, &bytes))) return st;
+        st = decode_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, ws, bytes, s, e);
+    } else {
+        st = gemm_dispatch_epi(A, SFA, B, SFB, alpha, D, M, N, K, s, false, e);
+    }
+    if (st || !e.q) return st;
+    DeviceInfo di;
+    if ((st = device_info(&di))) return st;
+    return sf_pad_zero(e.sf, M, N, s, di);  // the output's scale padding rows
 }
 
 int nvfp4_gemm_persistent(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,

@@ -230,7 +230,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_acc_empty);  // accumulator may be overwritten now
 
-            store_row<kCols, F16>(acc, p, tm * kBlockM + quarter * 32 + lane, tn * BN + half * kCols);
+            if (p.epi.plain())
+                store_row<kCols, F16>(acc, p, tm * kBlockM + quarter * 32 + lane, tn * BN + half * kCols);
+            else
+                store_row_epi<kCols>(acc, p, tm * kBlockM + quarter * 32 + lane, tn * BN + half * kCols);
         }
     }
 
@@ -294,7 +297,7 @@ int operand_map(const void *ptr, int64_t rows, int64_t K, int box_rows, int box_
 
 template <int BN, int STAGES, bool F16>
 static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
-                  int M, int N, int K, cudaStream_t stream, const DeviceInfo &di) {
+                  int M, int N, int K, cudaStream_t stream, const DeviceInfo &di, const Epi &epi) {
     using L = Layout<BN, STAGES>;
     auto kern = nvfp4_gemm_kernel<BN, STAGES, F16>;
     static int configured[64] = {};
@@ -322,6 +325,7 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     p.k_groups = K / 64;
     p.vec32_store = ((reinterpret_cast<uintptr_t>(D) & 31u) == 0) && (N % 16 == 0);
     p.trace = nullptr;
+    p.epi = epi;
     if ((st = kernel_ctl(&p.ctl))) return st;
     const int grid = p.num_tiles < di.sm_count ? p.num_tiles : di.sm_count;
     kern<<<grid, kThreads, L::kDynamicSmem, stream>>>(ta, tb, p);
@@ -340,7 +344,7 @@ int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
 }
 
 int pair_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
-                  int M, int N, int K, cudaStream_t stream, bool f16, const DeviceInfo &di);
+                  int M, int N, int K, cudaStream_t stream, bool f16, const DeviceInfo &di, const Epi &epi);
 
 // Kernel choice for the persistent path: the CTA-pair kernel for M > 128, the
 // single-CTA kernel otherwise.  NVFP4_GEMM_VARIANT=single|pair forces one.
@@ -356,15 +360,22 @@ static int gemm_variant(int M) {
     return M > 128 ? 2 : 1;
 }
 
-int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
-                  int M, int N, int K, cudaStream_t stream, bool f16) {
-    int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
+// Persistent GEMM (single-CTA or CTA-pair kernel) with an optional fused epilogue;
+// with NVFP4 output (epi.q) D is not written and may be null.
+int gemm_dispatch_epi(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
+                      int M, int N, int K, cudaStream_t stream, bool f16, const Epi &epi) {
+    int st = gemm_validate(A, SFA, B, SFB, epi.q ? epi.q : D, M, N, K);
     if (st) return st;
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
-    if (gemm_variant(M) == 2) return pair_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, stream, f16, di);
-    if (f16) return gemm::launch<256, 4, true>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di);
-    return gemm::launch<256, 4, false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di);
+    if (gemm_variant(M) == 2) return pair_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, stream, f16, di, epi);
+    if (f16) return gemm::launch<256, 4, true>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, epi);
+    return gemm::launch<256, 4, false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, epi);
+}
+
+int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
+                  int M, int N, int K, cudaStream_t stream, bool f16) {
+    return gemm_dispatch_epi(A, SFA, B, SFB, alpha, D, M, N, K, stream, f16, Epi());
 }
 
 }  // namespace nvfp4

@@ -5,6 +5,7 @@
 #include <cuda_fp16.h>
 
 #include "common.cuh"
+#include "epilogue.cuh"
 #include "ptx.cuh"
 
 namespace nvfp4 {
@@ -35,6 +36,7 @@ struct Params {
     // [11] at the last accumulator commit
     unsigned long long *trace;
     int group_m;  // pair kernel: 256-row tile rows per raster group
+    Epi epi;      // fused epilogue (plain: alpha and bf16/fp16 rounding only)
 };
 constexpr int kTraceSlots = 12;
 
@@ -75,6 +77,64 @@ __device__ __forceinline__ void store_row(const uint32_t (&acc)[kCols], const Pa
                 v.z = pack2(__uint_as_float(acc[c * 8 + 4]) * p.alpha, __uint_as_float(acc[c * 8 + 5]) * p.alpha, F16);
                 v.w = pack2(__uint_as_float(acc[c * 8 + 6]) * p.alpha, __uint_as_float(acc[c * 8 + 7]) * p.alpha, F16);
                 *reinterpret_cast<uint4 *>(drow + c * 16) = v;
+            }
+        }
+    }
+}
+
+// The fused-epilogue form of store_row (bf16 or NVFP4 output, see epilogue.cuh).
+// NVFP4 output needs col0 and N to be multiples of 64: each 64-column k-group of
+// the row is then whole, its 32 bytes of codes leave as two 16-byte stores and its
+// 4 scale bytes as one 32-bit store.  Rows >= M are skipped (the caller zeroes the
+// scale padding rows).
+template <int kCols>
+__device__ __forceinline__ void store_row_epi(const uint32_t (&acc)[kCols], const Params &p, int row, int col0) {
+    if (row >= p.M) return;
+    const Epi &e = p.epi;
+    if (!e.q) {
+        uint8_t *drow = static_cast<uint8_t *>(p.d) + ((int64_t)row * p.N + col0) * 2;
+#pragma unroll
+        for (int c = 0; c < kCols / 8; c++) {
+            if (col0 + c * 8 < p.N) {
+                uint32_t w[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int k = c * 8 + 2 * i;
+                    w[i] = pack2(epi_value(__uint_as_float(acc[k]), p.alpha, e, col0 + k),
+                                 epi_value(__uint_as_float(acc[k + 1]), p.alpha, e, col0 + k + 1), false);
+                }
+                *reinterpret_cast<uint4 *>(drow + c * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
+        return;
+    }
+    if constexpr (kCols % 64 == 0) {
+        const float gs = *e.gs;
+        const bool gs_ok = gs_usable(gs);
+        const int64_t rest = p.N >> 6;
+#pragma unroll
+        for (int g = 0; g < kCols / 64; g++) {
+            const int c0 = col0 + g * 64;
+            if (c0 < p.N) {
+                uint32_t codes[8], scales = 0;
+#pragma unroll
+                for (int b = 0; b < 4; b++) {
+                    float v[16];
+                    float amax = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const int k = g * 64 + b * 16 + i;
+                        v[i] = round_bf16(epi_value(__uint_as_float(acc[k]), p.alpha, e, col0 + k));
+                        amax = fmaxf(amax, fabsf(v[i]));
+                    }
+                    const uint32_t code = block_scale_code(amax, gs, gs_ok);
+                    block_codes(v, block_inverse(code, gs, gs_ok), codes[2 * b], codes[2 * b + 1]);
+                    scales |= code << (8 * b);
+                }
+                uint8_t *qrow = e.q + (int64_t)row * (p.N >> 1) + (c0 >> 1);
+                *reinterpret_cast<uint4 *>(qrow) = make_uint4(codes[0], codes[1], codes[2], codes[3]);
+                *reinterpret_cast<uint4 *>(qrow + 16) = make_uint4(codes[4], codes[5], codes[6], codes[7]);
+                *reinterpret_cast<uint32_t *>(e.sf + sf_group_offset(row, c0 >> 6, rest)) = scales;
             }
         }
     }

@@ -66,6 +66,7 @@ struct Params {
     int64_t total_iters;
     int grid;
     KernelCtl ctl;
+    Epi epi;  // fused epilogue (plain: alpha and bf16 rounding only)
 };
 
 __device__ __forceinline__ int64_t range_begin(int64_t c, const Params &p) { return c * p.total_iters / p.grid; }
@@ -271,13 +272,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (etid == 0) p.counters[tile] = 0;  // reusable by the next call
             }
-            if (n < p.N) {
+            if (p.epi.plain()) {
+                if (n < p.N) {
 #pragma unroll
-                for (int m = 0; m < MPAD; m++)
+                    for (int m = 0; m < MPAD; m++)
+                        if (m < p.M) {
+                            __nv_bfloat16 v = __float2bfloat16_rn(sum[m] * p.alpha);
+                            p.d[(int64_t)m * p.N + n] = *reinterpret_cast<uint16_t *>(&v);
+                        }
+                }
+            } else if (!p.epi.q) {
+                if (n < p.N) {
+#pragma unroll
+                    for (int m = 0; m < MPAD; m++)
+                        if (m < p.M) {
+                            __nv_bfloat16 v = __float2bfloat16_rn(epi_value(sum[m], p.alpha, p.epi, n));
+                            p.d[(int64_t)m * p.N + n] = *reinterpret_cast<uint16_t *>(&v);
+                        }
+                }
+            } else {
+                // NVFP4 output: a 16-element scale block of row m is 16 consecutive n,
+                // i.e. 16 lanes of this warp (N % 64 == 0, so a block is all in or all
+                // out of range).  Every lane takes part in the shuffles.
+                const float gs = *p.epi.gs;
+                const bool gs_ok = gs_usable(gs);
+                const bool valid = n < p.N;
+                const int64_t rest = p.N >> 6;
+#pragma unroll
+                for (int m = 0; m < MPAD; m++) {
                     if (m < p.M) {
-                        __nv_bfloat16 v = __float2bfloat16_rn(sum[m] * p.alpha);
-                        p.d[(int64_t)m * p.N + n] = *reinterpret_cast<uint16_t *>(&v);
+                        const float v = valid ? round_bf16(epi_value(sum[m], p.alpha, p.epi, n)) : 0.0f;
+                        float amax = fabsf(v);
+#pragma unroll
+                        for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                        const uint32_t code = block_scale_code(amax, gs, gs_ok);
+                        const uint32_t q4 = e2m1x2(__fmul_rn(v, block_inverse(code, gs, gs_ok)), 0.0f) & 0xFu;
+                        const uint32_t hi = __shfl_down_sync(0xffffffffu, q4, 1);
+                        if (valid && !(lane & 1)) p.epi.q[(int64_t)m * (p.N >> 1) + (n >> 1)] = (uint8_t)(q4 | (hi << 4));
+                        if (valid && !(lane & 15))
+                            p.epi.sf[sf_group_offset(m, n >> 6, rest) + ((n >> 4) & 3)] = (uint8_t)code;
                     }
+                }
             }
         }
     }
@@ -306,7 +341,8 @@ size_t workspace_bytes(int M, int N, int sm_count) {
 
 template <int MPAD>
 static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
-                  uint16_t *D, int M, int N, int K, void *ws, cudaStream_t stream, const DeviceInfo &di) {
+                  uint16_t *D, int M, int N, int K, void *ws, cudaStream_t stream, const DeviceInfo &di,
+                  const Epi &epi) {
     using L = Layout<MPAD>;
     auto kern = nvfp4_decode_kernel<MPAD>;
     static int configured[64] = {};
@@ -335,6 +371,7 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     const size_t counters = ((size_t)p.n_tiles * sizeof(int) + 255) / 256 * 256;
     p.counters = static_cast<int *>(ws);
     p.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + counters);
+    p.epi = epi;
     if ((st = kernel_ctl(&p.ctl))) return st;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -362,9 +399,12 @@ size_t decode_workspace_bytes(int M, int N) {
     return decode::workspace_bytes(M, N, di.sm_count);
 }
 
+// Decode GEMM with an optional fused epilogue; with NVFP4 output (epi.q) D is not
+// written and may be null.
 int decode_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
-                    uint16_t *D, int M, int N, int K, void *ws, size_t ws_bytes, cudaStream_t stream) {
-    int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
+                    uint16_t *D, int M, int N, int K, void *ws, size_t ws_bytes, cudaStream_t stream,
+                    const Epi &epi) {
+    int st = gemm_validate(A, SFA, B, SFB, epi.q ? static_cast<const void *>(epi.q) : D, M, N, K);
     if (st) return st;
     if (M > 128) return NVFP4_ERR_SHAPE;
     DeviceInfo di;
@@ -373,11 +413,11 @@ int decode_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, cons
         (reinterpret_cast<uintptr_t>(ws) & 255u))
         return NVFP4_ERR_WORKSPACE;
     switch (decode::mpad_for(M)) {
-        case 8: return decode::launch<8>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
-        case 16: return decode::launch<16>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
-        case 32: return decode::launch<32>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
-        case 64: return decode::launch<64>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
-        default: return decode::launch<128>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
+        case 8: return decode::launch<8>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi);
+        case 16: return decode::launch<16>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi);
+        case 32: return decode::launch<32>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi);
+        case 64: return decode::launch<64>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi);
+        default: return decode::launch<128>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi);
     }
 }
 
@@ -429,11 +469,11 @@ int decode_noalloc_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t 
     const size_t counters = ((size_t)((N + decode::kTileN - 1) / decode::kTileN) * sizeof(int) + 255) / 256 * 256;
     if ((st = cuda_status(cudaMemsetAsync(ws, 0, counters, stream)))) return st;
     switch (decode::mpad_for(M)) {
-        case 8: return decode::launch<8>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
-        case 16: return decode::launch<16>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
-        case 32: return decode::launch<32>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
-        case 64: return decode::launch<64>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
-        default: return decode::launch<128>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di);
+        case 8: return decode::launch<8>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, Epi());
+        case 16: return decode::launch<16>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, Epi());
+        case 32: return decode::launch<32>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, Epi());
+        case 64: return decode::launch<64>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, Epi());
+        default: return decode::launch<128>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, Epi());
     }
 }
 

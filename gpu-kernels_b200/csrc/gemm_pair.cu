@@ -369,7 +369,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(lead_acc_empty + 8 * buf);
-            store_row<kCols, F16>(acc, p, tm * 256 + (int)rank * 128 + quarter * 32 + lane, tn * BN + half * kCols);
+            const int row = tm * 256 + (int)rank * 128 + quarter * 32 + lane, col0 = tn * BN + half * kCols;
+            if (p.epi.plain())
+                store_row<kCols, F16>(acc, p, row, col0);
+            else
+                store_row_epi<kCols>(acc, p, row, col0);
             if (TRACE && warp == 2 && lane == 0) t_store += clock64() - c_ready;
         }
         if (TRACE && warp == 2 && lane == 0) {
@@ -402,7 +406,8 @@ static int pair_group_m() {
 template <int STAGES, int BKB, int BN, bool F16>
 static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                        void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di,
-                       unsigned long long *trace) {
+                       unsigned long long *trace, const Epi &epi) {
+    if (epi.q && BN % 128 != 0) return NVFP4_ERR_UNSUPPORTED;  // NVFP4 output wants 64-column aligned halves
     using L = PairLayout<STAGES, BKB, BN>;
     auto kern = trace ? nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, true>
                       : nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, false>;
@@ -439,6 +444,7 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     p.vec32_store = ((reinterpret_cast<uintptr_t>(D) & 31u) == 0) && (N % 16 == 0);
     p.trace = trace;
     p.group_m = pair_group_m();
+    p.epi = epi;
     if ((st = kernel_ctl(&p.ctl))) return st;
     const int pairs = std::min(p.num_tiles, di.sm_count / 2);
     kern<<<2 * pairs, kPairThreads, L::kDynamicSmem, stream>>>(ta, tb, tsa, tsb, p);
@@ -478,12 +484,13 @@ static int pair_cfg() {
 template <bool F16>
 static int launch_pair_cfg(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                            void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di,
-                           unsigned long long *trace) {
+                           unsigned long long *trace, const Epi &epi) {
     switch (pair_cfg()) {
-        case kCfg11x64: return launch_pair<11, 64, 256, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
+        case kCfg11x64:
+            return launch_pair<11, 64, 256, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace, epi);
         case kCfg6x128n192:
-            return launch_pair<6, 128, 192, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
-        default: return launch_pair<5, 128, 256, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
+            return launch_pair<6, 128, 192, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace, epi);
+        default: return launch_pair<5, 128, 256, F16>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace, epi);
     }
 }
 
@@ -493,9 +500,9 @@ int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
                   int N, int K);
 
 int pair_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
-                  int M, int N, int K, cudaStream_t stream, bool f16, const DeviceInfo &di) {
-    if (f16) return gemm::launch_pair_cfg<true>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, nullptr);
-    return gemm::launch_pair_cfg<false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, nullptr);
+                  int M, int N, int K, cudaStream_t stream, bool f16, const DeviceInfo &di, const Epi &epi) {
+    if (f16) return gemm::launch_pair_cfg<true>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, nullptr, epi);
+    return gemm::launch_pair_cfg<false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, nullptr, epi);
 }
 
 // Pair kernel with the per-CTA cycle trace on (trace: 148 x kTraceSlots u64 on the device).
@@ -506,7 +513,7 @@ int gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uin
     if (!trace) return NVFP4_ERR_INVALID;
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
-    return gemm::launch_pair_cfg<false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace);
+    return gemm::launch_pair_cfg<false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace, Epi());
 }
 
 }  // namespace nvfp4

@@ -1,0 +1,62 @@
+// quant_common.cuh — the NVFP4 block-quantization arithmetic, shared by the
+// standalone quantizer (quantize.cu) and the GEMM epilogues that write NVFP4
+// output, so both give the same bytes for the same bf16 values.
+//
+// Specification (the CPU oracle's nvfp4o_quantize, each fp32 step one IEEE
+// round-to-nearest operation):
+//   sf  = e4m3_rn_sat((amax / 6) / gs)          amax over the 16-element block
+//   inv = 1 / (float(sf) * gs), 0 if that product is 0
+//   q   = e2m1_rn_sat(x * inv)
+// A gs outside [2^-100, FLT_MAX] is unusable: every block gets sf = 0, inv = 0.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp4.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+
+namespace nvfp4 {
+
+__device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
+    return static_cast<uint32_t>(__nv_cvt_float2_to_fp4x2(make_float2(lo, hi), __NV_E2M1, cudaRoundNearest));
+}
+
+__device__ __forceinline__ float e4m3_to_float(uint8_t code) {
+    __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(code), __NV_E4M3);
+    return __half2float(__half(h));
+}
+
+__device__ __forceinline__ bool gs_usable(float gs) { return gs >= 0x1p-100f && gs <= 0x1.fffffep127f; }
+
+// e4m3 scale code of a block whose absolute maximum is amax.
+__device__ __forceinline__ uint32_t block_scale_code(float amax, float gs, bool gs_ok) {
+    if (!gs_ok) return 0;
+    const float sfv = __fdiv_rn(__fdiv_rn(amax, 6.0f), gs);
+    return static_cast<uint32_t>(__nv_cvt_float_to_fp8(sfv, __NV_SATFINITE, __NV_E4M3));
+}
+
+// 1 / (float(sf) * gs) for scale code `code` (0 when the product is 0 or gs unusable).
+__device__ __forceinline__ float block_inverse(uint32_t code, float gs, bool gs_ok) {
+    const float denom = __fmul_rn(e4m3_to_float((uint8_t)code), gs);
+    return (!gs_ok || denom == 0.0f) ? 0.0f : __fdiv_rn(1.0f, denom);
+}
+
+// Codes of 16 values given the block's reciprocal: element 2i in the low nibble;
+// bytes 0-3 in lo, 4-7 in hi.
+__device__ __forceinline__ void block_codes(const float (&v)[16], float inv, uint32_t &lo, uint32_t &hi) {
+    lo = 0;
+    hi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        lo |= e2m1x2(__fmul_rn(v[2 * i], inv), __fmul_rn(v[2 * i + 1], inv)) << (8 * i);
+        hi |= e2m1x2(__fmul_rn(v[8 + 2 * i], inv), __fmul_rn(v[8 + 2 * i + 1], inv)) << (8 * i);
+    }
+}
+
+// Byte offset of the scale of (row r, 64-element k-group kg) in the blocked layout
+// of a [pad128(rows), K/16] scale tensor with rest_k = K / 64; the k-group's four
+// scales are the four bytes from there.
+__device__ __forceinline__ int64_t sf_group_offset(int64_t r, int64_t kg, int64_t rest_k) {
+    return ((r >> 7) * rest_k + kg) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4;
+}
+
+}  // namespace nvfp4

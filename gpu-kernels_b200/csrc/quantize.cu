@@ -13,22 +13,10 @@
 // reads 1 KB contiguous and writes 256 contiguous bytes of codes per step.  The
 // kernel is instruction-bound before it is HBM-bound (IEEE divisions), so the
 // per-block reciprocal comes from a 256-entry table.
-#include <cuda_bf16.h>
-#include <cuda_fp4.h>
-#include <cuda_fp8.h>
-
 #include "common.cuh"
+#include "quant_common.cuh"
 
 namespace nvfp4 {
-
-__device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
-    return static_cast<uint32_t>(__nv_cvt_float2_to_fp4x2(make_float2(lo, hi), __NV_E2M1, cudaRoundNearest));
-}
-
-__device__ __forceinline__ float e4m3_to_float(uint8_t code) {
-    __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(code), __NV_E4M3);
-    return __half2float(__half(h));
-}
 
 __device__ __forceinline__ uint4 ld_stream_u4(const void *p) {
     uint4 v;
@@ -57,14 +45,8 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16 *__re
                                                        int64_t n_blocks, int64_t K) {
     __shared__ float inv_table[256];
     const float gs = *gs_ptr;
-    // Same usability rule as the CPU specification: outside [2^-100, FLT_MAX]
-    // every block quantizes to sf = 0, q = e2m1(x * 0).
-    const bool gs_ok = gs >= 0x1p-100f && gs <= 0x1.fffffep127f;
-    {
-        const int c = threadIdx.x;  // blockDim.x == 256
-        const float denom = __fmul_rn(e4m3_to_float((uint8_t)c), gs);
-        inv_table[c] = (!gs_ok || denom == 0.0f) ? 0.0f : __fdiv_rn(1.0f, denom);
-    }
+    const bool gs_ok = gs_usable(gs);
+    inv_table[threadIdx.x] = block_inverse(threadIdx.x, gs, gs_ok);  // blockDim.x == 256
     __syncthreads();
     const int lane = threadIdx.x & 31;
     const int64_t rest_k = K >> 6;
@@ -96,18 +78,9 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16 *__re
             float amax = 0.0f;
 #pragma unroll
             for (int i = 0; i < 16; i++) amax = fmaxf(amax, fabsf(v[i]));
-            uint32_t code = 0;
-            if (gs_ok) {
-                const float sfv = __fdiv_rn(__fdiv_rn(amax, 6.0f), gs);
-                code = static_cast<uint32_t>(__nv_cvt_float_to_fp8(sfv, __NV_SATFINITE, __NV_E4M3));
-            }
-            const float inv = inv_table[code];
-            uint32_t lo = 0, hi = 0;
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                lo |= e2m1x2(__fmul_rn(v[2 * i], inv), __fmul_rn(v[2 * i + 1], inv)) << (8 * i);
-                hi |= e2m1x2(__fmul_rn(v[8 + 2 * i], inv), __fmul_rn(v[8 + 2 * i + 1], inv)) << (8 * i);
-            }
+            const uint32_t code = block_scale_code(amax, gs, gs_ok);
+            uint32_t lo, hi;
+            block_codes(v, inv_table[code], lo, hi);
             // gather the 4 scale codes of this lane's k-group into its first lane
             const uint32_t c1 = __shfl_down_sync(0xffffffffu, code, 1);
             const uint32_t c2 = __shfl_down_sync(0xffffffffu, code, 2);
@@ -117,8 +90,8 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16 *__re
                 if ((lane & 3) == 0) {
                     const int64_t e = gi * 16;  // first element of the k-group
                     const int64_t r = e / K, kg = (e - r * K) >> 6;
-                    const int64_t off = ((r >> 7) * rest_k + kg) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4;
-                    *reinterpret_cast<uint32_t *>(SF + off) = code | (c1 << 8) | (c2 << 16) | (c3 << 24);
+                    *reinterpret_cast<uint32_t *>(SF + sf_group_offset(r, kg, rest_k)) =
+                        code | (c1 << 8) | (c2 << 16) | (c3 << 24);
                 }
             }
         }
@@ -171,6 +144,15 @@ __global__ void global_scale_kernel(const uint32_t *amax_bits, float *amax_out, 
     if (gs_out) *gs_out = __fdiv_rn(a, 2688.0f);  // amax / (6 * 448)
 }
 
+// Zero the scale bytes of rows [M, pad128(M)) of a blocked [pad128(M), K/16] tensor.
+int sf_pad_zero(uint8_t *SF, int M, int K, cudaStream_t s, const DeviceInfo &di) {
+    if (M % 128 == 0) return NVFP4_OK;
+    sf_pad_zero_kernel<<<(unsigned)std::min<int64_t>(di.sm_count, (128 * (int64_t)K / 16 + 255) / 256), 256, 0, s>>>(
+        SF, M, K);
+    count_launch();
+    return cuda_status(cudaGetLastError());
+}
+
 }  // namespace nvfp4
 
 using namespace nvfp4;
@@ -194,12 +176,8 @@ extern "C" int nvfp4_quantize(const uint16_t *X, uint8_t *Q, uint8_t *SF, const 
     quantize_kernel<<<(unsigned)blocks, threads, 0, s>>>(reinterpret_cast<const __nv_bfloat16 *>(X), Q, SF,
                                                          global_scale, n_blocks, K);
     count_launch();
-    if (M % 128) {
-        sf_pad_zero_kernel<<<(unsigned)std::min<int64_t>(di.sm_count, (128 * (int64_t)K / 16 + 255) / 256), 256, 0,
-                             s>>>(SF, M, K);
-        count_launch();
-    }
-    return cuda_status(cudaGetLastError());
+    if ((st = cuda_status(cudaGetLastError()))) return st;
+    return sf_pad_zero(SF, M, K, s, di);
 }
 
 extern "C" int nvfp4_global_scale(const uint16_t *X, int64_t n, float *amax_out, float *gs_out, void *stream) {

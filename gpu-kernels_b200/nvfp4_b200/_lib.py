@@ -12,6 +12,16 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libnvfp4_b2
 
 # Every exported symbol, with (restype, argtypes).  Keep in step with the header.
 _u8p, _u16p, _f32p, _vp = C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p
+
+
+class Epilogue(C.Structure):
+    """struct nvfp4_epilogue of the header."""
+    _fields_ = [("bias", C.c_void_p), ("activation", C.c_int), ("q_out", C.c_void_p), ("sf_out", C.c_void_p),
+                ("out_global_scale", C.c_void_p)]
+
+
+ACTIVATIONS = {"none": 0, "relu": 1, "silu": 2, "gelu_tanh": 3}
+
 SIGNATURES = {
     "nvfp4_status_string": (C.c_char_p, [C.c_int]),
     "nvfp4_version": (C.c_int, []),
@@ -20,6 +30,8 @@ SIGNATURES = {
     "nvfp4_gemm": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp]),
     "nvfp4_gemm_f16": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp]),
     "nvfp4_gemm_persistent": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp]),
+    "nvfp4_gemm_epilogue": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int,
+                                      C.POINTER(Epilogue), _vp]),
     "nvfp4_gemm_decode_workspace_size": (C.c_size_t, [C.c_int, C.c_int]),
     "nvfp4_gemm_decode": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp,
                                     C.c_size_t, _vp]),

@@ -6,11 +6,12 @@ float8_e4m3fn (scales) tensors: only the bytes matter.  All calls are
 asynchronous on torch's current CUDA stream and raise NVFP4Error on a bad
 status.  Nothing here computes on the CPU.
 """
+import ctypes as C
 from typing import Optional, Tuple, Union
 
 import torch
 
-from ._lib import NVFP4Error, check, lib
+from ._lib import ACTIVATIONS, Epilogue, NVFP4Error, check, lib
 from .layout import sf_bytes, to_blocked
 
 
@@ -84,6 +85,48 @@ def gemm(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor,
     return d
 
 
+def gemm_epilogue(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, alpha: float = 1.0,
+                  bias: Optional[torch.Tensor] = None, activation: str = "none",
+                  out_global_scale: Union[torch.Tensor, float, None] = None, out: Optional[torch.Tensor] = None,
+                  q_out: Optional[torch.Tensor] = None, sf_out: Optional[torch.Tensor] = None):
+    """D = act(alpha * A . B^T + bias) in one kernel (nvfp4_gemm_epilogue).
+
+    Without `out_global_scale`: returns bf16 D [M, N].  With it: D is quantized to
+    NVFP4 in the epilogue (N % 64 == 0) and (codes uint8 [M, N/2], blocked scales
+    uint8 [pad128(M) * N/16]) are returned — the bytes nvfp4_quantize would give
+    for the bf16 result."""
+    for t, n in ((a, "a"), (sfa, "sfa"), (b, "b"), (sfb, "sfb")):
+        _bytes_tensor(t, n)
+    M, K, N = a.shape[0], a.shape[1] * 2, b.shape[0]
+    if b.shape[1] * 2 != K:
+        raise ValueError("A and B must have the same K")
+    if sfa.numel() < sf_bytes(M, K) or sfb.numel() < sf_bytes(N, K):
+        raise ValueError("scale tensors too small for the blocked layout (rows padded to 128)")
+    if activation not in ACTIVATIONS:
+        raise ValueError(f"activation must be one of {sorted(ACTIVATIONS)}")
+    e = Epilogue()
+    e.activation = ACTIVATIONS[activation]
+    if bias is not None:
+        if bias.dtype != torch.bfloat16 or bias.numel() != N or not bias.is_cuda or not bias.is_contiguous():
+            raise ValueError("bias must be a contiguous bf16 CUDA tensor of N elements")
+        e.bias = bias.data_ptr()
+    d = None
+    if out_global_scale is None:
+        d = out if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
+        if d.dtype != torch.bfloat16 or d.shape != (M, N) or not d.is_contiguous():
+            raise ValueError("out must be a contiguous bf16 [M, N] tensor")
+        d_ptr = d.data_ptr()
+    else:
+        gs = _scale_tensor(out_global_scale, a.device)
+        q = q_out if q_out is not None else torch.empty(M, N // 2, dtype=torch.uint8, device=a.device)
+        sf = sf_out if sf_out is not None else torch.empty(sf_bytes(M, N), dtype=torch.uint8, device=a.device)
+        e.q_out, e.sf_out, e.out_global_scale = q.data_ptr(), sf.data_ptr(), gs.data_ptr()
+        d_ptr = None
+    check(lib().nvfp4_gemm_epilogue(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), float(alpha), d_ptr,
+                                    M, N, K, C.byref(e), _stream(a.device)), "nvfp4_gemm_epilogue")
+    return d if d is not None else (q, sf)
+
+
 def gemm_host(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, alpha: float,
               out: torch.Tensor, device: Optional[torch.device] = None) -> torch.Tensor:
     """D = alpha * A . B^T from and to HOST tensors (pin them for overlap): uploads,
@@ -141,5 +184,5 @@ def launch_count() -> int:
     return int(lib().nvfp4_launch_count())
 
 
-__all__ = ["NVFP4Error", "global_scale", "quantize", "gemm", "gemm_host", "matmul_nvfp4", "create_tensors",
-           "device_status", "set_wait_timeout_ns", "selftest_wait_timeout", "launch_count"]
+__all__ = ["NVFP4Error", "global_scale", "quantize", "gemm", "gemm_epilogue", "gemm_host", "matmul_nvfp4",
+           "create_tensors", "device_status", "set_wait_timeout_ns", "selftest_wait_timeout", "launch_count"]

@@ -125,6 +125,40 @@ NVFP4_API int nvfp4_gemm_f16(const uint8_t *A, const uint8_t *SFA, const uint8_t
                    float alpha, uint16_t *D, int M, int N, int K, void *stream);
 
 /*
+ * Fused epilogue (no counterpart in the reference, whose kernels only convert the
+ * fp32 accumulator to fp16).  Per element of D, in fp32 with one IEEE rounding per
+ * operation:
+ *   y = alpha * acc;  y += bias[n] (bf16, optional);  y = act(y)
+ * with act one of
+ *   NVFP4_ACT_NONE, NVFP4_ACT_RELU (max(y, 0)), NVFP4_ACT_SILU (y / (1 + exp(-y))),
+ *   NVFP4_ACT_GELU_TANH (0.5 y (1 + tanh(sqrt(2/pi) (y + 0.044715 y^3)))).
+ * Output: bf16(y) into D, or — when q_out is given — the bf16(y) rows quantized to
+ * NVFP4 for the next layer: codes [M, N/2] into q_out and blocked e4m3 scales
+ * [pad128(M), N/16] into sf_out with the fp32 global scale *out_global_scale
+ * (device), byte-identical to nvfp4_quantize applied to the bf16 output.  NVFP4
+ * output needs N % 64 == 0; D is then not written and may be NULL.
+ */
+enum {
+    NVFP4_ACT_NONE = 0,
+    NVFP4_ACT_RELU = 1,
+    NVFP4_ACT_SILU = 2,
+    NVFP4_ACT_GELU_TANH = 3
+};
+typedef struct nvfp4_epilogue {
+    const uint16_t *bias;          /* bf16 [N] (2-byte aligned), or NULL */
+    int activation;                /* NVFP4_ACT_* */
+    uint8_t *q_out;                /* NVFP4 output codes [M, N/2] (16-byte aligned), or NULL for bf16 D */
+    uint8_t *sf_out;               /* its blocked scales [pad128(M) * N/16] (4-byte aligned) */
+    const float *out_global_scale; /* device fp32 global scale of the output */
+} nvfp4_epilogue;
+
+/* nvfp4_gemm with the fused epilogue `epi` (NULL = plain nvfp4_gemm).  Same kernel
+ * choice (split-K decode kernel for M <= 128, CTA-pair kernel above). */
+NVFP4_API int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+                                  float alpha, uint16_t *D, int M, int N, int K, const nvfp4_epilogue *epi,
+                                  void *stream);
+
+/*
  * Reference-signature shim: drop-in for matmul_nvfp4_vN in
  * matmul/sm100_nvfp4/runner.cu:61-96 (fp16 D, alpha = 1, legacy default
  * stream, no return value).  The status of the last call is kept for

@@ -355,6 +355,37 @@ void nvfp4o_gemm_rows(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, co
 }
 
 /* ---------------------------------------------------------------------------
+ * Fused GEMM epilogue (the product's nvfp4_gemm_epilogue; the reference has no
+ * epilogue beyond fp16 conversion).  Per element, each fp32 step one IEEE
+ * round-to-nearest operation (this file is built with -ffp-contract=off):
+ *   y = alpha * acc;  y = y + bias[n];  y = act(y);  out = bf16_rn(y)
+ * act: 0 none, 1 relu max(y, 0), 2 silu y / (1 + exp(-y)),
+ *      3 gelu (tanh form) 0.5 y (1 + tanh(0.7978845608028654 (y + 0.044715 y^3))).
+ * exp/tanh are the C library's, so silu/gelu agree with the GPU to a few ulp of
+ * fp32, not bit for bit.
+ * ------------------------------------------------------------------------- */
+void nvfp4o_epilogue(const float *acc, const uint16_t *bias, int act, float alpha, int64_t rows, int64_t N,
+                     float *Y32, uint16_t *Y16, int nthreads) {
+    const int64_t total = rows * N;
+#pragma omp parallel for schedule(static) num_threads(pick_threads(nthreads))
+    for (int64_t i = 0; i < total; i++) {
+        float y = alpha * acc[i];
+        if (bias) y = y + nvfp4o_bf16_to_f32(bias[i % N]);
+        if (act == 1) {
+            y = fmaxf(y, 0.0f);
+        } else if (act == 2) {
+            y = y / (1.0f + expf(-y));
+        } else if (act == 3) {
+            const float y3 = (y * y) * y;
+            const float u = 0.7978845608028654f * (y + 0.044715f * y3);
+            y = (0.5f * y) * (1.0f + tanhf(u));
+        }
+        if (Y32) Y32[i] = y;
+        if (Y16) Y16[i] = nvfp4o_f32_to_bf16(y);
+    }
+}
+
+/* ---------------------------------------------------------------------------
  * Deterministic inputs: splitmix64 counter stream + Box-Muller in double.
  * ------------------------------------------------------------------------- */
 static inline uint64_t splitmix64(uint64_t x) {

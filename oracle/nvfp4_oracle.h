@@ -72,6 +72,12 @@ void    nvfp4o_dequant_rows(const uint8_t *Q, const uint8_t *SF, float *out, int
 void    nvfp4o_sgemm_nt(const float *A, const float *B, float alpha, int64_t mrows, int64_t ncols,
                         int64_t K, float *D32, uint16_t *D16, int nthreads);
 
+/* ---- fused epilogue -------------------------------------------------------- */
+/* Y = act(alpha * acc + bias[n]) over rows x N (bias bf16 [N] or NULL; act 0 none,
+ * 1 relu, 2 silu, 3 gelu-tanh), fp32 and/or bf16 out. */
+void    nvfp4o_epilogue(const float *acc, const uint16_t *bias, int act, float alpha, int64_t rows,
+                        int64_t N, float *Y32, uint16_t *Y16, int nthreads);
+
 /* ---- deterministic synthetic inputs -------------------------------------- */
 /* Counter-based (splitmix64) so that any slice can be generated alone. */
 void    nvfp4o_fill_normal_bf16(uint16_t *X, int64_t n, uint64_t seed, float stddev,
