@@ -14,6 +14,8 @@ namespace nvfp4 {
 int gemm_dispatch_epi(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                       int M, int N, int K, cudaStream_t stream, bool f16, const Epi &epi);
 int sf_pad_zero(uint8_t *SF, int M, int K, cudaStream_t s, const DeviceInfo &di);
+int grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const float *alphas,
+                     uint16_t *D, const int *m_offsets, int groups, int m_total, int N, int K, cudaStream_t stream);
 int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                   int M, int N, int K, cudaStream_t stream, bool f16);
 size_t decode_workspace_bytes(int M, int N);
@@ -124,6 +126,12 @@ int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, 
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
     return sf_pad_zero(e.sf, M, N, s, di);  // the output's scale padding rows
+}
+
+int nvfp4_gemm_grouped(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const float *alpha,
+                       uint16_t *D, const int32_t *m_offsets, int groups, int m_total, int N, int K, void *stream) {
+    return grouped_dispatch(A, SFA, B, SFB, alpha, D, m_offsets, groups, m_total, N, K,
+                            static_cast<cudaStream_t>(stream));
 }
 
 int nvfp4_gemm_persistent(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,

@@ -231,9 +231,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive(bar_acc_empty);  // accumulator may be overwritten now
 
             if (p.epi.plain())
-                store_row<kCols, F16>(acc, p, tm * kBlockM + quarter * 32 + lane, tn * BN + half * kCols);
+                store_row<kCols, F16>(acc, p, tm * kBlockM + quarter * 32 + lane, tn * BN + half * kCols, p.M,
+                                      p.alpha);
             else
-                store_row_epi<kCols>(acc, p, tm * kBlockM + quarter * 32 + lane, tn * BN + half * kCols);
+                store_row_epi<kCols>(acc, p, tm * kBlockM + quarter * 32 + lane, tn * BN + half * kCols, p.M,
+                                     p.alpha);
         }
     }
 

@@ -16,6 +16,17 @@ constexpr int kBlockKBytes = 128;               // one 128-byte swizzle row = 25
 constexpr int kKGroups = 4;                     // 64-element MMA k-steps per 128-byte stage
 constexpr int kEpiWarps = 8;
 constexpr int kGroupM = 16;                     // m-tiles per raster group (single-CTA kernel)
+constexpr int kMaxGroups = 256;                 // experts of a grouped (MoE) GEMM
+
+// Grouped GEMM (pair kernel): group g covers rows [m_offsets[g], m_offsets[g+1]) of
+// A and D and uses weight rows [g*N, (g+1)*N) of B; its A scales start at 128-row
+// block sum_{h<g} ceil(M_h / 128) of SFA.  Device arrays.
+struct Grouped {
+    const int *m_offsets = nullptr;  // [groups + 1]
+    const float *alphas = nullptr;   // [groups]
+    int groups = 0;                  // 0: not grouped
+    int m_total = 0;                 // rows of A / D (offsets are clamped to it)
+};
 
 struct Params {
     const uint8_t *sfa;
@@ -37,6 +48,7 @@ struct Params {
     unsigned long long *trace;
     int group_m;  // pair kernel: 256-row tile rows per raster group
     Epi epi;      // fused epilogue (plain: alpha and bf16/fp16 rounding only)
+    Grouped grouped;
 };
 constexpr int kTraceSlots = 12;
 
@@ -50,10 +62,11 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool f16) {
 }
 
 // Convert this thread's kCols accumulator columns (one output row) with alpha and
-// store them to D[row, col0 .. col0+kCols), clipped to N.
+// store them to D[row, col0 .. col0+kCols), clipped to N; rows >= row_end are skipped.
 template <int kCols, bool F16>
-__device__ __forceinline__ void store_row(const uint32_t (&acc)[kCols], const Params &p, int row, int col0) {
-    if (row >= p.M) return;
+__device__ __forceinline__ void store_row(const uint32_t (&acc)[kCols], const Params &p, int row, int col0,
+                                          int row_end, float alpha) {
+    if (row >= row_end) return;
     uint8_t *drow = static_cast<uint8_t *>(p.d) + ((int64_t)row * p.N + col0) * 2;
     if (p.vec32_store) {
 #pragma unroll
@@ -62,8 +75,8 @@ __device__ __forceinline__ void store_row(const uint32_t (&acc)[kCols], const Pa
                 uint32_t v[8];
 #pragma unroll
                 for (int i = 0; i < 8; i++)
-                    v[i] = pack2(__uint_as_float(acc[c * 16 + 2 * i]) * p.alpha,
-                                 __uint_as_float(acc[c * 16 + 2 * i + 1]) * p.alpha, F16);
+                    v[i] = pack2(__uint_as_float(acc[c * 16 + 2 * i]) * alpha,
+                                 __uint_as_float(acc[c * 16 + 2 * i + 1]) * alpha, F16);
                 st_global_v8(drow + c * 32, v);
             }
         }
@@ -72,10 +85,10 @@ __device__ __forceinline__ void store_row(const uint32_t (&acc)[kCols], const Pa
         for (int c = 0; c < kCols / 8; c++) {
             if (col0 + c * 8 < p.N) {
                 uint4 v;
-                v.x = pack2(__uint_as_float(acc[c * 8 + 0]) * p.alpha, __uint_as_float(acc[c * 8 + 1]) * p.alpha, F16);
-                v.y = pack2(__uint_as_float(acc[c * 8 + 2]) * p.alpha, __uint_as_float(acc[c * 8 + 3]) * p.alpha, F16);
-                v.z = pack2(__uint_as_float(acc[c * 8 + 4]) * p.alpha, __uint_as_float(acc[c * 8 + 5]) * p.alpha, F16);
-                v.w = pack2(__uint_as_float(acc[c * 8 + 6]) * p.alpha, __uint_as_float(acc[c * 8 + 7]) * p.alpha, F16);
+                v.x = pack2(__uint_as_float(acc[c * 8 + 0]) * alpha, __uint_as_float(acc[c * 8 + 1]) * alpha, F16);
+                v.y = pack2(__uint_as_float(acc[c * 8 + 2]) * alpha, __uint_as_float(acc[c * 8 + 3]) * alpha, F16);
+                v.z = pack2(__uint_as_float(acc[c * 8 + 4]) * alpha, __uint_as_float(acc[c * 8 + 5]) * alpha, F16);
+                v.w = pack2(__uint_as_float(acc[c * 8 + 6]) * alpha, __uint_as_float(acc[c * 8 + 7]) * alpha, F16);
                 *reinterpret_cast<uint4 *>(drow + c * 16) = v;
             }
         }
@@ -85,11 +98,12 @@ __device__ __forceinline__ void store_row(const uint32_t (&acc)[kCols], const Pa
 // The fused-epilogue form of store_row (bf16 or NVFP4 output, see epilogue.cuh).
 // NVFP4 output needs col0 and N to be multiples of 64: each 64-column k-group of
 // the row is then whole, its 32 bytes of codes leave as two 16-byte stores and its
-// 4 scale bytes as one 32-bit store.  Rows >= M are skipped (the caller zeroes the
-// scale padding rows).
+// 4 scale bytes as one 32-bit store.  Rows >= row_end are skipped (the caller zeroes
+// the scale padding rows).
 template <int kCols>
-__device__ __forceinline__ void store_row_epi(const uint32_t (&acc)[kCols], const Params &p, int row, int col0) {
-    if (row >= p.M) return;
+__device__ __forceinline__ void store_row_epi(const uint32_t (&acc)[kCols], const Params &p, int row, int col0,
+                                              int row_end, float alpha) {
+    if (row >= row_end) return;
     const Epi &e = p.epi;
     if (!e.q) {
         uint8_t *drow = static_cast<uint8_t *>(p.d) + ((int64_t)row * p.N + col0) * 2;
@@ -100,8 +114,8 @@ __device__ __forceinline__ void store_row_epi(const uint32_t (&acc)[kCols], cons
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
                     const int k = c * 8 + 2 * i;
-                    w[i] = pack2(epi_value(__uint_as_float(acc[k]), p.alpha, e, col0 + k),
-                                 epi_value(__uint_as_float(acc[k + 1]), p.alpha, e, col0 + k + 1), false);
+                    w[i] = pack2(epi_value(__uint_as_float(acc[k]), alpha, e, col0 + k),
+                                 epi_value(__uint_as_float(acc[k + 1]), alpha, e, col0 + k + 1), false);
                 }
                 *reinterpret_cast<uint4 *>(drow + c * 16) = make_uint4(w[0], w[1], w[2], w[3]);
             }
@@ -124,7 +138,7 @@ __device__ __forceinline__ void store_row_epi(const uint32_t (&acc)[kCols], cons
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
                         const int k = g * 64 + b * 16 + i;
-                        v[i] = round_bf16(epi_value(__uint_as_float(acc[k]), p.alpha, e, col0 + k));
+                        v[i] = round_bf16(epi_value(__uint_as_float(acc[k]), alpha, e, col0 + k));
                         amax = fmaxf(amax, fabsf(v[i]));
                     }
                     const uint32_t code = block_scale_code(amax, gs, gs_ok);

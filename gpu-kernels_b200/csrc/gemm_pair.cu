@@ -28,6 +28,7 @@
 #include <cstring>
 
 #include "gemm_common.cuh"
+#include "grouped.cuh"
 
 namespace nvfp4 {
 namespace gemm {
@@ -49,7 +50,10 @@ struct PairLayout {
     static constexpr int kOffSfb = kOffSfa + STAGES * kSfa;
     static constexpr int kOffBar = kOffSfb + STAGES * kSfb;
     static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 16;  // full, empty, acc_full x2, acc_empty x2, drain
-    static constexpr int kDynamicSmem = kOffBar + kBarBytes + 1024;
+    // grouped GEMM tables: first row, first tile and first A-scale block of each group
+    static constexpr int kOffGroups = kOffBar + kBarBytes;
+    static constexpr int kGroupBytes = 4 * (kMaxGroups + 1) * 4;
+    static constexpr int kDynamicSmem = kOffGroups + kGroupBytes + 1024;
     static constexpr uint32_t kTxBytes = 2u * kStage;    // both CTAs complete on the leader's barrier
     // shared-memory matrix descriptor: 128B or 64B swizzle, 8-row core groups
     static constexpr uint32_t kLayout = BKB == 128 ? 2 : 4;
@@ -72,6 +76,17 @@ struct PairLayout {
 constexpr int kPairThreads = 32 * (3 + kEpiWarps);  // A/B producer, MMA, 8 epilogue, scale producer
 constexpr int kSfProducerWarp = 2 + kEpiWarps;
 
+// Output tile t of the persistent schedule: its coordinates and where its rows live.
+struct TileInfo {
+    int tm, tn;
+    int a_row0;      // first A / D row of the 256-row tile
+    int row_end;     // rows >= row_end are not stored
+    int sfa_block0;  // 128-row A scale block of the tile's first row
+    int b_row0;      // first B row of the tile's weight matrix
+    int sfb_block0;  // its first 128-row scale block
+    float alpha;
+};
+
 template <int STAGES, int BKB, int BN, bool F16, bool TRACE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -90,14 +105,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     const uint32_t bar_drain = bar_acc_empty + 16;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(base_ptr + L::kOffBar + (2 * STAGES + 5) * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    int *g_row0 = reinterpret_cast<int *>(base_ptr + L::kOffGroups);  // [groups] first row
+    int *g_rend = g_row0 + (kMaxGroups + 1);                           // [groups] end row
+    int *g_tile0 = g_rend + (kMaxGroups + 1);                          // [groups + 1] first tile
+    int *g_sfa0 = g_tile0 + (kMaxGroups + 1);                          // [groups + 1] first scale block
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
     if (TRACE && threadIdx.x == 0) p.trace[blockIdx.x * kTraceSlots + 8] = global_timer_ns();
     const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
-    const int n_m = (p.M + 255) / 256, n_n = (p.N + BN - 1) / BN, n_tiles = n_m * n_n;
-
+    const int n_m = (p.M + 255) / 256, n_n = (p.N + BN - 1) / BN;
+    const int G = p.grouped.groups;
+    if (G > 0 && warp == 2)
+        build_group_tables(p.grouped.m_offsets, G, p.grouped.m_total, n_n, lane, g_row0, g_rend, g_sfa0, g_tile0);
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(bar_full + 8 * s, 1);
@@ -125,14 +146,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     const uint32_t tmem_base = *tmem_slot;
     const uint64_t tmo = p.ctl.wait_timeout_ns;
     const uint32_t lead_full = map_to_cta(bar_full, 0);
+    const int n_tiles = G > 0 ? g_tile0[G] : n_m * n_n;
 
     // raster: groups of p.group_m 256-row tile rows sweep N together (L2 reuse of A)
-    auto coords = [&](int t, int &tm, int &tn) {
+    auto coords = [&](int t, int nm, int &tm, int &tn) {
         const int gm_max = p.group_m;
         const int per_group = gm_max * n_n;
-        const int g = t / per_group, first = g * gm_max, gm = min(n_m - first, gm_max), local = t - g * per_group;
+        const int g = t / per_group, first = g * gm_max, gm = min(nm - first, gm_max), local = t - g * per_group;
         tm = first + local % gm;
         tn = local / gm;
+    };
+    auto tile_info = [&](int t) {
+        TileInfo ti;
+        if (G == 0) {
+            coords(t, n_m, ti.tm, ti.tn);
+            ti.a_row0 = ti.tm * 256;
+            ti.row_end = p.M;
+            ti.sfa_block0 = ti.tm * 2;
+            ti.b_row0 = 0;
+            ti.sfb_block0 = 0;
+            ti.alpha = p.alpha;
+        } else {
+            const int g = last_group_at_or_before(g_tile0, G, t);  // g_tile0[g] <= t < g_tile0[g + 1]
+            const int r0 = g_row0[g], r1 = g_rend[g];
+            coords(t - g_tile0[g], (r1 - r0 + 255) / 256, ti.tm, ti.tn);
+            ti.a_row0 = r0 + ti.tm * 256;
+            ti.row_end = r1;
+            ti.sfa_block0 = g_sfa0[g] + ti.tm * 2;
+            ti.b_row0 = g * p.N;
+            ti.sfb_block0 = g * (p.N >> 7);
+            ti.alpha = p.grouped.alphas[g];
+        }
+        return ti;
     };
 
     if (warp == 0 || warp == kSfProducerWarp) {
@@ -148,13 +193,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             uint32_t issued_mask = 0, issued_parity = 0;
             long long t_wait = 0;
             for (int t = pair; ok && t < n_tiles; t += num_pairs) {
-                int tm, tn;
-                coords(t, tm, tn);
-                const int arow = tm * 256 + rank * 128, brow = tn * BN + rank * L::kBRows;
+                const TileInfo ti = tile_info(t);
+                const int arow = ti.a_row0 + rank * 128, brow = ti.b_row0 + ti.tn * BN + rank * L::kBRows;
                 // scale tensors viewed as rows of 256 bytes: one (128-row block, 64-K group) =
                 // 2 rows; the tile's B rows lie in 128-row blocks sb and sb + 1
-                const int sb = (tn * BN) >> 7;
-                const int ysa = (tm * 2 + (int)rank) * rest_k * 2, ysb0 = sb * rest_k * 2,
+                const int sb = ti.sfb_block0 + ((ti.tn * BN) >> 7);
+                const int ysa = (ti.sfa_block0 + (int)rank) * rest_k * 2, ysb0 = sb * rest_k * 2,
                           ysb1 = (sb + 1) * rest_k * 2;
                 for (int kb = 0; kb < p.num_kb; kb++) {
                     const long long c0 = TRACE ? clock64() : 0;
@@ -226,8 +270,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             long long t_full = 0, t_acc = 0, t_first = 0;
             uint64_t ns_first = 0;
             for (int t = pair; ok && t < n_tiles; t += num_pairs, local++) {
-                int tm, tn;
-                coords(t, tm, tn);
+                const int tn = tile_info(t).tn;
                 // accumulator buffer and its use count; B-scale column shift of this tile
                 const uint32_t buf = L::kAccBufs == 2 ? (uint32_t)(local & 1) : 0u;
                 const uint32_t use = L::kAccBufs == 2 ? (uint32_t)(local >> 1) : (uint32_t)local;
@@ -343,8 +386,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         int local = 0;
         long long t_accw = 0, t_store = 0, c_ready = 0;
         for (int t = pair; t < n_tiles; t += num_pairs, local++) {
-            int tm, tn;
-            coords(t, tm, tn);
+            const TileInfo ti = tile_info(t);
             const uint32_t buf = L::kAccBufs == 2 ? (uint32_t)(local & 1) : 0u;
             const uint32_t use = L::kAccBufs == 2 ? (uint32_t)(local >> 1) : (uint32_t)local;
             bool ok = true;
@@ -369,11 +411,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(lead_acc_empty + 8 * buf);
-            const int row = tm * 256 + (int)rank * 128 + quarter * 32 + lane, col0 = tn * BN + half * kCols;
+            const int row = ti.a_row0 + (int)rank * 128 + quarter * 32 + lane, col0 = ti.tn * BN + half * kCols;
             if (p.epi.plain())
-                store_row<kCols, F16>(acc, p, row, col0);
+                store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha);
             else
-                store_row_epi<kCols>(acc, p, row, col0);
+                store_row_epi<kCols>(acc, p, row, col0, ti.row_end, ti.alpha);
             if (TRACE && warp == 2 && lane == 0) t_store += clock64() - c_ready;
         }
         if (TRACE && warp == 2 && lane == 0) {
@@ -403,10 +445,13 @@ static int pair_group_m() {
     return v;
 }
 
+// Grouped launches (grp.groups > 0) take M = grp.m_total; A's scale tensor then
+// holds ceil(m_total / 128) + groups blocks (every group's scales start on a block),
+// B and its scales groups x N rows.
 template <int STAGES, int BKB, int BN, bool F16>
 static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                        void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di,
-                       unsigned long long *trace, const Epi &epi) {
+                       unsigned long long *trace, const Epi &epi, const Grouped &grp = Grouped()) {
     if (epi.q && BN % 128 != 0) return NVFP4_ERR_UNSUPPORTED;  // NVFP4 output wants 64-column aligned halves
     using L = PairLayout<STAGES, BKB, BN>;
     auto kern = trace ? nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, true>
@@ -417,12 +462,16 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
             return NVFP4_ERR_CUDA;
         configured[trace != nullptr][di.device] = 1;
     }
+    const int G = grp.groups;
+    const int64_t b_rows = G > 0 ? (int64_t)G * N : N;
     CUtensorMap ta, tb, tsa, tsb;
     int st = operand_map(A, M, K, 128, BKB, &ta);
-    if (!st) st = operand_map(B, N, K, L::kBRows, BKB, &tb);
+    if (!st) st = operand_map(B, b_rows, K, L::kBRows, BKB, &tb);
     // scale tensors as [bytes/256, 256]: one (128-row block, 64-K group) chunk is two rows
-    const uint64_t sfa_rows = (uint64_t)((M + 127) / 128) * (K / 64) * 2;
-    const uint64_t sfb_rows = (uint64_t)((N + 127) / 128) * (K / 64) * 2;
+    const uint64_t sfa_blocks = (uint64_t)((M + 127) / 128) + (uint64_t)G;
+    const uint64_t sfb_blocks = (uint64_t)((b_rows + 127) / 128);
+    const uint64_t sfa_rows = sfa_blocks * (K / 64) * 2;
+    const uint64_t sfb_rows = sfb_blocks * (K / 64) * 2;
     if (!st) st = encode_tiled_2d(&tsa, CU_TENSOR_MAP_DATA_TYPE_UINT8, SFA, 256, sfa_rows, 256, 256, 2 * L::kKG,
                                   CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!st) st = encode_tiled_2d(&tsb, CU_TENSOR_MAP_DATA_TYPE_UINT8, SFB, 256, sfb_rows, 256, 256, 2 * L::kKG,
@@ -436,7 +485,7 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     p.N = N;
     p.K = K;
     p.alpha = alpha;
-    p.num_m_tiles = (M + 255) / 256;
+    p.num_m_tiles = (M + 255) / 256 + G;  // grouped: an upper bound (group sizes live on the device)
     p.num_n_tiles = (N + BN - 1) / BN;
     p.num_tiles = p.num_m_tiles * p.num_n_tiles;
     p.num_kb = (K + 2 * BKB - 1) / (2 * BKB);
@@ -445,6 +494,7 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     p.trace = trace;
     p.group_m = pair_group_m();
     p.epi = epi;
+    p.grouped = grp;
     if ((st = kernel_ctl(&p.ctl))) return st;
     const int pairs = std::min(p.num_tiles, di.sm_count / 2);
     kern<<<2 * pairs, kPairThreads, L::kDynamicSmem, stream>>>(ta, tb, tsa, tsb, p);
@@ -459,8 +509,11 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
 // Measured at M=N=K=8192: 5x128 spends 268K MMA-thread cycles per CTA pair, 11x64
 // 405K — the single issuing thread's fixed cost per slot (wait, fence, two commits)
 // outweighs the deeper ring.  6x128n192 (trace: 0.4 % waiting for an accumulator)
-// runs 213 us against 5x128's 200 us: the issuing thread needs ~455 cycles per slot
-// whatever the tile width, more than a 192-wide slot's 384 cycles of MMA work.
+// runs 213 us against 5x128's 200 us: the MMA thread spends ~455 cycles per slot
+// whatever the tile width, more than a 192-wide slot's 384 cycles of MMA work.  Not
+// instruction issue (probe: a scale copy issues in 8 cycles, commits are free);
+// the shared-memory traffic per slot (MMA operand reads plus TMA fills, per FLOP
+// higher for 192-wide tiles) is the likely limit.
 // Writing the scales into TMEM from other warps (tcgen05.st) instead of tcgen05.cp
 // was measured 2.4-3x slower: those stores complete only behind the MMAs already
 // queued, so the scale path serialises with the tensor pipe.
@@ -503,6 +556,27 @@ int pair_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
                   int M, int N, int K, cudaStream_t stream, bool f16, const DeviceInfo &di, const Epi &epi) {
     if (f16) return gemm::launch_pair_cfg<true>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, nullptr, epi);
     return gemm::launch_pair_cfg<false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, nullptr, epi);
+}
+
+// Grouped (mixture-of-experts) GEMM on the CTA-pair kernel, bf16 output.
+int grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const float *alphas,
+                     uint16_t *D, const int *m_offsets, int groups, int m_total, int N, int K, cudaStream_t stream) {
+    if (!A || !SFA || !B || !SFB || !alphas || !D || !m_offsets) return NVFP4_ERR_INVALID;
+    if (groups < 1 || groups > gemm::kMaxGroups || m_total < 1 || N < 128 || N % 128 || K < 64 || K % 64)
+        return NVFP4_ERR_SHAPE;
+    if (!aligned16(A) || !aligned16(SFA) || !aligned16(B) || !aligned16(SFB) || !aligned16(D) ||
+        (reinterpret_cast<uintptr_t>(alphas) & 3u) || (reinterpret_cast<uintptr_t>(m_offsets) & 3u))
+        return NVFP4_ERR_ALIGN;
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    gemm::Grouped grp;
+    grp.m_offsets = m_offsets;
+    grp.alphas = alphas;
+    grp.groups = groups;
+    grp.m_total = m_total;
+    return gemm::launch_pair<5, 128, 256, false>(A, SFA, B, SFB, 1.0f, D, m_total, N, K, stream, di, nullptr, Epi(),
+                                                 grp);
 }
 
 // Pair kernel with the per-CTA cycle trace on (trace: 148 x kTraceSlots u64 on the device).

@@ -14,6 +14,7 @@
 // kernel is instruction-bound before it is HBM-bound (IEEE divisions), so the
 // per-block reciprocal comes from a 256-entry table.
 #include "common.cuh"
+#include "grouped.cuh"
 #include "quant_common.cuh"
 
 namespace nvfp4 {
@@ -98,6 +99,82 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16 *__re
     }
 }
 
+// Grouped quantizer: the same per-block arithmetic over a stacked [m_total, K]
+// matrix whose row groups (grouped.cuh) each get their own blocked scale tensor.
+// Codes keep the stacked row order; rows outside every group get codes but no
+// scales.  Group tables are built per CTA in shared memory (G <= 256).
+constexpr int kQuantMaxGroups = 256;
+__global__ void __launch_bounds__(256) quantize_grouped_kernel(const __nv_bfloat16 *__restrict__ X,
+                                                               uint8_t *__restrict__ Q, uint8_t *__restrict__ SF,
+                                                               const float *__restrict__ gs_ptr,
+                                                               const int *__restrict__ m_offsets, int G,
+                                                               int m_total, int64_t K) {
+    __shared__ float inv_table[256];
+    __shared__ int g_r0[kQuantMaxGroups], g_r1[kQuantMaxGroups], g_b0[kQuantMaxGroups + 1];
+    const float gs = *gs_ptr;
+    const bool gs_ok = gs_usable(gs);
+    inv_table[threadIdx.x] = block_inverse(threadIdx.x, gs, gs_ok);  // blockDim.x == 256
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x < 32) build_group_tables(m_offsets, G, m_total, 0, lane, g_r0, g_r1, g_b0, nullptr);
+    __syncthreads();
+    const int64_t rest_k = K >> 6;
+    const int64_t n_blocks = (int64_t)m_total * K / 16;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g - lane < n_blocks; g += stride) {
+        uint32_t raw[8];
+        if (g < n_blocks) {
+            ld_stream_v8(X + g * 16, raw);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) raw[i] = 0;
+        }
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            v[2 * i] = __uint_as_float(raw[i] << 16);
+            v[2 * i + 1] = __uint_as_float(raw[i] & 0xFFFF0000u);
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; i++) amax = fmaxf(amax, fabsf(v[i]));
+        const uint32_t code = block_scale_code(amax, gs, gs_ok);
+        uint32_t lo, hi;
+        block_codes(v, inv_table[code], lo, hi);
+        const uint32_t c1 = __shfl_down_sync(0xffffffffu, code, 1);
+        const uint32_t c2 = __shfl_down_sync(0xffffffffu, code, 2);
+        const uint32_t c3 = __shfl_down_sync(0xffffffffu, code, 3);
+        if (g < n_blocks) {
+            *reinterpret_cast<uint2 *>(Q + g * 8) = make_uint2(lo, hi);
+            if ((lane & 3) == 0) {
+                const int64_t e = g * 16;
+                const int r = (int)(e / K);
+                const int64_t kg = (e - (int64_t)r * K) >> 6;
+                const int gr = last_group_at_or_before(g_r0, G, r);
+                if (r >= g_r0[gr] && r < g_r1[gr]) {
+                    const int local = r - g_r0[gr];
+                    const int64_t off = sf_group_offset((int64_t)g_b0[gr] * 128 + local, kg, rest_k);
+                    *reinterpret_cast<uint32_t *>(SF + off) = code | (c1 << 8) | (c2 << 16) | (c3 << 24);
+                }
+            }
+        }
+    }
+}
+
+// Zero the padding scale rows [M_g, pad128(M_g)) of every group (one CTA per group).
+__global__ void grouped_sf_pad_zero_kernel(uint8_t *SF, const int *m_offsets, int G, int m_total, int64_t K) {
+    __shared__ int g_r0[kQuantMaxGroups], g_r1[kQuantMaxGroups], g_b0[kQuantMaxGroups + 1];
+    if (threadIdx.x < 32) build_group_tables(m_offsets, G, m_total, 0, threadIdx.x & 31, g_r0, g_r1, g_b0, nullptr);
+    __syncthreads();
+    const int gr = blockIdx.x;
+    const int mg = g_r1[gr] - g_r0[gr];
+    const int pad = (mg + 127) / 128 * 128 - mg;
+    const int64_t rest_k = K >> 6, per_row = K >> 4;
+    for (int64_t i = threadIdx.x; i < (int64_t)pad * per_row; i += blockDim.x) {
+        const int64_t r = (int64_t)g_b0[gr] * 128 + mg + i / per_row, k16 = i % per_row;
+        SF[sf_group_offset(r, k16 >> 2, rest_k) + (k16 & 3)] = 0;
+    }
+}
+
 // Zero the scale bytes of rows [M, pad128(M)) (the blocked layout's padding).
 __global__ void sf_pad_zero_kernel(uint8_t *SF, int64_t M, int64_t K) {
     const int64_t rest_k = K >> 6;
@@ -178,6 +255,28 @@ extern "C" int nvfp4_quantize(const uint16_t *X, uint8_t *Q, uint8_t *SF, const 
     count_launch();
     if ((st = cuda_status(cudaGetLastError()))) return st;
     return sf_pad_zero(SF, M, K, s, di);
+}
+
+extern "C" int nvfp4_quantize_grouped(const uint16_t *X, uint8_t *Q, uint8_t *SF, const float *global_scale,
+                                      const int32_t *m_offsets, int groups, int m_total, int K, void *stream) {
+    if (!X || !Q || !SF || !global_scale || !m_offsets) return NVFP4_ERR_INVALID;
+    if (groups < 1 || groups > kQuantMaxGroups || m_total < 1 || K < 64 || K % 64) return NVFP4_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(X) & 31u) || !aligned16(Q) || (reinterpret_cast<uintptr_t>(SF) & 3u) ||
+        (reinterpret_cast<uintptr_t>(global_scale) & 3u) || (reinterpret_cast<uintptr_t>(m_offsets) & 3u))
+        return NVFP4_ERR_ALIGN;
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t n_blocks = (int64_t)m_total * K / 16;
+    int64_t blocks = (n_blocks + 255) / 256;
+    if (blocks > (int64_t)di.sm_count * 8) blocks = (int64_t)di.sm_count * 8;
+    quantize_grouped_kernel<<<(unsigned)blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16 *>(X), Q, SF,
+                                                             global_scale, m_offsets, groups, m_total, K);
+    grouped_sf_pad_zero_kernel<<<groups, 256, 0, s>>>(SF, m_offsets, groups, m_total, K);
+    count_launch();
+    count_launch();
+    return cuda_status(cudaGetLastError());
 }
 
 extern "C" int nvfp4_global_scale(const uint16_t *X, int64_t n, float *amax_out, float *gs_out, void *stream) {

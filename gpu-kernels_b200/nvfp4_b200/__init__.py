@@ -6,8 +6,10 @@ this package binds it for torch tensors.  Import path: put `gpu-kernels_b200/`
 on sys.path (the repository's conftest, bench.py and __graft_entry__ do).
 """
 from ._lib import LIB_PATH, NVFP4Error, SIGNATURES, lib  # noqa: F401
-from .layout import from_blocked, pad128, sf_bytes, sf_offset, to_blocked  # noqa: F401
-from .ops import (create_tensors, device_status, gemm, gemm_epilogue, gemm_host, global_scale,  # noqa: F401
-                  launch_count, matmul_nvfp4, quantize, selftest_wait_timeout, set_wait_timeout_ns)
+from .layout import (from_blocked, grouped_sf_block0, grouped_sf_bytes, pad128, sf_bytes, sf_offset,  # noqa: F401
+                     to_blocked)
+from .ops import (create_tensors, device_status, gemm, gemm_epilogue, gemm_grouped, gemm_host,  # noqa: F401
+                  global_scale, launch_count, matmul_nvfp4, quantize, quantize_grouped, selftest_wait_timeout,
+                  set_wait_timeout_ns)
 from . import runner_io  # noqa: F401,E402
 from . import torch_ops  # noqa: F401,E402  (registers torch.ops.nvfp4_b200.gemm / .quantize)

@@ -42,3 +42,19 @@ def from_blocked(sf_blocked: torch.Tensor, rows: int, K: int) -> torch.Tensor:
     rp, kb = pad128(rows), K // 16
     t = sf_blocked.view(torch.uint8).reshape(rp // 128, kb // 4, 32, 4, 4).permute(0, 3, 2, 1, 4)
     return t.reshape(rp, kb)[:rows].contiguous()
+
+
+def grouped_sf_bytes(m_total: int, groups: int, K: int) -> int:
+    """Capacity of a grouped scale buffer: each group's blocked tensor starts on a
+    128-row block, so at most ceil(m_total/128) + groups blocks of 128 x K/16 bytes."""
+    return ((m_total + 127) // 128 + groups) * 128 * (K // 16)
+
+
+def grouped_sf_block0(m_offsets):
+    """First 128-row scale block of each group (host copy of the device rule)."""
+    out, b = [], 0
+    for g in range(len(m_offsets) - 1):
+        out.append(b)
+        b += (max(0, m_offsets[g + 1] - m_offsets[g]) + 127) // 128
+    out.append(b)
+    return out

@@ -12,7 +12,7 @@ from typing import Optional, Tuple, Union
 import torch
 
 from ._lib import ACTIVATIONS, Epilogue, NVFP4Error, check, lib
-from .layout import sf_bytes, to_blocked
+from .layout import grouped_sf_bytes, sf_bytes, to_blocked
 
 
 def _stream(device: torch.device) -> int:
@@ -127,6 +127,61 @@ def gemm_epilogue(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torc
     return d if d is not None else (q, sf)
 
 
+def _offsets_tensor(m_offsets: torch.Tensor, device: torch.device) -> torch.Tensor:
+    if m_offsets.dtype != torch.int32 or m_offsets.dim() != 1 or m_offsets.numel() < 2 or \
+            m_offsets.device != device or not m_offsets.is_contiguous():
+        raise ValueError("m_offsets must be a contiguous 1-D int32 tensor of groups + 1 entries on the device")
+    return m_offsets
+
+
+def quantize_grouped(x: torch.Tensor, global_scale: Union[torch.Tensor, float], m_offsets: torch.Tensor,
+                     q_out: Optional[torch.Tensor] = None,
+                     sf_out: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [m_total, K] stacked by group -> (codes [m_total, K/2], grouped scales of
+    grouped_sf_bytes(m_total, groups, K) bytes: each group's blocked tensor starting on
+    a 128-row block).  m_offsets: device int32 [groups + 1]."""
+    if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous 2-D bf16 CUDA tensor")
+    m_total, K = x.shape
+    offs = _offsets_tensor(m_offsets, x.device)
+    G = offs.numel() - 1
+    gs = _scale_tensor(global_scale, x.device)
+    q = q_out if q_out is not None else torch.empty(m_total, K // 2, dtype=torch.uint8, device=x.device)
+    sf = sf_out if sf_out is not None else torch.empty(grouped_sf_bytes(m_total, G, K), dtype=torch.uint8,
+                                                       device=x.device)
+    check(lib().nvfp4_quantize_grouped(x.data_ptr(), q.data_ptr(), sf.data_ptr(), gs.data_ptr(), offs.data_ptr(), G,
+                                       m_total, K, _stream(x.device)), "nvfp4_quantize_grouped")
+    return q, sf
+
+
+def gemm_grouped(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, alphas: torch.Tensor,
+                 m_offsets: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Grouped (mixture-of-experts) GEMM: rows [m_offsets[g], m_offsets[g+1]) of the
+    stacked A times expert g's weight B[g*N:(g+1)*N], scaled by alphas[g] -> bf16 D
+    [m_total, N].  sfa in the grouped layout (quantize_grouped), sfb the experts'
+    blocked scales concatenated; alphas fp32 [groups] and m_offsets int32 [groups + 1]
+    on the device.  Rows outside every group are left as they are in `out`."""
+    for t, n in ((a, "a"), (sfa, "sfa"), (b, "b"), (sfb, "sfb")):
+        _bytes_tensor(t, n)
+    offs = _offsets_tensor(m_offsets, a.device)
+    G = offs.numel() - 1
+    m_total, K = a.shape[0], a.shape[1] * 2
+    if b.shape[1] * 2 != K or b.shape[0] % G:
+        raise ValueError("B must be [groups * N, K/2] with A's K")
+    N = b.shape[0] // G
+    if sfa.numel() < grouped_sf_bytes(m_total, G, K) or sfb.numel() < G * sf_bytes(N, K):
+        raise ValueError("scale tensors too small for the grouped layout")
+    if alphas.dtype != torch.float32 or alphas.numel() != G or alphas.device != a.device:
+        raise ValueError("alphas must be a float32 tensor of groups entries on the device")
+    d = out if out is not None else torch.zeros(m_total, N, dtype=torch.bfloat16, device=a.device)
+    if d.dtype != torch.bfloat16 or d.shape != (m_total, N) or not d.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 [m_total, N] tensor")
+    check(lib().nvfp4_gemm_grouped(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), alphas.data_ptr(),
+                                   d.data_ptr(), offs.data_ptr(), G, m_total, N, K, _stream(a.device)),
+          "nvfp4_gemm_grouped")
+    return d
+
+
 def gemm_host(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, alpha: float,
               out: torch.Tensor, device: Optional[torch.device] = None) -> torch.Tensor:
     """D = alpha * A . B^T from and to HOST tensors (pin them for overlap): uploads,
@@ -184,5 +239,6 @@ def launch_count() -> int:
     return int(lib().nvfp4_launch_count())
 
 
-__all__ = ["NVFP4Error", "global_scale", "quantize", "gemm", "gemm_epilogue", "gemm_host", "matmul_nvfp4",
+__all__ = ["NVFP4Error", "global_scale", "quantize", "quantize_grouped", "gemm", "gemm_epilogue", "gemm_grouped",
+           "gemm_host", "matmul_nvfp4",
            "create_tensors", "device_status", "set_wait_timeout_ns", "selftest_wait_timeout", "launch_count"]

@@ -159,6 +159,29 @@ NVFP4_API int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const ui
                                   void *stream);
 
 /*
+ * Grouped (mixture-of-experts) GEMM and its quantizer — no counterpart in the
+ * reference.  G <= 256 groups share N and K.  Group g is rows
+ * [m_offsets[g], m_offsets[g+1]) of the stacked activations A [m_total, K/2] (and of
+ * D [m_total, N]) and uses expert weight g = rows [g*N, (g+1)*N) of B [G*N, K/2]:
+ *     D[r, :] = alpha[g] * A[r, :] . B_g^T        for r in group g.
+ * m_offsets (G+1 int32, non-decreasing, clamped to [0, m_total]) and alpha (G fp32)
+ * are DEVICE arrays, so routing decided on the GPU needs no host round trip.
+ * Block scales of a grouped operand are laid out group by group: group g's blocked
+ * [pad128(M_g), K/16] tensor starts at 128-row block sum_{h<g} ceil(M_h/128), so a
+ * scale buffer needs (ceil(m_total/128) + G) * 128 * K/16 bytes
+ * (nvfp4_quantize_grouped writes this layout).  SFB is the G experts' blocked scale
+ * tensors one after another (N % 128 == 0).  D rows outside every group are not
+ * written.
+ */
+NVFP4_API int nvfp4_gemm_grouped(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+                                 const float *alpha, uint16_t *D, const int32_t *m_offsets, int groups,
+                                 int m_total, int N, int K, void *stream);
+/* bf16 X [m_total, K] -> codes Q [m_total, K/2] and the grouped scale layout above,
+ * one global scale for all groups (padding scale rows of every group zeroed). */
+NVFP4_API int nvfp4_quantize_grouped(const uint16_t *X, uint8_t *Q, uint8_t *SF, const float *global_scale,
+                                     const int32_t *m_offsets, int groups, int m_total, int K, void *stream);
+
+/*
  * Reference-signature shim: drop-in for matmul_nvfp4_vN in
  * matmul/sm100_nvfp4/runner.cu:61-96 (fp16 D, alpha = 1, legacy default
  * stream, no return value).  The status of the last call is kept for

@@ -1,0 +1,153 @@
+"""Grouped (mixture-of-experts) GEMM and quantizer.
+
+Group g = rows [m_offsets[g], m_offsets[g+1]) of the stacked activations, expert
+weight g = rows [g*N, (g+1)*N) of B; scales of a grouped operand are each group's
+blocked tensor starting on a 128-row block (the layout MoE kernels use for
+per-expert scale factors).  The oracle is applied group by group:
+  * quantizer: codes and every group's scale blocks byte-identical to the oracle's
+    quantizer run on that group alone (padding rows zero);
+  * GEMM: each group's D rows against the oracle GEMM of (A_g, B_g, alpha_g) with
+    max|D - D_ref| / max|D_ref| <= 1e-2; rows outside every group untouched;
+  * device-side routing: one captured CUDA graph replayed after the offsets change
+    in place follows the new routing.
+"""
+import numpy as np
+import pytest
+import torch
+
+
+def test_grouped_layout_rules(nv):
+    assert nv.grouped_sf_bytes(1000, 4, 1024) == (8 + 4) * 128 * 64
+    assert nv.grouped_sf_block0([0, 100, 100, 357, 900]) == [0, 1, 1, 4, 9]
+
+
+def test_grouped_host_checks(nv):
+    L = nv.lib()
+    f = 0x10000
+    assert L.nvfp4_gemm_grouped(f, f, f, f, f, f, f, 0, 256, 256, 256, None) == -2     # no groups
+    assert L.nvfp4_gemm_grouped(f, f, f, f, f, f, f, 257, 256, 256, 256, None) == -2   # > 256 groups
+    assert L.nvfp4_gemm_grouped(f, f, f, f, f, f, f, 4, 256, 200, 256, None) == -2     # N % 128
+    assert L.nvfp4_gemm_grouped(f, f, f, f, f, f, None, 4, 256, 256, 256, None) == -1  # no offsets
+    assert L.nvfp4_gemm_grouped(f + 8, f, f, f, f, f, f, 4, 256, 256, 256, None) == -3
+    assert L.nvfp4_quantize_grouped(f, f, f, f, f, 0, 256, 256, None) == -2
+    assert L.nvfp4_quantize_grouped(f + 16, f, f, f, f, 4, 256, 256, None) == -3      # X 32-byte aligned
+
+
+def _group_rows(offsets, m_total):
+    out = []
+    for g in range(len(offsets) - 1):
+        a = min(max(offsets[g], 0), m_total)
+        z = min(max(offsets[g + 1], a), m_total)
+        out.append((a, z))
+    return out
+
+
+CASES = [
+    # (offsets, m_total, N, K): empty group, groups not 128/256-aligned, rows outside all groups
+    ([0, 100, 100, 357, 900], 1000, 512, 1024),
+    # N % 256 == 128: the last column tile of an expert reads into the next expert's rows
+    ([0, 600, 640, 1500], 1500, 384, 512),
+    # eight experts, one of them holding most rows
+    ([0, 7, 300, 301, 2400, 2401, 2402, 2600, 3000], 3072, 1024, 2048),
+]
+
+
+def _make(oracle, nv, dev, offsets, m_total, N, K, seed):
+    G = len(offsets) - 1
+    x = oracle.normal_bf16((m_total, K), seed=seed)
+    gsa = oracle.global_scale_for(oracle.amax_bf16(x))
+    xt = torch.from_numpy(x.view(np.int16)).to(dev).view(torch.bfloat16)
+    offs = torch.tensor(offsets, dtype=torch.int32, device=dev)
+    q, sf = nv.quantize_grouped(xt, torch.tensor([gsa], dtype=torch.float32, device=dev), offs)
+    bq, bsf, alphas = [], [], []
+    for g in range(G):
+        w = oracle.normal_bf16((N, K), seed=seed + 100 + g, std=0.02)
+        gsb = oracle.global_scale_for(oracle.amax_bf16(w))
+        qb, sfb = oracle.quantize(w, gsb)
+        bq.append(qb)
+        bsf.append(sfb)
+        alphas.append(np.float32(gsa) * np.float32(gsb))
+    return x, gsa, offs, q, sf, np.concatenate(bq), np.concatenate(bsf), np.array(alphas, dtype=np.float32)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("offsets,m_total,N,K", CASES)
+def test_quantize_grouped_matches_oracle_per_group(nv, oracle, cuda_dev, offsets, m_total, N, K):
+    x, gsa, offs, q, sf, *_ = _make(oracle, nv, cuda_dev, offsets, m_total, N, K, seed=5)
+    torch.cuda.synchronize()
+    q, sf = q.cpu().numpy(), sf.cpu().numpy()
+    blk = 128 * K // 16
+    block0 = 0
+    for a, z in _group_rows(offsets, m_total):
+        if z == a:
+            continue
+        q_ref, sf_ref = oracle.quantize(x[a:z], gsa)
+        assert np.array_equal(q[a:z], q_ref)
+        nb = (z - a + 127) // 128
+        assert np.array_equal(sf[block0 * blk:(block0 + nb) * blk], sf_ref), (a, z)
+        block0 += nb
+    # rows outside every group still get codes (same per-block arithmetic)
+    last = _group_rows(offsets, m_total)[-1][1]
+    if last < m_total:
+        q_ref, _ = oracle.quantize(x[last:], gsa)
+        assert np.array_equal(q[last:], q_ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("offsets,m_total,N,K", CASES)
+def test_gemm_grouped_matches_oracle_per_group(nv, oracle, cuda_dev, offsets, m_total, N, K):
+    x, gsa, offs, q, sf, bq, bsf, alphas = _make(oracle, nv, cuda_dev, offsets, m_total, N, K, seed=7)
+    out = torch.full((m_total, N), 7.0, dtype=torch.bfloat16, device=cuda_dev)  # sentinel outside the groups
+    d = nv.gemm_grouped(q, sf, torch.from_numpy(bq).to(cuda_dev), torch.from_numpy(bsf).to(cuda_dev),
+                        torch.from_numpy(alphas).to(cuda_dev), offs, out=out)
+    torch.cuda.synchronize()
+    nv.device_status()
+    got = d.float().cpu().numpy()
+    qh, sfh = q.cpu().numpy(), sf.cpu().numpy()
+    blk = 128 * K // 16
+    block0 = 0
+    covered = np.zeros(m_total, dtype=bool)
+    for g, (a, z) in enumerate(_group_rows(offsets, m_total)):
+        if z == a:
+            continue
+        nb = (z - a + 127) // 128
+        _, d16 = oracle.gemm(qh[a:z], sfh[block0 * blk:(block0 + nb) * blk], bq[g * N:(g + 1) * N],
+                             bsf[g * (N // 128) * blk:(g + 1) * (N // 128) * blk], float(alphas[g]), z - a, N, K)
+        ref = oracle.bf16_bits_to_f32(d16).reshape(z - a, N)
+        err = np.abs(got[a:z] - ref).max() / np.abs(ref).max()
+        assert err <= 1e-2, (g, err)
+        covered[a:z] = True
+        block0 += nb
+    assert (got[~covered] == 7.0).all()
+
+
+@pytest.mark.gpu
+def test_gemm_grouped_graph_follows_device_routing(nv, oracle, cuda_dev):
+    offsets, m_total, N, K = [0, 300, 700, 1024], 1024, 256, 512
+    x, gsa, offs, q, sf, bq, bsf, alphas = _make(oracle, nv, cuda_dev, offsets, m_total, N, K, seed=9)
+    b, sfb, al = (torch.from_numpy(t).to(cuda_dev) for t in (bq, bsf, alphas))
+    out = torch.zeros(m_total, N, dtype=torch.bfloat16, device=cuda_dev)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        nv.gemm_grouped(q, sf, b, sfb, al, offs, out=out)  # warm-up: tensor maps, attributes
+        s.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            nv.gemm_grouped(q, sf, b, sfb, al, offs, out=out)
+    graph.replay()
+    torch.cuda.synchronize()
+    first = out.clone()
+    # new routing written on the device: every row to expert 2 (the activations are
+    # re-quantized into the captured buffers for the new grouping first)
+    new = torch.tensor([0, 0, 0, 1024], dtype=torch.int32, device=cuda_dev)
+    xt = torch.from_numpy(x.view(np.int16)).to(cuda_dev).view(torch.bfloat16)
+    nv.quantize_grouped(xt, torch.tensor([gsa], dtype=torch.float32, device=cuda_dev), new, q_out=q, sf_out=sf)
+    offs.copy_(new)
+    graph.replay()
+    torch.cuda.synchronize()
+    del graph
+    ref = nv.gemm(q, sf[:nv.sf_bytes(m_total, K)], b[2 * N:], sfb[2 * (N // 128) * 128 * K // 16:], float(alphas[2]))
+    torch.cuda.synchronize()
+    got, want = out.float(), ref.float()
+    assert (got - want).abs().max().item() <= 1e-2 * want.abs().max().item()
+    assert not torch.equal(first, out)
