@@ -58,8 +58,9 @@ def committed_traffic():
 
 
 class ClockSampler:
-    """SM clock, power and clock-event (throttle) reasons sampled every 5 ms through
-    NVML on a background thread for the duration of the timed region."""
+    """SM clock, power and clock-event (throttle) reasons sampled through NVML on a
+    background thread (every ~1 ms plus the call's own latency) for the duration of
+    the timed region."""
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                0x80: "hw_power_brake_slowdown"}
 
@@ -102,7 +103,7 @@ class ClockSampler:
                                          nvml.nvmlDeviceGetPowerUsage(h) / 1000.0, int(get_reasons(h))))
                 except Exception:
                     pass
-                self._stop.wait(0.005)
+                self._stop.wait(0.001)
 
         self._thread = threading.Thread(target=loop, daemon=True)
         self._thread.start()
@@ -432,6 +433,91 @@ def quantize_section(nv, dev, pk, reps=20):
     return res
 
 
+def moe_section(nv, dev, reps=20):
+    """Grouped (mixture-of-experts) GEMM: Mixtral-8x7B-like expert up-projection,
+    8 experts N=14336 K=4096, 4096 tokens x top-2 = 8192 routed rows split by a
+    seeded random routing; useful TFLOP/s (2 * sum M_g * N * K / time) beside one
+    dense GEMM of the same total shape."""
+    G, N, K, tokens, top = 8, 14336, 4096, 4096, 2
+    g = torch.Generator().manual_seed(77)
+    counts = torch.bincount(torch.randint(0, G, (tokens * top,), generator=g), minlength=G)
+    offsets = [0] + torch.cumsum(counts, 0).tolist()
+    m_total = offsets[-1]
+    gen = torch.Generator(device=dev).manual_seed(78)
+    x = torch.randn(m_total, K, device=dev, generator=gen).to(torch.bfloat16)
+    _, gsx = nv.global_scale(x)
+    offs = torch.tensor(offsets, dtype=torch.int32, device=dev)
+    q, sf = nv.quantize_grouped(x, gsx, offs)
+    bq = torch.empty(G * N, K // 2, dtype=torch.uint8, device=dev)
+    bsf = torch.empty(G * nv.sf_bytes(N, K), dtype=torch.uint8, device=dev)
+    alphas = torch.empty(G, dtype=torch.float32, device=dev)
+    for e in range(G):
+        w = (torch.randn(N, K, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        _, gw = nv.global_scale(w)
+        nv.quantize(w, gw, q_out=bq[e * N:(e + 1) * N], sf_out=bsf[e * nv.sf_bytes(N, K):(e + 1) * nv.sf_bytes(N, K)])
+        alphas[e:e + 1] = gsx * gw
+    d = torch.empty(m_total, N, dtype=torch.bfloat16, device=dev)
+    flops = 2.0 * m_total * N * K
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    ms = timed(lambda: nv.gemm_grouped(q, sf, bq, bsf, alphas, offs, out=d))
+    # the same total work as one dense GEMM (expert 0's weights for every row)
+    dense_ms = timed(lambda: nv.gemm(q, sf[:nv.sf_bytes(m_total, K)], bq[:N], bsf[:nv.sf_bytes(N, K)], 1.0, out=d))
+    nv.device_status()
+    return {"what": "grouped NVFP4 GEMM, 8 experts N=14336 K=4096, 8192 routed rows (4096 tokens x top-2)",
+            "rows_per_expert": counts.tolist(), "ms": ms, "tflops": flops / (ms / 1e3) / 1e12,
+            "dense_same_shape_ms": dense_ms, "dense_same_shape_tflops": flops / (dense_ms / 1e3) / 1e12}
+
+
+def epilogue_section(nv, sets, M, N, K, reps=30):
+    """Cost of the fused epilogue at 8192^3: plain bf16 GEMM, GEMM + bias + SiLU with
+    NVFP4 output (the next layer's operand), and the unfused sequence (GEMM with
+    bias + SiLU in bf16, then nvfp4_quantize)."""
+    a, sfa, b, sfb, alpha = sets[0]
+    dev = a.device
+    bias = torch.zeros(N, dtype=torch.bfloat16, device=dev)
+    gs = torch.tensor([1e-3], dtype=torch.float32, device=dev)
+    d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    q = torch.empty(M, N // 2, dtype=torch.uint8, device=dev)
+    sf = torch.empty(nv.sf_bytes(M, N), dtype=torch.uint8, device=dev)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    plain = timed(lambda: nv.gemm(a, sfa, b, sfb, alpha, out=d))
+    fused = timed(lambda: nv.gemm_epilogue(a, sfa, b, sfb, alpha, bias=bias, activation="silu",
+                                           out_global_scale=gs, q_out=q, sf_out=sf))
+
+    def unfused():
+        nv.gemm_epilogue(a, sfa, b, sfb, alpha, bias=bias, activation="silu", out=d)
+        nv.quantize(d, gs, q_out=q, sf_out=sf)
+
+    two = timed(unfused)
+    nv.device_status()
+    return {"what": "8192^3 GEMM: plain bf16 / bias+SiLU+NVFP4-out fused / bias+SiLU bf16 then nvfp4_quantize",
+            "plain_ms": plain, "fused_nvfp4_out_ms": fused, "unfused_ms": two}
+
+
 def run_decode_workload(args, M, N, K):
     """One skinny-M shape alone (for profiling): weights rotate over 3 sets."""
     import nvfp4_b200 as nv
@@ -572,10 +658,12 @@ def run_ours(args):
     traffic = committed_traffic().get("gemm_8192", {}).get("dram_bytes_per_launch")
     cpu = None
     vendor = vendor_scaled_mm(sets, M, N, K) if rank == 0 else None
-    decode = quant = None
+    decode = quant = moe = epi = None
     if not args.no_decode:
         decode = decode_section(nv, dev, pk)
         quant = quantize_section(nv, dev, pk)
+        moe = moe_section(nv, dev)
+        epi = epilogue_section(nv, sets, M, N, K)
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu, _, _ = cpu_reference_sample(a, sfa, b, sfb, alpha, M, N, K, target_s=args.cpu_seconds)
 
@@ -608,6 +696,10 @@ def run_ours(args):
             line["decode"] = decode
         if quant is not None:
             line["quantize"] = quant
+        if moe is not None:
+            line["moe_grouped"] = moe
+        if epi is not None:
+            line["fused_epilogue"] = epi
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

@@ -106,11 +106,13 @@ int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, 
     e.sf = epi->sf_out;
     e.gs = epi->out_global_scale;
     if (e.act < NVFP4_ACT_NONE || e.act > NVFP4_ACT_GELU_TANH) return NVFP4_ERR_INVALID;
-    if (e.bias && (reinterpret_cast<uintptr_t>(e.bias) & 1u)) return NVFP4_ERR_ALIGN;
+    if (e.bias && !aligned16(e.bias)) return NVFP4_ERR_ALIGN;
     if (e.q) {
         if (!e.sf || !e.gs) return NVFP4_ERR_INVALID;
         if (N % 64) return NVFP4_ERR_SHAPE;
-        if ((reinterpret_cast<uintptr_t>(e.sf) & 3u) || (reinterpret_cast<uintptr_t>(e.gs) & 3u)) return NVFP4_ERR_ALIGN;
+        if ((reinterpret_cast<uintptr_t>(e.q) & 31u) || (reinterpret_cast<uintptr_t>(e.sf) & 3u) ||
+            (reinterpret_cast<uintptr_t>(e.gs) & 3u))
+            return NVFP4_ERR_ALIGN;
     }
     int st = gemm_validate(A, SFA, B, SFB, e.q ? static_cast<const void *>(e.q) : D, M, N, K);
     if (st) return st;

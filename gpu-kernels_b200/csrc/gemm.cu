@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       p.alpha);
             else
                 store_row_epi<kCols>(acc, p, tm * kBlockM + quarter * 32 + lane, tn * BN + half * kCols, p.M,
-                                     p.alpha);
+                                     p.alpha, load_bias_lane(p.epi, p.N, tn * BN + half * kCols, lane));
         }
     }
 

@@ -96,28 +96,47 @@ __device__ __forceinline__ void store_row(const uint32_t (&acc)[kCols], const Pa
 }
 
 // The fused-epilogue form of store_row (bf16 or NVFP4 output, see epilogue.cuh).
-// NVFP4 output needs col0 and N to be multiples of 64: each 64-column k-group of
-// the row is then whole, its 32 bytes of codes leave as two 16-byte stores and its
-// 4 scale bytes as one 32-bit store.  Rows >= row_end are skipped (the caller zeroes
-// the scale padding rows).
+// Called by all 32 lanes of a warp, each with its own row and the same col0: the
+// tile's bias columns col0 .. col0+127 arrive as 4 bf16 per lane (bias_raw, lane l
+// holding columns col0 + 4l .. +3) and are broadcast with shuffles, so every lane
+// takes part whether or not its row is stored.  NVFP4 output needs col0 and N to be
+// multiples of 64: each 64-column k-group of the row is then whole, its 32 bytes of
+// codes leave as one 32-byte store and its 4 scale bytes as one 32-bit store.  Rows
+// >= row_end are not stored (the caller zeroes the scale padding rows).
 template <int kCols>
 __device__ __forceinline__ void store_row_epi(const uint32_t (&acc)[kCols], const Params &p, int row, int col0,
-                                              int row_end, float alpha) {
-    if (row >= row_end) return;
+                                              int row_end, float alpha, uint2 bias_raw) {
+    static_assert(kCols <= 128, "bias is broadcast from 4 columns per lane");
     const Epi &e = p.epi;
+    const bool row_ok = row < row_end;
+    // bias of columns col0 + k, col0 + k + 1 (k even)
+    auto bias2 = [&](int k, float &b0, float &b1) {
+        const uint32_t w = __shfl_sync(0xffffffffu, ((k >> 1) & 1) ? bias_raw.y : bias_raw.x, k >> 2);
+        b0 = __uint_as_float(w << 16);
+        b1 = __uint_as_float(w & 0xFFFF0000u);
+    };
     if (!e.q) {
         uint8_t *drow = static_cast<uint8_t *>(p.d) + ((int64_t)row * p.N + col0) * 2;
 #pragma unroll
-        for (int c = 0; c < kCols / 8; c++) {
-            if (col0 + c * 8 < p.N) {
-                uint32_t w[4];
+        for (int c = 0; c < kCols / 16; c++) {
+            uint32_t w[8];
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int k = c * 8 + 2 * i;
-                    w[i] = pack2(epi_value(__uint_as_float(acc[k]), alpha, e, col0 + k),
-                                 epi_value(__uint_as_float(acc[k + 1]), alpha, e, col0 + k + 1), false);
+            for (int i = 0; i < 8; i++) {
+                const int k = c * 16 + 2 * i;
+                float b0, b1;
+                bias2(k, b0, b1);
+                w[i] = pack2(epi_value(__uint_as_float(acc[k]), alpha, e, b0),
+                             epi_value(__uint_as_float(acc[k + 1]), alpha, e, b1), false);
+            }
+            if (row_ok) {
+                if (p.vec32_store) {
+                    if (col0 + c * 16 < p.N) st_global_v8(drow + c * 32, w);
+                } else {
+                    if (col0 + c * 16 < p.N)
+                        *reinterpret_cast<uint4 *>(drow + c * 32) = make_uint4(w[0], w[1], w[2], w[3]);
+                    if (col0 + c * 16 + 8 < p.N)
+                        *reinterpret_cast<uint4 *>(drow + c * 32 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
                 }
-                *reinterpret_cast<uint4 *>(drow + c * 16) = make_uint4(w[0], w[1], w[2], w[3]);
             }
         }
         return;
@@ -129,29 +148,38 @@ __device__ __forceinline__ void store_row_epi(const uint32_t (&acc)[kCols], cons
 #pragma unroll
         for (int g = 0; g < kCols / 64; g++) {
             const int c0 = col0 + g * 64;
-            if (c0 < p.N) {
-                uint32_t codes[8], scales = 0;
+            uint32_t codes[8], scales = 0;
 #pragma unroll
-                for (int b = 0; b < 4; b++) {
-                    float v[16];
-                    float amax = 0.0f;
+            for (int b = 0; b < 4; b++) {
+                float v[16];
+                float amax = 0.0f;
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        const int k = g * 64 + b * 16 + i;
-                        v[i] = round_bf16(epi_value(__uint_as_float(acc[k]), alpha, e, col0 + k));
-                        amax = fmaxf(amax, fabsf(v[i]));
-                    }
-                    const uint32_t code = block_scale_code(amax, gs, gs_ok);
-                    block_codes(v, block_inverse(code, gs, gs_ok), codes[2 * b], codes[2 * b + 1]);
-                    scales |= code << (8 * b);
+                for (int i = 0; i < 16; i += 2) {
+                    const int k = g * 64 + b * 16 + i;
+                    float b0, b1;
+                    bias2(k, b0, b1);
+                    v[i] = round_bf16(epi_value(__uint_as_float(acc[k]), alpha, e, b0));
+                    v[i + 1] = round_bf16(epi_value(__uint_as_float(acc[k + 1]), alpha, e, b1));
+                    amax = fmaxf(amax, fmaxf(fabsf(v[i]), fabsf(v[i + 1])));
                 }
-                uint8_t *qrow = e.q + (int64_t)row * (p.N >> 1) + (c0 >> 1);
-                *reinterpret_cast<uint4 *>(qrow) = make_uint4(codes[0], codes[1], codes[2], codes[3]);
-                *reinterpret_cast<uint4 *>(qrow + 16) = make_uint4(codes[4], codes[5], codes[6], codes[7]);
+                const uint32_t code = block_scale_code(amax, gs, gs_ok);
+                block_codes(v, block_inverse(code, gs, gs_ok), codes[2 * b], codes[2 * b + 1]);
+                scales |= code << (8 * b);
+            }
+            if (row_ok && c0 < p.N) {
+                st_global_v8(e.q + (int64_t)row * (p.N >> 1) + (c0 >> 1), codes);
                 *reinterpret_cast<uint32_t *>(e.sf + sf_group_offset(row, c0 >> 6, rest)) = scales;
             }
         }
     }
+}
+
+// This lane's 4 bias values of the columns col0 + 4 * lane .. +3 (zero without a
+// bias or past N), for store_row_epi.
+__device__ __forceinline__ uint2 load_bias_lane(const Epi &e, int N, int col0, int lane) {
+    const int n = col0 + 4 * lane;
+    if (!e.bias || n >= N) return make_uint2(0u, 0u);
+    return __ldg(reinterpret_cast<const uint2 *>(e.bias + n));
 }
 
 // Encoded (and cached) 2-D tensor map over an NVFP4 operand [rows, K/2] bytes with a

@@ -283,10 +283,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             } else if (!p.epi.q) {
                 if (n < p.N) {
+                    const float bias_n = p.epi.bias ? bf16_bits_to_float(p.epi.bias[n]) : 0.0f;
 #pragma unroll
                     for (int m = 0; m < MPAD; m++)
                         if (m < p.M) {
-                            __nv_bfloat16 v = __float2bfloat16_rn(epi_value(sum[m], p.alpha, p.epi, n));
+                            __nv_bfloat16 v = __float2bfloat16_rn(epi_value(sum[m], p.alpha, p.epi, bias_n));
                             p.d[(int64_t)m * p.N + n] = *reinterpret_cast<uint16_t *>(&v);
                         }
                 }
@@ -297,11 +298,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float gs = *p.epi.gs;
                 const bool gs_ok = gs_usable(gs);
                 const bool valid = n < p.N;
+                const float bias_n = (valid && p.epi.bias) ? bf16_bits_to_float(p.epi.bias[n]) : 0.0f;
                 const int64_t rest = p.N >> 6;
 #pragma unroll
                 for (int m = 0; m < MPAD; m++) {
                     if (m < p.M) {
-                        const float v = valid ? round_bf16(epi_value(sum[m], p.alpha, p.epi, n)) : 0.0f;
+                        const float v = valid ? round_bf16(epi_value(sum[m], p.alpha, p.epi, bias_n)) : 0.0f;
                         float amax = fabsf(v);
 #pragma unroll
                         for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));

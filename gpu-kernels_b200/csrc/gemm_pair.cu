@@ -415,7 +415,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             if (p.epi.plain())
                 store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha);
             else
-                store_row_epi<kCols>(acc, p, row, col0, ti.row_end, ti.alpha);
+                store_row_epi<kCols>(acc, p, row, col0, ti.row_end, ti.alpha, load_bias_lane(p.epi, p.N, col0, lane));
             if (TRACE && warp == 2 && lane == 0) t_store += clock64() - c_ready;
         }
         if (TRACE && warp == 2 && lane == 0) {

@@ -131,7 +131,8 @@ NVFP4_API int nvfp4_gemm_f16(const uint8_t *A, const uint8_t *SFA, const uint8_t
  *   y = alpha * acc;  y += bias[n] (bf16, optional);  y = act(y)
  * with act one of
  *   NVFP4_ACT_NONE, NVFP4_ACT_RELU (max(y, 0)), NVFP4_ACT_SILU (y / (1 + exp(-y))),
- *   NVFP4_ACT_GELU_TANH (0.5 y (1 + tanh(sqrt(2/pi) (y + 0.044715 y^3)))).
+ *   NVFP4_ACT_GELU_TANH (0.5 y (1 + tanh(sqrt(2/pi) (y + 0.044715 y^3)))),
+ * silu and gelu with the GPU's approximate exp / reciprocal / tanh instructions.
  * Output: bf16(y) into D, or — when q_out is given — the bf16(y) rows quantized to
  * NVFP4 for the next layer: codes [M, N/2] into q_out and blocked e4m3 scales
  * [pad128(M), N/16] into sf_out with the fp32 global scale *out_global_scale
@@ -145,9 +146,9 @@ enum {
     NVFP4_ACT_GELU_TANH = 3
 };
 typedef struct nvfp4_epilogue {
-    const uint16_t *bias;          /* bf16 [N] (2-byte aligned), or NULL */
+    const uint16_t *bias;          /* bf16 [N] (16-byte aligned), or NULL */
     int activation;                /* NVFP4_ACT_* */
-    uint8_t *q_out;                /* NVFP4 output codes [M, N/2] (16-byte aligned), or NULL for bf16 D */
+    uint8_t *q_out;                /* NVFP4 output codes [M, N/2] (32-byte aligned), or NULL for bf16 D */
     uint8_t *sf_out;               /* its blocked scales [pad128(M) * N/16] (4-byte aligned) */
     const float *out_global_scale; /* device fp32 global scale of the output */
 } nvfp4_epilogue;

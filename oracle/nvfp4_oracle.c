@@ -361,8 +361,8 @@ void nvfp4o_gemm_rows(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, co
  *   y = alpha * acc;  y = y + bias[n];  y = act(y);  out = bf16_rn(y)
  * act: 0 none, 1 relu max(y, 0), 2 silu y / (1 + exp(-y)),
  *      3 gelu (tanh form) 0.5 y (1 + tanh(0.7978845608028654 (y + 0.044715 y^3))).
- * exp/tanh are the C library's, so silu/gelu agree with the GPU to a few ulp of
- * fp32, not bit for bit.
+ * exp/tanh are the C library's; the GPU uses its approximate exp, reciprocal and
+ * tanh instructions, so silu/gelu agree within the GEMM tolerance, not bit for bit.
  * ------------------------------------------------------------------------- */
 void nvfp4o_epilogue(const float *acc, const uint16_t *bias, int act, float alpha, int64_t rows, int64_t N,
                      float *Y32, uint16_t *Y16, int nthreads) {

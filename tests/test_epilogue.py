@@ -51,10 +51,11 @@ def test_epilogue_host_checks(nv):
         return L.nvfp4_gemm_epilogue(fake, fake, fake, fake, 1.0, d, M, N, K, C.byref(e), None)
 
     assert call(256, 256, 256, E(activation=7)) == -1                                   # INVALID
-    assert call(256, 256, 256, E(bias=fake + 1)) == -3                                  # ALIGN
+    assert call(256, 256, 256, E(bias=fake + 8)) == -3                                  # ALIGN: bias 16 B
     assert call(256, 200, 256, E(q_out=fake, sf_out=fake, out_global_scale=fake)) == -2  # SHAPE: N % 64
     assert call(256, 256, 256, E(q_out=fake, sf_out=None, out_global_scale=fake)) == -1  # INVALID
     assert call(256, 256, 256, E(q_out=fake, sf_out=fake + 2, out_global_scale=fake)) == -3
+    assert call(256, 256, 256, E(q_out=fake + 16, sf_out=fake, out_global_scale=fake)) == -3  # q 32 B
     assert call(256, 256, 100, E()) == -2                                               # K % 64
 
 
