@@ -153,6 +153,21 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
+def in_kernel_clock(nv, operands, d, M, N, K, dev):
+    """SM clock the GEMM itself runs at: one launch of the traced CTA-pair kernel on
+    the bench's operands, clock64 cycles over globaltimer ns of each pair's MMA thread."""
+    a, sfa, b, sfb, alpha = operands
+    tr = torch.zeros(148 * 12, dtype=torch.int64, device=dev)
+    st = nv.lib().nvfp4_gemm_trace(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), alpha, d.data_ptr(),
+                                   M, N, K, tr.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+    torch.cuda.synchronize()
+    if st != 0:
+        return None
+    t = tr.view(148, 12)[0::2].double().cpu()
+    ok = t[:, 7] > 0
+    return float((t[ok, 6] / t[ok, 7]).mean() * 1e3) if ok.any() else None
+
+
 def make_operand_sets(nv, n_sets, M, N, K, seed, dev):
     """Quantized operand sets generated on the device by the product's own kernels."""
     g = torch.Generator(device=dev)
@@ -617,6 +632,7 @@ def run_ours(args):
         barrier(world)
     launches = nv.launch_count() - launches0
     nv.device_status()
+    in_kernel_mhz = in_kernel_clock(nv, sets[0], d, M, N, K, dev)
     per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
     total_ms = max_over_ranks(sum(per), world)
     ms_step = total_ms / args.steps
@@ -684,7 +700,9 @@ def run_ours(args):
                          "frac_of_nominal_9000": achieved / 9000.0,
                          "kernel_ms": kernel_ms, "flops_per_launch": flops},
             "gpu_launches": int(launches),
-            "clocks": clk.summary(),
+            "clocks": dict(clk.summary(), in_kernel_sm_mhz=in_kernel_mhz,
+                           in_kernel_note="SM cycles (clock64) / ns (globaltimer) of the MMA thread over one "
+                                          "traced launch of the same GEMM right after the timed region"),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                     "ms_per_step": e2e_ms, "path": "pinned host -> nvfp4_gemm_host (4x4 blocks, copies overlapped) -> pinned host"},
         }
