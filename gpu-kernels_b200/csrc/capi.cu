@@ -14,6 +14,9 @@ namespace nvfp4 {
 int gemm_dispatch_epi(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                       int M, int N, int K, cudaStream_t stream, bool f16, const Epi &epi);
 int sf_pad_zero(uint8_t *SF, int M, int K, cudaStream_t s, const DeviceInfo &di);
+int decode_trace_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                          uint16_t *D, int M, int N, int K, void *ws, size_t ws_bytes, unsigned long long *trace,
+                          cudaStream_t stream);
 int grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const float *alphas,
                      uint16_t *D, const int *m_offsets, int groups, int m_total, int N, int K, cudaStream_t stream);
 int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
@@ -174,6 +177,13 @@ int nvfp4_gemm_decode_noalloc(const uint8_t *A, const uint8_t *SFA, const uint8_
 int nvfp4_gemm_host(const uint8_t *hA, const uint8_t *hSFA, const uint8_t *hB, const uint8_t *hSFB, float alpha,
                     uint16_t *hD, int M, int N, int K, void *stream) {
     return gemm_host(hA, hSFA, hB, hSFB, alpha, hD, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+int nvfp4_gemm_decode_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                            uint16_t *D, int M, int N, int K, void *workspace, size_t workspace_bytes, uint64_t *trace,
+                            void *stream) {
+    return decode_trace_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, workspace, workspace_bytes,
+                                 reinterpret_cast<unsigned long long *>(trace), static_cast<cudaStream_t>(stream));
 }
 
 int nvfp4_gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,

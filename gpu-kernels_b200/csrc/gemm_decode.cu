@@ -9,8 +9,12 @@
 //     tcgen05 kind::mxf4nvf4 (M = 128 weight rows, N = MPAD activation rows, MPAD in
 //     {8,16,32,64,128}); weights stream from HBM (evict-first), the small activation
 //     matrix stays L2-resident (evict-last);
-//   * stream-K: the n_tiles x k_blocks iteration space is cut into one contiguous
-//     range per CTA (grid = #SMs), so every SM streams the same number of bytes;
+//   * hybrid data-parallel + stream-K: with n_tiles >= grid, each CTA owns
+//     floor(n_tiles / grid) whole tiles and the k-blocks of the remaining tiles are cut
+//     into one contiguous range per CTA (grid = #SMs), so every SM streams the same
+//     number of bytes; a CTA works through its cut tiles first and its whole tiles
+//     last, so the cross-CTA reductions happen while the other CTAs still stream and
+//     every CTA ends on a plain store;
 //   * a tile whose k-range is split across CTAs is finished by the last contributor,
 //     which adds the fp32 partials in CTA order (deterministic) — partials and
 //     per-tile arrival counters live in a caller-provided workspace that the kernel
@@ -19,6 +23,7 @@
 //   * bounded waits as in gemm.cu.
 #include <cuda_bf16.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm_common.cuh"
@@ -45,12 +50,16 @@ struct Layout {
     static constexpr int kOffSfw = kOffX + STAGES * kX;
     static constexpr int kOffSfx = kOffSfw + STAGES * kSfw;
     static constexpr int kOffBar = kOffSfx + STAGES * kSfx;
-    static constexpr int kBarBytes = (2 * STAGES + 3) * 8 + 32;
+    static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 32;  // full, empty, acc_full x2, acc_empty x2, drain
     static constexpr int kDynamicSmem = kOffBar + kBarBytes + 1024;
     static constexpr int kSfColsPerStage = kKGroups * 8;  // SFw 4 + SFx 4 per k-group
-    static constexpr int kTmemCols = MPAD + 2 * kSfColsPerStage <= 128 ? 128 : 256;
+    // TMEM: two accumulators of MPAD columns (the MMAs of the next tile segment run
+    // while the epilogue drains this one), then two sets of scale columns
+    static constexpr int kSfBase = 2 * MPAD;
+    static constexpr int kTmemNeed = 2 * MPAD + 2 * kSfColsPerStage;
+    static constexpr int kTmemCols = kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512);
     static_assert(MPAD % 8 == 0 && MPAD <= 128, "MPAD");
-    static_assert(MPAD + 2 * kSfColsPerStage <= kTmemCols, "tensor memory budget");
+    static_assert(kTmemNeed <= kTmemCols, "tensor memory budget");
     static_assert(kDynamicSmem <= 232448, "shared memory budget");
 };
 
@@ -64,16 +73,26 @@ struct Params {
     float alpha;
     int n_tiles, num_kb, k_groups;
     int64_t total_iters;
+    int sk_tiles;         // tiles [0, sk_tiles) are cut across CTAs (stream-K)
+    int64_t sk_iters;     // their k-blocks: sk_tiles * num_kb
+    int dp_per_cta;       // whole tiles per CTA: tiles sk_tiles + c * dp_per_cta + j
+    int rotate;           // process a cut last tile of the stream-K range first
     int grid;
     KernelCtl ctl;
     Epi epi;  // fused epilogue (plain: alpha and bf16 rounding only)
+    // Optional per-CTA %globaltimer stamps (nullptr = off), kDecodeTraceSlots u64 per
+    // CTA: [0] entry [1] dependency wait released [2] first slot full (MMA thread)
+    // [3] last slot full [4] epilogue done [5] iterations
+    unsigned long long *trace;
 };
+constexpr int kDecodeTraceSlots = 6;
 
-__device__ __forceinline__ int64_t range_begin(int64_t c, const Params &p) { return c * p.total_iters / p.grid; }
+// Stream-K range of CTA c over the cut tiles' k-blocks: [range_begin(c), range_begin(c+1)).
+__device__ __forceinline__ int64_t range_begin(int64_t c, const Params &p) { return c * p.sk_iters / p.grid; }
 
 // CTA whose range holds iteration `it` (ranges are [begin(c), begin(c+1))).
 __device__ __forceinline__ int owner_of(int64_t it, const Params &p) {
-    return (int)(((it + 1) * p.grid - 1) / p.total_iters);
+    return (int)(((it + 1) * p.grid - 1) / p.sk_iters);
 }
 
 template <int MPAD>
@@ -87,19 +106,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *base_ptr = smem_raw + (base - smem_u32(smem_raw));
     const uint32_t sW = base + L::kOffW, sX = base + L::kOffX, sSfw = base + L::kOffSfw, sSfx = base + L::kOffSfx;
     const uint32_t bar_full = base + L::kOffBar, bar_empty = bar_full + 8 * S;
-    const uint32_t bar_acc_full = bar_empty + 8 * S, bar_acc_empty = bar_acc_full + 8, bar_drain = bar_acc_empty + 8;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(base_ptr + L::kOffBar + (2 * S + 3) * 8);
+    const uint32_t bar_acc_full = bar_empty + 8 * S, bar_acc_empty = bar_acc_full + 16, bar_drain = bar_acc_empty + 16;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(base_ptr + L::kOffBar + (2 * S + 5) * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     volatile int *last_flag = reinterpret_cast<volatile int *>(tmem_slot + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned long long *trace = p.trace ? p.trace + blockIdx.x * kDecodeTraceSlots : nullptr;
+    if (trace && threadIdx.x == 0) trace[0] = global_timer_ns();
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(bar_full + 8 * s, 1);
             mbar_init(bar_empty + 8 * s, 1);
         }
-        mbar_init(bar_acc_full, 1);
-        mbar_init(bar_acc_empty, 4);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(bar_acc_full + 8 * b, 1);
+            mbar_init(bar_acc_empty + 8 * b, 4);
+        }
         mbar_init(bar_drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -117,6 +140,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t tmo = p.ctl.wait_timeout_ns;
     const int64_t it_begin = range_begin(blockIdx.x, p), it_end = range_begin(blockIdx.x + 1, p);
     const int64_t rest_k = p.K >> 6;
+    // Processing order of this CTA's work: its stream-K range [it_begin, it_end) over
+    // the cut tiles — a last tile that is cut (shared with the next CTA) first, then
+    // the range from its start — and then its whole tiles.  The cut tiles are thus
+    // reduced across CTAs early, and a CTA with whole tiles ends on a plain store.
+    // v in [0, n_iters) is the position in that order, iter(v) the k-block.
+    const int64_t sk_len = it_end - it_begin;
+    const int64_t n_iters = sk_len + (int64_t)p.dp_per_cta * p.num_kb;
+    const int64_t dp_first = ((int64_t)p.sk_tiles + (int64_t)blockIdx.x * p.dp_per_cta) * p.num_kb;
+    const int64_t last_tile0 = sk_len ? ((it_end - 1) / p.num_kb) * p.num_kb : 0;
+    const int64_t head =
+        (p.rotate && sk_len && it_end % p.num_kb != 0 && last_tile0 > it_begin) ? it_end - last_tile0 : 0;
+    auto iter = [&](int64_t v) {
+        return v < head ? last_tile0 + v : (v < sk_len ? it_begin + (v - head) : dp_first + (v - sk_len));
+    };
+    // end (exclusive, in k-blocks) of the contiguous piece that k-block `it` belongs to
+    auto piece_end = [&](int64_t it) {
+        if (it >= p.sk_iters) return dp_first + (int64_t)p.dp_per_cta * p.num_kb;
+        return (head && it >= last_tile0) ? it_end : (head ? last_tile0 : it_end);
+    };
 
     // Launched as a programmatic dependent of the previous kernel in the stream:
     // everything above overlapped that kernel's tail.  Warm L2 with this CTA's first
@@ -124,17 +166,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     // previous kernel still makes), then wait for the previous kernel before touching
     // any input or output.
     if (warp == 0 && lane == 0) {
-        for (int64_t it = it_begin; it < it_end && it < it_begin + L::STAGES; it++)
+        for (int64_t v = 0; v < n_iters && v < L::STAGES; v++) {
+            const int64_t it = iter(v);
             tma_prefetch_2d(&tmap_w, (int)(it % p.num_kb) * kBlockKBytes, (int)(it / p.num_kb) * kTileN);
+        }
     }
     grid_dependency_wait();
+    if (trace && threadIdx.x == 0) {
+        trace[1] = global_timer_ns();
+        trace[5] = (unsigned long long)n_iters;
+    }
 
     if (warp == 0) {
         if (elect_one()) {
             const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
             bool ok = true;
             uint32_t issued_mask = 0, issued_parity = 0, i = 0;
-            for (int64_t it = it_begin; it < it_end; it++, i++) {
+            for (int64_t v = 0; v < n_iters; v++, i++) {
+                const int64_t it = iter(v);
                 const int s = i % S;
                 const uint32_t ph = (i / S) & 1;
                 if (!wait_parity(bar_empty + 8 * s, ph ^ 1, tmo, abort_flag)) {
@@ -168,10 +217,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true, any = false;
             uint32_t i = 0;
             int seg = 0;
-            for (int64_t it = it_begin; ok && it < it_end; seg++) {
+            for (; ok && (int64_t)i < n_iters; seg++) {  // i: k-blocks consumed so far
+                int64_t it = iter(i);
                 const int tile = (int)(it / p.num_kb);
-                const int64_t seg_end = min(it_end, (int64_t)(tile + 1) * p.num_kb);
-                if (!wait_parity(bar_acc_empty, (seg & 1) ^ 1, tmo, abort_flag)) {
+                const int64_t seg_end = min(piece_end(it), (int64_t)(tile + 1) * p.num_kb);
+                const uint32_t buf = (uint32_t)(seg & 1), use = (uint32_t)(seg >> 1);
+                const uint32_t d_tmem = tmem_base + buf * MPAD;
+                if (!wait_parity(bar_acc_empty + 8 * buf, (use & 1) ^ 1, tmo, abort_flag)) {
                     report_timeout(abort_flag, p.ctl.status);
                     ok = false;
                     break;
@@ -186,14 +238,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc_fence_after();
+                    if (trace && (i == 0 || (int64_t)i + 1 == n_iters)) trace[i == 0 ? 2 : 3] = global_timer_ns();
                     const int kb = (int)(it % p.num_kb);
                     const int kg = min(kKGroups, p.k_groups - kb * kKGroups);
-                    const uint32_t sf_cols = tmem_base + MPAD + (i & 1) * L::kSfColsPerStage;
+                    const uint32_t sf_cols = tmem_base + L::kSfBase + (i & 1) * L::kSfColsPerStage;
                     for (int j = 0; j < kg; j++) {
                         const uint32_t col = sf_cols + j * 8;
                         tmem_cp_32x128_x4(col, smem_desc(sSfw + s * L::kSfw + j * 512, 16, 128, 0));
                         tmem_cp_32x128_x4(col + 4, smem_desc(sSfx + s * L::kSfx + j * 512, 16, 128, 0));
-                        mma_mxf4nvf4(tmem_base, smem_desc(sW + s * L::kW + j * 32, 16, 1024, 2),
+                        mma_mxf4nvf4(d_tmem, smem_desc(sW + s * L::kW + j * 32, 16, 1024, 2),
                                      smem_desc(sX + s * L::kX + j * 32, 16, 1024, 2), idesc, col, col + 4,
                                      !(first && j == 0));
                     }
@@ -202,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mma_commit(bar_empty + 8 * s);
                 }
                 if (!ok) break;
-                mma_commit(bar_acc_full);
+                mma_commit(bar_acc_full + 8 * buf);
             }
             if (!ok && any) {
                 volatile int never = 0;
@@ -216,16 +269,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nl = quarter * 32 + lane;  // row of the weight tile this thread owns
         const int etid = threadIdx.x - 64;   // 0..127
         int seg = 0;
-        for (int64_t it = it_begin; it < it_end; seg++) {
+        for (int64_t v = 0; v < n_iters; seg++) {
+            const int64_t it = iter(v);
             const int tile = (int)(it / p.num_kb);
             const int64_t tile_first = (int64_t)tile * p.num_kb, tile_last = tile_first + p.num_kb - 1;
-            const int64_t seg_end = min(it_end, tile_last + 1);
+            const int64_t seg_end = min(piece_end(it), tile_last + 1);
             const bool whole = (it == tile_first) && (seg_end == tile_last + 1);
+            // partials slot: 0 for the tile the range starts in, 1 for the one it ends in
             const int slot = (it == it_begin) ? 0 : 1;
-            it = seg_end;
+            v += seg_end - it;
 
             bool ok = true;
-            if (lane == 0) ok = wait_parity(bar_acc_full, seg & 1, tmo, abort_flag);
+            const uint32_t buf = (uint32_t)(seg & 1), use = (uint32_t)(seg >> 1);
+            if (lane == 0) ok = wait_parity(bar_acc_full + 8 * buf, use & 1, tmo, abort_flag);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) {
                 if (lane == 0) report_timeout(abort_flag, p.ctl.status);
@@ -233,11 +289,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_fence_after();
             uint32_t acc[MPAD];
-            tmem_ld_cols<MPAD>(tmem_base + ((uint32_t)(quarter * 32) << 16), acc);
+            tmem_ld_cols<MPAD>(tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * MPAD, acc);
             tmem_ld_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bar_acc_empty);
+            if (lane == 0) mbar_arrive(bar_acc_empty + 8 * buf);
 
             const int n = tile * kTileN + nl;
             float sum[MPAD];
@@ -249,13 +305,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float *mine = p.partials + ((int64_t)blockIdx.x * 2 + slot) * MPAD * kTileN;
 #pragma unroll
                 for (int m = 0; m < MPAD; m++) __stcg(mine + m * kTileN + nl, __uint_as_float(acc[m]));
-                __threadfence();
+                // The barrier orders every epilogue thread's partial stores before thread
+                // 0's release-acquire increment, which publishes them to the other
+                // contributors and, for the last one, orders their partials before the
+                // loads that follow the second barrier: one L2 round trip instead of a
+                // fence per thread plus the atomic.
                 named_barrier(1, 128);
                 if (etid == 0) {
                     const int c_lo = owner_of(tile_first, p), c_hi = owner_of(tile_last, p);
-                    const int prev = atomicAdd(p.counters + tile, 1);
+                    const int prev = atomic_add_acq_rel_gpu(p.counters + tile, 1);
                     *last_flag = (prev + 1 == c_hi - c_lo + 1);
-                    __threadfence();
                 }
                 named_barrier(1, 128);
                 if (!*last_flag) continue;
@@ -326,6 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem_base, L::kTmemCols);
     }
+    if (trace && threadIdx.x == 0) trace[4] = global_timer_ns();
 }
 
 int mpad_for(int M) {
@@ -341,10 +401,20 @@ size_t workspace_bytes(int M, int N, int sm_count) {
     return counters + (size_t)sm_count * 2 * mpad * kTileN * sizeof(float);
 }
 
+// Rotation of the stream-K range (cut last tile first): on by default when the CTA
+// also owns whole tiles; NVFP4_DECODE_ROTATE=0|1 forces it.
+static int decode_rotate(int dp_per_cta) {
+    static int forced = [] {
+        const char *e = std::getenv("NVFP4_DECODE_ROTATE");
+        return e ? (std::atoi(e) ? 1 : 0) : -1;
+    }();
+    return forced >= 0 ? forced : (dp_per_cta > 0 ? 1 : 0);
+}
+
 template <int MPAD>
 static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                   uint16_t *D, int M, int N, int K, void *ws, cudaStream_t stream, const DeviceInfo &di,
-                  const Epi &epi) {
+                  const Epi &epi, unsigned long long *trace = nullptr) {
     using L = Layout<MPAD>;
     auto kern = nvfp4_decode_kernel<MPAD>;
     static int configured[64] = {};
@@ -370,10 +440,15 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     p.k_groups = K / 64;
     p.total_iters = (int64_t)p.n_tiles * p.num_kb;
     p.grid = (int)std::min<int64_t>(di.sm_count, p.total_iters);
+    p.dp_per_cta = p.n_tiles / p.grid;  // whole tiles per CTA (0 when tiles are fewer than CTAs)
+    p.sk_tiles = p.n_tiles - p.dp_per_cta * p.grid;
+    p.sk_iters = (int64_t)p.sk_tiles * p.num_kb;
+    p.rotate = decode_rotate(p.dp_per_cta);
     const size_t counters = ((size_t)p.n_tiles * sizeof(int) + 255) / 256 * 256;
     p.counters = static_cast<int *>(ws);
     p.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + counters);
     p.epi = epi;
+    p.trace = trace;
     if ((st = kernel_ctl(&p.ctl))) return st;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -420,6 +495,27 @@ int decode_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, cons
         case 32: return decode::launch<32>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi);
         case 64: return decode::launch<64>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi);
         default: return decode::launch<128>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi);
+    }
+}
+
+// Decode GEMM with per-CTA %globaltimer stamps (trace: grid x kDecodeTraceSlots u64,
+// grid = min(#SMs, tiles x k-blocks)); a diagnostic of the launch timeline.
+int decode_trace_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                          uint16_t *D, int M, int N, int K, void *ws, size_t ws_bytes, unsigned long long *trace,
+                          cudaStream_t stream) {
+    int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
+    if (st) return st;
+    if (M > 128 || !trace) return M > 128 ? NVFP4_ERR_SHAPE : NVFP4_ERR_INVALID;
+    DeviceInfo di;
+    if ((st = device_info(&di))) return st;
+    if (!ws || ws_bytes < decode::workspace_bytes(M, N, di.sm_count) || (reinterpret_cast<uintptr_t>(ws) & 255u))
+        return NVFP4_ERR_WORKSPACE;
+    switch (decode::mpad_for(M)) {
+        case 8: return decode::launch<8>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, Epi(), trace);
+        case 16: return decode::launch<16>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, Epi(), trace);
+        case 32: return decode::launch<32>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, Epi(), trace);
+        case 64: return decode::launch<64>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, Epi(), trace);
+        default: return decode::launch<128>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, Epi(), trace);
     }
 }
 

@@ -317,6 +317,13 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[COLS]
     }
 }
 
+// Atomic add with release-acquire semantics at GPU scope; returns the old value.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int *p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 // Named barrier over `count` threads (a multiple of 32) of the CTA.
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

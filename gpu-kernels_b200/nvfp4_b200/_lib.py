@@ -48,6 +48,8 @@ SIGNATURES = {
     "nvfp4_gemm_host": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp]),
     "nvfp4_gemm_decode_noalloc": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int,
                                             _vp]),
+    "nvfp4_gemm_decode_trace": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int,
+                                          _vp, C.c_size_t, _vp, _vp]),
     "nvfp4_probe_mma_rate": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
 }
 

@@ -2,6 +2,7 @@
 
     python -m nvfp4_b200.diag probe [iters]        measured mxf4nvf4 tensor rate per issue mode
     python -m nvfp4_b200.diag trace M N K [reps]    per-CTA cycle breakdown of the CTA-pair GEMM (last of reps)
+    python -m nvfp4_b200.diag decode M N K          timeline of back-to-back decode GEMMs (graph replay)
 
 (run with gpu-kernels_b200/ on sys.path).  Each prints JSON lines.
 """
@@ -83,7 +84,86 @@ def trace(M: int, N: int, K: int, reps: int = 3):
     return res
 
 
+def decode_trace(M: int, N: int, K: int, calls: int = 8, sets: int = 3):
+    """Timeline of `calls` back-to-back decode GEMMs replayed from a CUDA graph (weights
+    rotating over `sets` copies, as in bench.py's decode section), from the kernel's
+    per-CTA %globaltimer stamps.  Per call, in us: gap from the previous call's last
+    CTA exit to this call's wait release, first data after release, streaming span,
+    tail (last data to last exit), and the call's period."""
+    from ._lib import lib as _l
+    from .ops import create_tensors
+    dev = torch.device("cuda", 0)
+    ops = [create_tensors(M, N, K, seed=10 + i) for i in range(sets)]
+    d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    ws_bytes = _l().nvfp4_gemm_decode_workspace_size(M, N)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+    grid = 148
+    tr = torch.zeros(calls, grid * 6, dtype=torch.int64, device=dev)
+    s = torch.cuda.Stream()
+
+    def launch(c):
+        a, b, sfa, sfb = ops[c % sets]
+        check(_l().nvfp4_gemm_decode_trace(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), 1.0,
+                                           d.data_ptr(), M, N, K, ws.data_ptr(), ws_bytes, tr[c].data_ptr(),
+                                           s.cuda_stream), "decode trace")
+
+    with torch.cuda.stream(s):
+        for c in range(calls):
+            launch(c)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for c in range(calls):
+                launch(c)
+    g.replay()
+    torch.cuda.synchronize()
+    tr.zero_()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    g.replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    del g
+    t = tr.view(calls, grid, 6).cpu()
+    used = t[0, :, 0] > 0
+    t = t[:, used]
+    t0 = int(t[0, :, 0].min())
+    us = lambda x: round(float(x) / 1e3, 2)  # noqa: E731
+    rows = []
+    for c in range(calls):
+        tc = t[c]
+        row = {"call": c, "entry_first": us(tc[:, 0].min() - t0), "release_first": us(tc[:, 1].min() - t0),
+               "release_last": us(tc[:, 1].max() - t0), "first_data_first": us(tc[:, 2].min() - t0),
+               "first_data_last": us(tc[:, 2].max() - t0), "last_data_first": us(tc[:, 3].min() - t0),
+               "last_data_last": us(tc[:, 3].max() - t0), "exit_last": us(tc[:, 4].max() - t0)}
+        if c:
+            row["gap_prev_exit_to_release"] = us(tc[:, 1].min() - t[c - 1, :, 4].max())
+            row["period"] = us(tc[:, 4].max() - t[c - 1, :, 4].max())
+        rows.append(row)
+    iters = t[0, :, 5]
+    # per-CTA phases of one steady-state call, as percentiles over CTAs (us)
+    c = t[calls // 2].double()
+    q = torch.tensor([0.0, 0.1, 0.5, 0.9, 1.0], dtype=torch.float64)
+    pct = lambda x: [round(v, 2) for v in (torch.quantile(x, q) / 1e3).tolist()]  # noqa: E731
+    per_cta = {"percentiles": [0, 10, 50, 90, 100],
+               "release_to_first_data": pct(c[:, 2] - c[:, 1]),
+               "first_to_last_data": pct(c[:, 3] - c[:, 2]),
+               "last_data_to_exit": pct(c[:, 4] - c[:, 3]),
+               "entry_to_release": pct(c[:, 1] - c[:, 0]),
+               "release_after_first_release": pct(c[:, 1] - c[:, 1].min()),
+               "exit_after_first_exit": pct(c[:, 4] - c[:, 4].min())}
+    tail = ((c[:, 4] - c[:, 3]) / 1e3).tolist()
+    slow = [i for i, x in enumerate(tail) if x > 2.0]
+    per_cta["slow_tail_ctas"] = slow
+    return {"M": M, "N": N, "K": K, "ctas": int(used.sum()), "iters_per_cta": [int(iters.min()), int(iters.max())],
+            "graph_us_per_call": e0.elapsed_time(e1) * 1e3 / calls, "per_cta": per_cta, "calls": rows}
+
+
 def main(argv):
+    if argv and argv[0] == "decode":
+        M, N, K = (int(x) for x in argv[1:4])
+        print(json.dumps(decode_trace(M, N, K)))
+        return 0
     if not argv or argv[0] not in ("probe", "trace"):
         print(__doc__)
         return 2

@@ -268,6 +268,13 @@ NVFP4_API int nvfp4_gemm_decode_noalloc(const uint8_t *A, const uint8_t *SFA, co
 NVFP4_API int nvfp4_gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
                float alpha, uint16_t *D, int M, int N, int K, uint64_t *trace, void *stream);
 NVFP4_API int nvfp4_probe_mma_rate(int mode, int iters, double *tflops, double *cycles_per_mma);
+/* nvfp4_gemm_decode with per-CTA %globaltimer stamps in `trace` (device, grid x 6
+ * uint64, grid = min(#SMs, ceil(N/128) * ceil(K/256))): [0] CTA entry, [1] release of
+ * the wait on the preceding kernel, [2] first and [3] last ring slot reaching the
+ * MMA thread, [4] CTA exit, [5] k-block iterations of the CTA. */
+NVFP4_API int nvfp4_gemm_decode_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+                                      float alpha, uint16_t *D, int M, int N, int K, void *workspace,
+                                      size_t workspace_bytes, uint64_t *trace, void *stream);
 
 /* Number of kernel launches this library has issued in this process. */
 NVFP4_API uint64_t nvfp4_launch_count(void);
