@@ -327,6 +327,7 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     p.k_groups = K / 64;
     p.vec32_store = ((reinterpret_cast<uintptr_t>(D) & 31u) == 0) && (N % 16 == 0);
     p.trace = nullptr;
+    p.group_m = kGroupM;
     p.epi = epi;
     if ((st = kernel_ctl(&p.ctl))) return st;
     const int grid = p.num_tiles < di.sm_count ? p.num_tiles : di.sm_count;
