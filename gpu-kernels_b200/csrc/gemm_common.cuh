@@ -47,6 +47,7 @@ struct Params {
     // [11] at the last accumulator commit
     unsigned long long *trace;
     int group_m;  // pair kernel: 256-row tile rows per raster group
+    int clc;      // pair kernel: tiles handed out by cluster launch control (else static persistent)
     Epi epi;      // fused epilogue (plain: alpha and bf16/fp16 rounding only)
     Grouped grouped;
 };

@@ -66,6 +66,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with cluster-scope acquire: for barriers that another CTA of the cluster
+// arrives on after writing this CTA's shared memory.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool wait_parity_cluster(uint32_t bar, uint32_t parity, uint64_t timeout_ns,
+                                                    volatile int *abort);
+
 // Bounded wait for the phase with the given parity to complete.  Returns false
 // when `timeout_ns` elapsed first or when *abort (a shared-memory flag raised by
 // another role of the same CTA) became non-zero.
@@ -75,6 +92,17 @@ __device__ __forceinline__ bool wait_parity(uint32_t bar, uint32_t parity, uint6
     const uint64_t t0 = global_timer_ns();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if (global_timer_ns() - t0 > timeout_ns) return false;
+    }
+}
+
+__device__ __forceinline__ bool wait_parity_cluster(uint32_t bar, uint32_t parity, uint64_t timeout_ns,
+                                                    volatile int *abort) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
         if (*abort) return false;
         if (global_timer_ns() - t0 > timeout_ns) return false;
     }
@@ -408,6 +436,38 @@ __device__ __forceinline__ void st_global_v8(void *p, const uint32_t (&v)[8]) {
     asm volatile("st.global.L1::no_allocate.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]),
                  "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
                  : "memory");
+}
+
+// Cluster launch control: ask the hardware to cancel one not-yet-launched cluster of
+// this grid; the 16-byte response lands in this CTA's shared memory `resp` and
+// completes 16 transaction bytes on `bar`.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+    asm volatile("clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(
+                     resp),
+                 "r"(bar)
+                 : "memory");
+}
+
+// Decode a try_cancel response: true and the canceled cluster's first CTA x index, or
+// false when no cluster was left to cancel.
+__device__ __forceinline__ bool clc_query(uint32_t resp, uint32_t &ctaid_x) {
+    uint32_t ok, x;
+    asm volatile(
+        "{\n\t.reg .b128 r;\n\t.reg .pred p;\n\t"
+        "ld.shared.b128 r, [%2];\n\t"
+        "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t"
+        "clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, r;\n\t}"
+        : "=r"(ok), "=r"(x)
+        : "r"(resp)
+        : "memory");
+    ctaid_x = x;
+    return ok != 0;
+}
+
+// Store to shared memory of a CTA of the cluster (address from map_to_cta).
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {

@@ -153,12 +153,17 @@ def test_c2_full_size_sampled(nv, oracle, cuda_dev, N, K):
     ("pair", "6x128n192", (520, 776, 1344)),
     # 16 x 22 tiles of 256x192 over 74 pairs: each TMEM accumulator is reused 2-3 times
     ("pair", "6x128n192", (4096, 4224, 512)),
+    # cluster launch control: one cluster per tile, running clusters cancel the rest
+    ("pair", "5x128/clc", (520, 776, 1344)),
+    ("pair", "5x128/clc", (4096, 4224, 512)),
+    ("pair", "6x128n192/clc", (4096, 4224, 512)),
 ])
 def test_forced_kernel_variant(variant, ring, shape, tmp_path):
     """The persistent kernels (single-CTA 128x256 tiles; CTA-pair 256x256 tiles with
     both ring shapes; CTA-pair 256x192 tiles with two accumulators, whose odd column
-    tiles read shifted B-scale columns) on ragged shapes, each forced through
-    NVFP4_GEMM_VARIANT / NVFP4_PAIR_RING in a fresh process."""
+    tiles read shifted B-scale columns; static persistent or cluster-launch-control
+    tile scheduling) on ragged shapes, each forced through NVFP4_GEMM_VARIANT /
+    NVFP4_PAIR_RING / NVFP4_PAIR_SCHED in a fresh process."""
     import os
     import subprocess
     import sys
@@ -182,6 +187,7 @@ err = np.abs(got - ref).max() / np.abs(ref).max()
 assert err <= 1e-2, err
 print("ok", err)
 """
-    env = dict(os.environ, NVFP4_GEMM_VARIANT=variant, NVFP4_PAIR_RING=ring)
+    ring, _, sched = ring.partition("/")
+    env = dict(os.environ, NVFP4_GEMM_VARIANT=variant, NVFP4_PAIR_RING=ring, NVFP4_PAIR_SCHED=sched or "static")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
