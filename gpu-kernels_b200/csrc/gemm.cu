@@ -254,27 +254,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 struct MapKey {
     int device;
+    int kind;  // 0: NVFP4 operand, 1: 16-bit output D
     const void *ptr;
-    int64_t rows, kbytes;
+    int64_t rows, row_bytes;
     int box_rows, box_bytes;
     bool operator==(const MapKey &o) const {
-        return device == o.device && ptr == o.ptr && rows == o.rows && kbytes == o.kbytes && box_rows == o.box_rows &&
-               box_bytes == o.box_bytes;
+        return device == o.device && kind == o.kind && ptr == o.ptr && rows == o.rows && row_bytes == o.row_bytes &&
+               box_rows == o.box_rows && box_bytes == o.box_bytes;
     }
 };
 
-// Small LRU of encoded operand tensor maps (the reference re-encodes on every
-// call, nvfp4_v5.cu:294-308).  Thread-safe.
-int operand_map(const void *ptr, int64_t rows, int64_t K, int box_rows, int box_bytes, CUtensorMap *out) {
+// Small LRU of encoded tensor maps (the reference re-encodes on every call,
+// nvfp4_v5.cu:294-308).  Thread-safe.
+static int cached_map(const MapKey &key, CUtensorMapDataType dtype, uint64_t inner, CUtensorMapSwizzle swizzle,
+                      uint32_t box_inner, CUtensorMap *out) {
     static std::mutex mu;
     constexpr int kCap = 64;
     static MapKey keys[kCap];
     static CUtensorMap maps[kCap];
     static uint64_t stamp[kCap];
     static uint64_t clock = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    MapKey key{dev, ptr, rows, K / 2, box_rows, box_bytes};
     std::lock_guard<std::mutex> lock(mu);
     int victim = 0;
     for (int i = 0; i < kCap; i++) {
@@ -286,15 +285,31 @@ int operand_map(const void *ptr, int64_t rows, int64_t K, int box_rows, int box_
         if (stamp[i] < stamp[victim]) victim = i;
     }
     CUtensorMap m;
-    int st = encode_tiled_2d(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, ptr, (uint64_t)(K / 2), (uint64_t)rows,
-                             (uint64_t)(K / 2), (uint32_t)box_bytes, (uint32_t)box_rows,
-                             box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+    int st = encode_tiled_2d(&m, dtype, key.ptr, inner, (uint64_t)key.rows, (uint64_t)key.row_bytes, box_inner,
+                             (uint32_t)key.box_rows, swizzle);
     if (st) return st;
     keys[victim] = key;
     maps[victim] = m;
     stamp[victim] = ++clock;
     *out = m;
     return NVFP4_OK;
+}
+
+int operand_map(const void *ptr, int64_t rows, int64_t K, int box_rows, int box_bytes, CUtensorMap *out) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const MapKey key{dev, 0, ptr, rows, K / 2, box_rows, box_bytes};
+    return cached_map(key, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)(K / 2),
+                      box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, (uint32_t)box_bytes,
+                      out);
+}
+
+// Store map of a 16-bit [M, N] output: boxes of 16 columns x box_rows rows, 32-byte swizzle.
+int output_map(const void *ptr, int64_t M, int64_t N, int box_rows, CUtensorMap *out) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const MapKey key{dev, 1, ptr, M, N * 2, box_rows, 32};
+    return cached_map(key, CU_TENSOR_MAP_DATA_TYPE_UINT16, (uint64_t)N, CU_TENSOR_MAP_SWIZZLE_32B, 16u, out);
 }
 
 template <int BN, int STAGES, bool F16>
@@ -328,6 +343,8 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     p.vec32_store = ((reinterpret_cast<uintptr_t>(D) & 31u) == 0) && (N % 16 == 0);
     p.trace = nullptr;
     p.group_m = kGroupM;
+    p.clc = 0;
+    p.tma_store = 0;
     p.epi = epi;
     if ((st = kernel_ctl(&p.ctl))) return st;
     const int grid = p.num_tiles < di.sm_count ? p.num_tiles : di.sm_count;

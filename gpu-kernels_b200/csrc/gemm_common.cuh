@@ -48,6 +48,7 @@ struct Params {
     unsigned long long *trace;
     int group_m;  // pair kernel: 256-row tile rows per raster group
     int clc;      // pair kernel: tiles handed out by cluster launch control (else static persistent)
+    int tma_store;  // pair kernel: plain D stored through shared memory by TMA (else direct stores)
     Epi epi;      // fused epilogue (plain: alpha and bf16/fp16 rounding only)
     Grouped grouped;
 };
@@ -186,6 +187,9 @@ __device__ __forceinline__ uint2 load_bias_lane(const Epi &e, int N, int col0, i
 // Encoded (and cached) 2-D tensor map over an NVFP4 operand [rows, K/2] bytes with a
 // box of `box_bytes` x `box_rows` and the matching shared-memory swizzle.
 int operand_map(const void *ptr, int64_t rows, int64_t K, int box_rows, int box_bytes, CUtensorMap *out);
+// Encoded (and cached) store map over a 16-bit [M, N] output with boxes of 16 columns x
+// box_rows rows and the 32-byte swizzle.
+int output_map(const void *ptr, int64_t M, int64_t N, int box_rows, CUtensorMap *out);
 
 }  // namespace gemm
 }  // namespace nvfp4

@@ -59,7 +59,13 @@ struct PairLayout {
     // with full / empty barriers
     static constexpr int kOffSched = (kOffGroups + kGroupBytes + 127) / 128 * 128;
     static constexpr int kSchedBytes = 16 + 8 + kTileQ * (4 + 8 + 8) + 8;
-    static constexpr int kDynamicSmem = kOffSched + kSchedBytes + 1024;
+    // epilogue staging for TMA stores of D: per epilogue warp two 1 KB boxes of 32 rows x
+    // 16 16-bit columns (32-byte swizzle), where the shared-memory budget allows it
+    static constexpr int kStageBox = 32 * 32;
+    static constexpr int kStageNeed = kEpiWarps * 2 * kStageBox;
+    static constexpr int kOffStage = (kOffSched + kSchedBytes + 1023) / 1024 * 1024;
+    static constexpr bool kHasStage = kOffStage + kStageNeed + 1024 <= 232448;
+    static constexpr int kDynamicSmem = (kHasStage ? kOffStage + kStageNeed : kOffSched + kSchedBytes) + 1024;
     static constexpr uint32_t kTxBytes = 2u * kStage;    // both CTAs complete on the leader's barrier
     // shared-memory matrix descriptor: 128B or 64B swizzle, 8-row core groups
     static constexpr uint32_t kLayout = BKB == 128 ? 2 : 4;
@@ -104,7 +110,7 @@ template <int STAGES, int BKB, int BN, bool F16, bool TRACE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     nvfp4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                            const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
-                           const Params p) {
+                           const __grid_constant__ CUtensorMap tmap_d, const Params p) {
     using L = PairLayout<STAGES, BKB, BN>;
     constexpr int KG = L::kKG;
     extern __shared__ uint8_t smem_raw[];
@@ -160,6 +166,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         prefetch_tmap(&tmap_b);
         prefetch_tmap(&tmap_sfa);
         prefetch_tmap(&tmap_sfb);
+        if (p.tma_store) prefetch_tmap(&tmap_d);
     }
     if (warp == 1) {
         tmem_alloc_pair(smem_u32(tmem_slot), L::kTmemCols);
@@ -465,6 +472,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         constexpr int kCols = BN / 2;
         const uint32_t lead_acc_empty = map_to_cta(bar_acc_empty, 0);
         int local = 0;
+        uint32_t chunk = 0;  // TMA-store boxes issued by this warp (two staging boxes alternate)
         long long t_accw = 0, t_store = 0, c_ready = 0;
         for (int k = 0;; k++, local++) {
             bool okq = true;
@@ -498,16 +506,59 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(lead_acc_empty + 8 * buf);
             const int row = ti.a_row0 + (int)rank * 128 + quarter * 32 + lane, col0 = ti.tn * BN + half * kCols;
-            if (p.epi.plain())
-                store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha);
-            else
-                store_row_epi<kCols>(acc, p, row, col0, ti.row_end, ti.alpha, load_bias_lane(p.epi, p.N, col0, lane));
+            if constexpr (L::kHasStage) {
+                if (p.tma_store) {
+                    // 16 columns at a time: convert, write this lane's row of the warp's
+                    // staging box (32-byte swizzle: the 16-byte halves of rows 4-7 of
+                    // each group of 8 swap places, so a warp's writes hit every bank
+                    // once), then one TMA store of the 32 x 16 box; the box rows and
+                    // columns outside D are clipped by the tensor map
+                    const uint32_t my_stage = base + L::kOffStage + (uint32_t)(warp - 2) * 2u * L::kStageBox;
+                    const int row0 = ti.a_row0 + (int)rank * 128 + quarter * 32;
+                    const uint32_t sw = ((uint32_t)lane >> 2) & 1u;
+#pragma unroll
+                    for (int c = 0; c < kCols / 16; c++, chunk++) {
+                        const uint32_t box = my_stage + (chunk & 1u) * L::kStageBox;
+                        if (chunk >= 2) {  // this box's previous store has finished reading it
+                            if (lane == 0) bulk_wait_group_read<1>();
+                            __syncwarp();
+                        }
+                        uint32_t w[8];
+#pragma unroll
+                        for (int i = 0; i < 8; i++)
+                            w[i] = pack2(__uint_as_float(acc[c * 16 + 2 * i]) * ti.alpha,
+                                         __uint_as_float(acc[c * 16 + 2 * i + 1]) * ti.alpha, F16);
+                        const uint32_t rowaddr = box + (uint32_t)lane * 32u;
+                        st_shared_v4(rowaddr + 16u * sw, w[0], w[1], w[2], w[3]);
+                        st_shared_v4(rowaddr + 16u * (sw ^ 1u), w[4], w[5], w[6], w[7]);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&tmap_d, box, col0 + c * 16, row0);
+                            bulk_commit_group();
+                        }
+                    }
+                } else if (p.epi.plain()) {
+                    store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha);
+                } else {
+                    store_row_epi<kCols>(acc, p, row, col0, ti.row_end, ti.alpha,
+                                         load_bias_lane(p.epi, p.N, col0, lane));
+                }
+            } else {
+                if (p.epi.plain())
+                    store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha);
+                else
+                    store_row_epi<kCols>(acc, p, row, col0, ti.row_end, ti.alpha,
+                                         load_bias_lane(p.epi, p.N, col0, lane));
+            }
             if (TRACE && warp == 2 && lane == 0) t_store += clock64() - c_ready;
         }
         if (TRACE && warp == 2 && lane == 0) {
             p.trace[blockIdx.x * kTraceSlots + 3] = t_accw;
             p.trace[blockIdx.x * kTraceSlots + 4] = t_store;
         }
+        if (p.tma_store && lane == 0) bulk_wait_group<0>();  // stores done before the staging memory goes
+        __syncwarp();
     }
 
     __syncwarp();
@@ -519,6 +570,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         tmem_dealloc_pair(tmem_base, L::kTmemCols);
     }
     if (TRACE && threadIdx.x == 0) p.trace[blockIdx.x * kTraceSlots + 9] = global_timer_ns();
+}
+
+// Epilogue stores of the pair kernel: through shared memory with TMA (1) or direct
+// 32-byte stores from registers (0, the default); env NVFP4_PAIR_TMA_STORE=0|1
+// overrides.  Measured at M=N=K=8192: TMA stores 199.5 us, direct stores 198.3 us —
+// the epilogue runs in the shadow of the next tile's MMAs either way, and the box
+// stores add a shared-memory round trip per 16 columns.
+static int pair_tma_store() {
+    static int v = [] {
+        const char *e = std::getenv("NVFP4_PAIR_TMA_STORE");
+        return e ? (std::atoi(e) ? 1 : 0) : 0;
+    }();
+    return v;
 }
 
 // Tile scheduler of the pair kernel: static persistent (0) or cluster launch control
@@ -564,7 +628,8 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     }
     const int G = grp.groups;
     const int64_t b_rows = G > 0 ? (int64_t)G * N : N;
-    CUtensorMap ta, tb, tsa, tsb;
+    CUtensorMap ta, tb, tsa, tsb, td;
+    std::memset(&td, 0, sizeof(td));
     int st = operand_map(A, M, K, 128, BKB, &ta);
     if (!st) st = operand_map(B, b_rows, K, L::kBRows, BKB, &tb);
     // scale tensors as [bytes/256, 256]: one (128-row block, 64-K group) chunk is two rows
@@ -596,11 +661,16 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     p.clc = pair_clc();
     p.epi = epi;
     p.grouped = grp;
+    // TMA stores of D only for a plain output whose tiles lie inside one matrix (a
+    // grouped tile can reach into the next group's rows, which a box store would clip
+    // to D's extent but not to the group)
+    p.tma_store = (L::kHasStage && epi.plain() && G == 0 && pair_tma_store()) ? 1 : 0;
+    if (p.tma_store && (st = output_map(D, M, N, 32, &td))) return st;
     if ((st = kernel_ctl(&p.ctl))) return st;
     // static: one persistent cluster per SM pair; cluster launch control: one cluster
     // per tile, the running ones cancelling the rest as they finish
     const int pairs = p.clc ? p.num_tiles : std::min(p.num_tiles, di.sm_count / 2);
-    kern<<<2 * pairs, kPairThreads, L::kDynamicSmem, stream>>>(ta, tb, tsa, tsb, p);
+    kern<<<2 * pairs, kPairThreads, L::kDynamicSmem, stream>>>(ta, tb, tsa, tsb, td, p);
     count_launch();
     return cuda_status(cudaGetLastError());
 }

@@ -157,6 +157,10 @@ def test_c2_full_size_sampled(nv, oracle, cuda_dev, N, K):
     ("pair", "5x128/clc", (520, 776, 1344)),
     ("pair", "5x128/clc", (4096, 4224, 512)),
     ("pair", "6x128n192/clc", (4096, 4224, 512)),
+    # D stored through shared memory by TMA instead of direct 32-byte stores
+    ("pair", "5x128/static/tma", (520, 776, 1344)),
+    ("pair", "5x128/static/tma", (4096, 4224, 512)),
+    ("pair", "6x128n192/static/tma", (4096, 4224, 512)),
 ])
 def test_forced_kernel_variant(variant, ring, shape, tmp_path):
     """The persistent kernels (single-CTA 128x256 tiles; CTA-pair 256x256 tiles with
@@ -187,7 +191,9 @@ err = np.abs(got - ref).max() / np.abs(ref).max()
 assert err <= 1e-2, err
 print("ok", err)
 """
-    ring, _, sched = ring.partition("/")
-    env = dict(os.environ, NVFP4_GEMM_VARIANT=variant, NVFP4_PAIR_RING=ring, NVFP4_PAIR_SCHED=sched or "static")
+    ring, _, rest = ring.partition("/")
+    sched, _, store = rest.partition("/")
+    env = dict(os.environ, NVFP4_GEMM_VARIANT=variant, NVFP4_PAIR_RING=ring, NVFP4_PAIR_SCHED=sched or "static",
+               NVFP4_PAIR_TMA_STORE="1" if store == "tma" else "0")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
