@@ -49,6 +49,7 @@ struct Params {
     int group_m;  // pair kernel: 256-row tile rows per raster group
     int clc;      // pair kernel: tiles handed out by cluster launch control (else static persistent)
     int tma_store;  // pair kernel: plain D stored through shared memory by TMA (else direct stores)
+    int spin;       // pair kernel: MMA thread and epilogue poll their barriers (test_wait)
     Epi epi;      // fused epilogue (plain: alpha and bf16/fp16 rounding only)
     Grouped grouped;
 };

@@ -259,7 +259,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                           ysb1 = (sb + 1) * rest_k * 2;
                 for (int kb = 0; kb < p.num_kb; kb++) {
                     const long long c0 = TRACE ? clock64() : 0;
-                    if (!mbar_try_wait(emp, phase ^ 1) && !wait_parity(emp, phase ^ 1, tmo, abort_flag)) {
+                    if (!(p.spin >= 2 ? spin_parity(emp, phase ^ 1, tmo, abort_flag)
+                                      : (mbar_try_wait(emp, phase ^ 1) || wait_parity(emp, phase ^ 1, tmo, abort_flag)))) {
                         report_timeout(abort_flag, p.ctl.status);
                         ok = false;
                         break;
@@ -365,7 +366,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 const uint32_t d_tmem = tmem_base + buf * BN;
                 const uint32_t sfb_shift = (uint32_t)(((tn * BN) & 127) >> 5);
                 long long c0 = TRACE ? clock64() : 0;
-                if (!wait_parity(bar_acc_empty + 8 * buf, (use & 1) ^ 1, tmo, abort_flag)) {
+                if (!(p.spin ? spin_parity(bar_acc_empty + 8 * buf, (use & 1) ^ 1, tmo, abort_flag)
+                             : wait_parity(bar_acc_empty + 8 * buf, (use & 1) ^ 1, tmo, abort_flag))) {
                     report_timeout(abort_flag, p.ctl.status);
                     ok = false;
                     break;
@@ -381,7 +383,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 tc_fence_after();
                 for (int kb = 0; kb < p.num_kb; kb++) {
                     if (TRACE) c0 = clock64();
-                    if (!mbar_try_wait(full_bar, phase) && !wait_parity(full_bar, phase, tmo, abort_flag)) {
+                    if (!(p.spin ? spin_parity(full_bar, phase, tmo, abort_flag)
+                                 : (mbar_try_wait(full_bar, phase) || wait_parity(full_bar, phase, tmo, abort_flag)))) {
                         report_timeout(abort_flag, p.ctl.status);
                         ok = false;
                         break;
@@ -485,7 +488,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             const uint32_t use = L::kAccBufs == 2 ? (uint32_t)(local >> 1) : (uint32_t)local;
             bool ok = true;
             const long long c0 = TRACE ? clock64() : 0;
-            if (lane == 0) ok = wait_parity(bar_acc_full + 8 * buf, use & 1, tmo, abort_flag);
+            if (lane == 0)
+                ok = p.spin ? spin_parity(bar_acc_full + 8 * buf, use & 1, tmo, abort_flag)
+                            : wait_parity(bar_acc_full + 8 * buf, use & 1, tmo, abort_flag);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (TRACE) {
                 c_ready = clock64();
@@ -585,6 +590,17 @@ static int pair_tma_store() {
     return v;
 }
 
+// Barrier waits: 0 the suspending try_wait everywhere, 1 polling (test_wait) in the
+// MMA thread and the epilogue, 2 also in the producers; env NVFP4_PAIR_SPIN overrides.
+static int pair_spin() {
+    static int v = [] {
+        const char *e = std::getenv("NVFP4_PAIR_SPIN");
+        const int x = e ? std::atoi(e) : 1;
+        return x < 0 ? 0 : (x > 2 ? 2 : x);
+    }();
+    return v;
+}
+
 // Tile scheduler of the pair kernel: static persistent (0) or cluster launch control
 // (1); env NVFP4_PAIR_SCHED=static|clc overrides.  Measured at M=N=K=8192 on one box:
 // static 203.2 us, cluster launch control 208.2 us (MoE grouped: 232 vs 242 us) —
@@ -665,6 +681,7 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     // grouped tile can reach into the next group's rows, which a box store would clip
     // to D's extent but not to the group)
     p.tma_store = (L::kHasStage && epi.plain() && G == 0 && pair_tma_store()) ? 1 : 0;
+    p.spin = pair_spin();
     if (p.tma_store && (st = output_map(D, M, N, 32, &td))) return st;
     if ((st = kernel_ctl(&p.ctl))) return st;
     // static: one persistent cluster per SM pair; cluster launch control: one cluster

@@ -66,6 +66,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking probe of a phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait that polls with test_wait instead of the suspending try_wait: for
+// waits on the critical path whose wake-up latency matters more than issue slots.
+__device__ __forceinline__ bool spin_parity(uint32_t bar, uint32_t parity, uint64_t timeout_ns,
+                                            volatile int *abort) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1;; i++) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((i & 63) == 0) {
+            if (*abort) return false;
+            if (global_timer_ns() - t0 > timeout_ns) return false;
+        }
+    }
+}
+
 // try_wait with cluster-scope acquire: for barriers that another CTA of the cluster
 // arrives on after writing this CTA's shared memory.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
