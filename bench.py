@@ -533,6 +533,68 @@ def epilogue_section(nv, sets, M, N, K, reps=30):
             "plain_ms": plain, "fused_nvfp4_out_ms": fused, "unfused_ms": two}
 
 
+def gather_section(nv, dev, world, rank, reps=10):
+    """BASELINE configs[3] with the full output requested: prefill FFN up-projection
+    M=16384, N=28672, K=8192, B sharded by 128-row blocks across the ranks.  Per call,
+    max over ranks: the shard GEMM alone; GEMM + NCCL all-gather of the bf16 shards
+    (nvfp4_b200.dist.gather_columns); the gather fused into the GEMM epilogue
+    (nvfp4_b200.dist.FusedGather) with NVLink stores to every rank's buffer, and with
+    one NVLink-multicast store per element where the fabric offers it."""
+    import torch.distributed as dist
+    from nvfp4_b200.dist import FusedGather, gather_columns, shard_bounds, shard_weight
+    M, N, K = 16384, 28672, 8192
+    g = torch.Generator(device=dev).manual_seed(91)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    _, gx = nv.global_scale(x)
+    a, sfa = nv.quantize(x, gx)
+    del x
+    n0, n1 = shard_bounds(N, world, rank)
+    w = (torch.randn(n1 - n0, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    _, gw = nv.global_scale(w)
+    bs, ss = nv.quantize(w, gw)
+    del w
+    alpha = float((gx * gw).item())
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / reps, world)
+
+    d = torch.empty(M, n1 - n0, dtype=torch.bfloat16, device=dev)
+    res = {"what": "prefill FFN M=16384 N=28672 K=8192, N-sharded, full bf16 D on every rank",
+           "full_output_bytes": M * N * 2, "n_gpus": world}
+    res["shard_gemm_ms"] = timed(lambda: nv.gemm(a, sfa, bs, ss, alpha, out=d))
+    res["gemm_plus_nccl_all_gather_ms"] = timed(lambda: gather_columns(nv.gemm(a, sfa, bs, ss, alpha, out=d), N))
+    fg = FusedGather(M, N, dev, multicast=False)
+    res["fused_nvlink_stores_ms"] = timed(lambda: fg.gemm(a, sfa, bs, ss, alpha, n0))
+    del fg
+    try:
+        fm = FusedGather(M, N, dev, multicast=True)
+    except RuntimeError:
+        fm = None
+    ok = [fm is not None]
+    oks = [None] * world
+    dist.all_gather_object(oks, ok[0])
+    if all(oks):
+        res["fused_nvlink_multicast_ms"] = timed(lambda: fm.gemm(a, sfa, bs, ss, alpha, n0))
+    else:
+        res["fused_nvlink_multicast_ms"] = None
+    del fm
+    nv.device_status()
+    flops = 2.0 * M * N * K
+    for k in [k for k in res if k.endswith("_ms") and res[k]]:
+        res[k.replace("_ms", "_tflops")] = flops / (res[k] / 1e3) / 1e12
+    return res
+
+
 def run_decode_workload(args, M, N, K):
     """One skinny-M shape alone (for profiling): weights rotate over 3 sets."""
     import nvfp4_b200 as nv
@@ -680,6 +742,7 @@ def run_ours(args):
         quant = quantize_section(nv, dev, pk)
         moe = moe_section(nv, dev)
         epi = epilogue_section(nv, sets, M, N, K)
+    gath = gather_section(nv, dev, world, rank) if (world > 1 and not args.no_gather) else None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu, _, _ = cpu_reference_sample(a, sfa, b, sfb, alpha, M, N, K, target_s=args.cpu_seconds)
 
@@ -718,6 +781,8 @@ def run_ours(args):
             line["moe_grouped"] = moe
         if epi is not None:
             line["fused_epilogue"] = epi
+        if gath is not None:
+            line["gather"] = gath
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
@@ -735,6 +800,7 @@ def main():
     ap.add_argument("--sets", type=int, default=0, help="operand sets to rotate (default: > 3x L2)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-shape GB/s section")
+    ap.add_argument("--no-gather", action="store_true", help="skip the N>1 all-gather section")
     ap.add_argument("--workload", default="square",
                     help="square (default, the bench line), decode:M:N:K or quantize:M:K (one kernel, for profiling)")
     args = ap.parse_args()

@@ -17,6 +17,9 @@ int sf_pad_zero(uint8_t *SF, int M, int K, cudaStream_t s, const DeviceInfo &di)
 int decode_trace_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                           uint16_t *D, int M, int N, int K, void *ws, size_t ws_bytes, unsigned long long *trace,
                           cudaStream_t stream);
+int gather_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, int M,
+                    int N, int K, const uint64_t *dst, int n_dst, int multicast, int64_t ld, int col_off,
+                    cudaStream_t stream);
 int grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const float *alphas,
                      uint16_t *D, const int *m_offsets, int groups, int m_total, int N, int K, cudaStream_t stream);
 int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
@@ -137,6 +140,13 @@ int nvfp4_gemm_grouped(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
                        uint16_t *D, const int32_t *m_offsets, int groups, int m_total, int N, int K, void *stream) {
     return grouped_dispatch(A, SFA, B, SFB, alpha, D, m_offsets, groups, m_total, N, K,
                             static_cast<cudaStream_t>(stream));
+}
+
+int nvfp4_gemm_gather(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, int M,
+                      int N, int K, const uint64_t *dst, int n_dst, int multicast, int64_t ld, int col_off,
+                      void *stream) {
+    return gather_dispatch(A, SFA, B, SFB, alpha, M, N, K, dst, n_dst, multicast, ld, col_off,
+                           static_cast<cudaStream_t>(stream));
 }
 
 int nvfp4_gemm_persistent(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,

@@ -28,6 +28,19 @@ struct Grouped {
     int m_total = 0;                 // rows of A / D (offsets are clamped to it)
 };
 
+// Column-parallel GEMM with the all-gather fused into the epilogue: this rank's
+// [M, N] output shard is written straight into the full [M, ld] output of every rank
+// at column col_off — through NVLink stores to each rank's buffer, or one multimem
+// store to an NVLink multicast address that the switch delivers to all of them.
+constexpr int kMaxGatherRanks = 8;
+struct Gather {
+    uint64_t dst[kMaxGatherRanks] = {};  // full-D base of each rank, or dst[0] = the multicast address
+    int n_dst = 0;                       // 0: no gather
+    int multicast = 0;
+    int64_t ld = 0;                      // row pitch of the full D in elements
+    int col_off = 0;                     // this rank's first column in the full D
+};
+
 struct Params {
     const uint8_t *sfa;
     const uint8_t *sfb;
@@ -52,6 +65,7 @@ struct Params {
     int spin;       // pair kernel: MMA thread and epilogue poll their barriers (test_wait)
     Epi epi;      // fused epilogue (plain: alpha and bf16/fp16 rounding only)
     Grouped grouped;
+    Gather gather;
 };
 constexpr int kTraceSlots = 12;
 
@@ -174,6 +188,83 @@ __device__ __forceinline__ void store_row_epi(const uint32_t (&acc)[kCols], cons
                 *reinterpret_cast<uint32_t *>(e.sf + sf_group_offset(row, c0 >> 6, rest)) = scales;
             }
         }
+    }
+}
+
+// The gather form of store_row (bf16 output): each 16-column chunk of this row goes
+// to every destination of p.gather (32-byte stores, or two 16-byte multimem stores to
+// the multicast address).  Rows >= row_end and columns >= N are not stored.
+template <int kCols>
+__device__ __forceinline__ void store_row_gather(const uint32_t (&acc)[kCols], const Params &p, int row, int col0,
+                                                 int row_end, float alpha) {
+    if (row >= row_end) return;
+    const Gather &g = p.gather;
+    const int64_t off = ((int64_t)row * g.ld + g.col_off + col0) * 2;
+#pragma unroll
+    for (int c = 0; c < kCols / 16; c++) {
+        if (col0 + c * 16 < p.N) {
+            uint32_t v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                v[i] = pack2(__uint_as_float(acc[c * 16 + 2 * i]) * alpha,
+                             __uint_as_float(acc[c * 16 + 2 * i + 1]) * alpha, false);
+            if (g.multicast) {
+                const uint64_t a = g.dst[0] + off + c * 32;
+                multimem_st_bf16x8(a, v[0], v[1], v[2], v[3]);
+                multimem_st_bf16x8(a + 16, v[4], v[5], v[6], v[7]);
+            } else {
+#pragma unroll
+                for (int d = 0; d < kMaxGatherRanks; d++)
+                    if (d < g.n_dst) st_global_v8(reinterpret_cast<void *>(g.dst[d] + off + c * 32), v);
+            }
+        }
+    }
+}
+
+// Coalesced gather store of one warp's 32 rows x kCols columns (bf16), through the
+// warp's 4 KB of shared memory `stage`: each 64-column chunk is written row by row
+// (lane = row, 16-byte pieces XOR-swizzled by row so the 32 lanes hit every bank
+// once per four rows), then read back four rows per instruction, eight lanes per row,
+// so that every global store instruction writes four 128-byte row segments — to each
+// destination, or once through the multicast address.  Rows >= row_end and columns
+// >= N are not stored.  All 32 lanes call it.
+template <int kCols>
+__device__ __forceinline__ void store_rows_gather_staged(const uint32_t (&acc)[kCols], const Params &p, int row0,
+                                                         int col0, int row_end, float alpha, uint32_t stage,
+                                                         int lane) {
+    static_assert(kCols % 64 == 0, "64-column chunks");
+    const Gather &g = p.gather;
+#pragma unroll
+    for (int h = 0; h < kCols / 64; h++) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int k = h * 64 + j * 8;
+            const uint32_t w0 = pack2(__uint_as_float(acc[k + 0]) * alpha, __uint_as_float(acc[k + 1]) * alpha, false);
+            const uint32_t w1 = pack2(__uint_as_float(acc[k + 2]) * alpha, __uint_as_float(acc[k + 3]) * alpha, false);
+            const uint32_t w2 = pack2(__uint_as_float(acc[k + 4]) * alpha, __uint_as_float(acc[k + 5]) * alpha, false);
+            const uint32_t w3 = pack2(__uint_as_float(acc[k + 6]) * alpha, __uint_as_float(acc[k + 7]) * alpha, false);
+            st_shared_v4(stage + (uint32_t)lane * 128u + 16u * ((uint32_t)j ^ ((uint32_t)lane & 7u)), w0, w1, w2, w3);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int step = 0; step < 8; step++) {
+            const int r = step * 4 + (lane >> 3), j = lane & 7;
+            uint32_t v0, v1, v2, v3;
+            ld_shared_v4(stage + (uint32_t)r * 128u + 16u * ((uint32_t)j ^ ((uint32_t)r & 7u)), v0, v1, v2, v3);
+            const int grow = row0 + r, gcol = col0 + h * 64 + j * 8;
+            if (grow < row_end && gcol < p.N) {
+                const int64_t off = ((int64_t)grow * g.ld + g.col_off + gcol) * 2;
+                if (g.multicast) {
+                    multimem_st_bf16x8(g.dst[0] + off, v0, v1, v2, v3);
+                } else {
+#pragma unroll
+                    for (int d = 0; d < kMaxGatherRanks; d++)
+                        if (d < g.n_dst)
+                            *reinterpret_cast<uint4 *>(g.dst[d] + off) = make_uint4(v0, v1, v2, v3);
+                }
+            }
+        }
+        __syncwarp();
     }
 }
 

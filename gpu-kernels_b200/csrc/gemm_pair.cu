@@ -52,20 +52,24 @@ struct PairLayout {
     static constexpr int kOffSfb = kOffSfa + STAGES * kSfa;
     static constexpr int kOffBar = kOffSfb + STAGES * kSfb;
     static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 16;  // full, empty, acc_full x2, acc_empty x2, drain
-    // grouped GEMM tables: first row, first tile and first A-scale block of each group
-    static constexpr int kOffGroups = kOffBar + kBarBytes;
-    static constexpr int kGroupBytes = 4 * (kMaxGroups + 1) * 4;
     // cluster-launch-control tile queue: response (16 B), its barrier, kTileQ entries
     // with full / empty barriers
-    static constexpr int kOffSched = (kOffGroups + kGroupBytes + 127) / 128 * 128;
+    static constexpr int kOffSched = (kOffBar + kBarBytes + 127) / 128 * 128;
     static constexpr int kSchedBytes = 16 + 8 + kTileQ * (4 + 8 + 8) + 8;
-    // epilogue staging for TMA stores of D: per epilogue warp two 1 KB boxes of 32 rows x
-    // 16 16-bit columns (32-byte swizzle), where the shared-memory budget allows it
+    // One region, two uses that never meet: the grouped GEMM's tables (first row, end
+    // row, first tile and first A-scale block of each group), or the epilogue's staging
+    // — per epilogue warp 4 KB, holding either two 1 KB boxes of 32 rows x 16 16-bit
+    // columns for TMA stores of D (32-byte swizzle) or a 32 x 64 chunk that the gather
+    // epilogue writes out row-contiguously.  Staging only where the budget allows.
+    static constexpr int kGroupBytes = 4 * (kMaxGroups + 1) * 4;
     static constexpr int kStageBox = 32 * 32;
-    static constexpr int kStageNeed = kEpiWarps * 2 * kStageBox;
+    static constexpr int kStageWarp = 4096;
+    static constexpr int kStageNeed = kEpiWarps * kStageWarp;
     static constexpr int kOffStage = (kOffSched + kSchedBytes + 1023) / 1024 * 1024;
+    static constexpr int kOffGroups = kOffStage;
     static constexpr bool kHasStage = kOffStage + kStageNeed + 1024 <= 232448;
-    static constexpr int kDynamicSmem = (kHasStage ? kOffStage + kStageNeed : kOffSched + kSchedBytes) + 1024;
+    static constexpr int kRegion = (kHasStage && kStageNeed > kGroupBytes) ? kStageNeed : kGroupBytes;
+    static constexpr int kDynamicSmem = kOffStage + kRegion + 1024;
     static constexpr uint32_t kTxBytes = 2u * kStage;    // both CTAs complete on the leader's barrier
     // shared-memory matrix descriptor: 128B or 64B swizzle, 8-row core groups
     static constexpr uint32_t kLayout = BKB == 128 ? 2 : 4;
@@ -511,14 +515,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(lead_acc_empty + 8 * buf);
             const int row = ti.a_row0 + (int)rank * 128 + quarter * 32 + lane, col0 = ti.tn * BN + half * kCols;
-            if constexpr (L::kHasStage) {
+            if (p.gather.n_dst > 0) {
+                if constexpr (L::kHasStage && kCols % 64 == 0)
+                    store_rows_gather_staged<kCols>(acc, p, ti.a_row0 + (int)rank * 128 + quarter * 32, col0,
+                                                    ti.row_end, ti.alpha,
+                                                    base + L::kOffStage + (uint32_t)(warp - 2) * L::kStageWarp, lane);
+                else
+                    store_row_gather<kCols>(acc, p, row, col0, ti.row_end, ti.alpha);
+            } else if constexpr (L::kHasStage) {
                 if (p.tma_store) {
                     // 16 columns at a time: convert, write this lane's row of the warp's
                     // staging box (32-byte swizzle: the 16-byte halves of rows 4-7 of
                     // each group of 8 swap places, so a warp's writes hit every bank
                     // once), then one TMA store of the 32 x 16 box; the box rows and
                     // columns outside D are clipped by the tensor map
-                    const uint32_t my_stage = base + L::kOffStage + (uint32_t)(warp - 2) * 2u * L::kStageBox;
+                    const uint32_t my_stage = base + L::kOffStage + (uint32_t)(warp - 2) * L::kStageWarp;
                     const int row0 = ti.a_row0 + (int)rank * 128 + quarter * 32;
                     const uint32_t sw = ((uint32_t)lane >> 2) & 1u;
 #pragma unroll
@@ -563,6 +574,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             p.trace[blockIdx.x * kTraceSlots + 4] = t_store;
         }
         if (p.tma_store && lane == 0) bulk_wait_group<0>();  // stores done before the staging memory goes
+        // the peer / multicast stores of this thread are ordered before whatever follows
+        // the kernel (the cross-rank barrier that publishes the gathered output)
+        if (p.gather.n_dst > 0) __threadfence_system();
         __syncwarp();
     }
 
@@ -631,7 +645,8 @@ static int pair_group_m() {
 template <int STAGES, int BKB, int BN, bool F16>
 static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                        void *D, int M, int N, int K, cudaStream_t stream, const DeviceInfo &di,
-                       unsigned long long *trace, const Epi &epi, const Grouped &grp = Grouped()) {
+                       unsigned long long *trace, const Epi &epi, const Grouped &grp = Grouped(),
+                       const Gather &gat = Gather()) {
     if (epi.q && BN % 128 != 0) return NVFP4_ERR_UNSUPPORTED;  // NVFP4 output wants 64-column aligned halves
     using L = PairLayout<STAGES, BKB, BN>;
     auto kern = trace ? nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, true>
@@ -680,7 +695,8 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     // TMA stores of D only for a plain output whose tiles lie inside one matrix (a
     // grouped tile can reach into the next group's rows, which a box store would clip
     // to D's extent but not to the group)
-    p.tma_store = (L::kHasStage && epi.plain() && G == 0 && pair_tma_store()) ? 1 : 0;
+    p.gather = gat;
+    p.tma_store = (L::kHasStage && epi.plain() && G == 0 && gat.n_dst == 0 && pair_tma_store()) ? 1 : 0;
     p.spin = pair_spin();
     if (p.tma_store && (st = output_map(D, M, N, 32, &td))) return st;
     if ((st = kernel_ctl(&p.ctl))) return st;
@@ -769,6 +785,36 @@ int grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, con
     grp.m_total = m_total;
     return gemm::launch_pair<5, 128, 256, false>(A, SFA, B, SFB, 1.0f, D, m_total, N, K, stream, di, nullptr, Epi(),
                                                  grp);
+}
+
+// Column-parallel GEMM with the all-gather fused into the epilogue (bf16 output):
+// D_shard = alpha * A . B_shard^T is stored into the full [M, ld] output of every rank
+// at column col_off, through each rank's buffer (dst[0..n_dst)) or one multicast
+// address (dst[0], multicast != 0).  The caller orders the ranks afterwards.
+int gather_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, int M,
+                    int N, int K, const uint64_t *dst, int n_dst, int multicast, int64_t ld, int col_off,
+                    cudaStream_t stream) {
+    if (!A || !SFA || !B || !SFB || !dst) return NVFP4_ERR_INVALID;
+    if (M < 1 || N < 16 || N % 16 || K < 64 || K % 64 || n_dst < 1 || n_dst > gemm::kMaxGatherRanks ||
+        (multicast && n_dst != 1) || col_off < 0 || col_off % 16 || ld % 16 || ld < (int64_t)col_off + N)
+        return NVFP4_ERR_SHAPE;
+    if (!aligned16(A) || !aligned16(SFA) || !aligned16(B) || !aligned16(SFB)) return NVFP4_ERR_ALIGN;
+    gemm::Gather g;
+    for (int d = 0; d < n_dst; d++) {
+        if (!dst[d]) return NVFP4_ERR_INVALID;
+        if (dst[d] & 31u) return NVFP4_ERR_ALIGN;
+        g.dst[d] = dst[d];
+    }
+    g.n_dst = n_dst;
+    g.multicast = multicast ? 1 : 0;
+    g.ld = ld;
+    g.col_off = col_off;
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    // D is never written through the shard pointer: dst[0] stands in for validation only
+    return gemm::launch_pair<5, 128, 256, false>(A, SFA, B, SFB, alpha, reinterpret_cast<void *>(dst[0]), M, N, K,
+                                                 stream, di, nullptr, Epi(), gemm::Grouped(), g);
 }
 
 // Pair kernel with the per-CTA cycle trace on (trace: 148 x kTraceSlots u64 on the device).

@@ -498,6 +498,14 @@ __device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uin
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
+// 16 bytes (8 bf16) stored through an NVLink multicast address: the switch writes
+// them to the same offset of every GPU bound to the multicast object.
+__device__ __forceinline__ void multimem_st_bf16x8(uint64_t mc_addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr), "r"(a), "r"(b),
+                 "r"(c), "r"(d)
+                 : "memory");
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
                  : "memory");

@@ -45,6 +45,8 @@ SIGNATURES = {
     "nvfp4_gemm_grouped": (C.c_int, [_u8p, _u8p, _u8p, _u8p, _f32p, _u16p, _vp, C.c_int, C.c_int, C.c_int, C.c_int,
                                      _vp]),
     "nvfp4_quantize_grouped": (C.c_int, [_u16p, _u8p, _u8p, _f32p, _vp, C.c_int, C.c_int, C.c_int, _vp]),
+    "nvfp4_gemm_gather": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, C.c_int, C.c_int, C.c_int,
+                                    C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_int64, C.c_int, _vp]),
     "nvfp4_gemm_host": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp]),
     "nvfp4_gemm_decode_noalloc": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int,
                                             _vp]),

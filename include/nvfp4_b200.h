@@ -183,6 +183,24 @@ NVFP4_API int nvfp4_quantize_grouped(const uint16_t *X, uint8_t *Q, uint8_t *SF,
                                      const int32_t *m_offsets, int groups, int m_total, int K, void *stream);
 
 /*
+ * Column-parallel GEMM with the all-gather of the output fused into the epilogue (no
+ * counterpart in the reference, whose kernels run on one GPU; the multi-GPU plan
+ * gathers the N-shards with NCCL).  This rank computes its shard
+ *     D_shard[M, N] = alpha * A . B_shard^T          (bf16)
+ * and stores it straight into the full [M, ld] bf16 output of every rank at column
+ * col_off: dst holds n_dst device addresses of those full outputs as this process
+ * sees them (peer buffers mapped over NVLink, e.g. symmetric memory), or — with
+ * multicast != 0 — one NVLink multicast address (n_dst = 1) whose stores the switch
+ * delivers to every bound GPU, so each rank sends its shard once.  The call ends when
+ * this rank's stores are issued; the caller orders the ranks before reading the full
+ * output (a cross-rank barrier on the stream).  N, ld and col_off multiples of 16;
+ * destinations 32-byte aligned; the CTA-pair kernel runs for every M.
+ */
+NVFP4_API int nvfp4_gemm_gather(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+                                float alpha, int M, int N, int K, const uint64_t *dst, int n_dst, int multicast,
+                                int64_t ld, int col_off, void *stream);
+
+/*
  * Reference-signature shim: drop-in for matmul_nvfp4_vN in
  * matmul/sm100_nvfp4/runner.cu:61-96 (fp16 D, alpha = 1, legacy default
  * stream, no return value).  The status of the last call is kept for

@@ -78,3 +78,74 @@ def test_column_parallel_nccl_matches_single_gpu(M, N, K):
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert q.get(timeout=5) is True
+
+
+def _rank_fused(rank, world, port, M, N, K, q):
+    """Fused GEMM + all-gather (nvfp4_gemm_gather through symmetric memory): NVLink
+    stores to every rank's buffer first; the NVLink-multicast form only once that
+    matched, and only where the fabric offers a multicast address."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import torch.distributed as dist
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    result = {"unicast": None, "multicast": None}
+    try:
+        nv, a, sfa, b, sfb = _operands(M, N, K, dev)
+        from nvfp4_b200.dist import FusedGather, shard_bounds, shard_weight
+        bs, ss = shard_weight(b, sfb, K, world, rank)
+        n0, _ = shard_bounds(N, world, rank)
+        full = nv.gemm(a, sfa, b, sfb, 0.5)
+        fg = FusedGather(M, N, dev, multicast=False)
+        fg.out.fill_(float("nan"))
+        dist.barrier()
+        d = fg.gemm(a, sfa, bs.contiguous(), ss.contiguous(), 0.5, n0)
+        torch.cuda.synchronize()
+        nv.device_status()
+        ok = bool(torch.equal(d, full))
+        result["unicast"] = ok
+        oks = [None] * world
+        dist.all_gather_object(oks, ok)
+        if all(oks):
+            # multicast when the buffer has a multicast address
+            try:
+                probe = FusedGather(M, N, dev, multicast=True)
+            except RuntimeError:
+                probe = None
+            if probe is not None and probe.multicast:
+                probe.out.fill_(float("nan"))
+                dist.barrier()
+                d2 = probe.gemm(a, sfa, bs.contiguous(), ss.contiguous(), 0.5, n0)
+                torch.cuda.synchronize()
+                nv.device_status()
+                result["multicast"] = bool(torch.equal(d2, full))
+            else:
+                result["multicast"] = "unavailable"
+        if rank == 0:
+            q.put(result)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 3072, 1024), (300, 1280, 2048)])
+def test_fused_gather_matches_single_gpu(M, N, K):
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs at least two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_rank_fused, args=(r, world, port, M, N, K, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = q.get(timeout=5)
+    print("fused gather:", res)
+    assert res["unicast"] is True
+    assert res["multicast"] in (True, "unavailable")
