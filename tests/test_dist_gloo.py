@@ -123,3 +123,25 @@ def test_dead_rank_surfaces_as_error_not_hang():
             p.kill()
     assert procs[1].exitcode == 3
     assert q.get(timeout=5) != "no error"
+
+
+def test_gemm_gather_host_checks(nv):
+    """nvfp4_gemm_gather rejects bad arguments on the host, before any device call."""
+    import ctypes as C
+    L = nv.lib()
+    f = 0x10000
+    dst = (C.c_uint64 * 2)(f, f + 4096)
+
+    def call(M=256, N=256, K=256, d=dst, n_dst=2, mc=0, ld=512, col_off=256):
+        return L.nvfp4_gemm_gather(f, f, f, f, 1.0, M, N, K, d, n_dst, mc, ld, col_off, None)
+
+    assert call(N=200) == -2                    # N % 16
+    assert call(ld=400) == -2                   # ld < col_off + N
+    assert call(col_off=8) == -2                # col_off % 16
+    assert call(n_dst=9) == -2                  # more ranks than the kernel carries
+    assert call(mc=1) == -2                     # a multicast address is one destination
+    assert call(d=None) == -1
+    bad = (C.c_uint64 * 2)(f, f + 16)           # destinations 32-byte aligned
+    assert call(d=bad) == -3
+    zero = (C.c_uint64 * 2)(f, 0)
+    assert call(d=zero) == -1
