@@ -100,9 +100,12 @@ class FusedGather:
     same order.
     """
 
-    # below this many ranks the multicast form sends no fewer bytes than per-rank
-    # stores and costs more per store (2 B200s: 1.47 vs 0.86 ms for a 940 MB output)
-    MULTICAST_MIN_RANKS = 4
+    # Ranks from which the multicast form is the default.  Measured for a 940 MB output
+    # (M=16384, N=28672): 2 ranks 0.86 ms with per-rank stores vs 1.47 ms multicast, 4
+    # ranks 1.11 vs 1.36 ms.  Per-rank stores send P-1 copies of the shard near the
+    # NVLink rate; the multicast form sends one copy but stores through the switch at
+    # about a third of that rate, so it pays from about 8 ranks on.
+    MULTICAST_MIN_RANKS = 8
 
     def __init__(self, M: int, N: int, device: torch.device, group=None, multicast: Optional[bool] = None):
         import torch.distributed._symmetric_memory as symm_mem
