@@ -8,7 +8,10 @@ import ctypes as C
 import os
 import threading
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libnvfp4_b200.so")
+# The in-tree build; NVFP4_B200_LIB names another build of the same library (for
+# comparing builds side by side).
+LIB_PATH = os.environ.get("NVFP4_B200_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)),
+                                                            "libnvfp4_b200.so")
 
 # Every exported symbol, with (restype, argtypes).  Keep in step with the header.
 _u8p, _u16p, _f32p, _vp = C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p
