@@ -490,9 +490,41 @@ def moe_section(nv, dev, reps=20):
     # the same total work as one dense GEMM (expert 0's weights for every row)
     dense_ms = timed(lambda: nv.gemm(q, sf[:nv.sf_bytes(m_total, K)], bq[:N], bsf[:nv.sf_bytes(N, K)], 1.0, out=d))
     nv.device_status()
-    return {"what": "grouped NVFP4 GEMM, 8 experts N=14336 K=4096, 8192 routed rows (4096 tokens x top-2)",
-            "rows_per_expert": counts.tolist(), "ms": ms, "tflops": flops / (ms / 1e3) / 1e12,
-            "dense_same_shape_ms": dense_ms, "dense_same_shape_tflops": flops / (dense_ms / 1e3) / 1e12}
+    out = {"what": "grouped NVFP4 GEMM, 8 experts N=14336 K=4096, 8192 routed rows (4096 tokens x top-2)",
+           "rows_per_expert": counts.tolist(), "ms": ms, "tflops": flops / (ms / 1e3) / 1e12,
+           "dense_same_shape_ms": dense_ms, "dense_same_shape_tflops": flops / (dense_ms / 1e3) / 1e12}
+
+    # Decode: 32 tokens x top-2 = 64 routed rows.  The grouped call (m_total <= 128:
+    # the stream-K kernel over the active experts' weight tiles) is judged on HBM
+    # bytes: each active expert's weights and scales read once (the 8 experts' 235 MB
+    # exceed L2).  Beside it, one decode GEMM per active expert.
+    dec_tokens = 32
+    counts_d = torch.bincount(torch.randint(0, G, (dec_tokens * top,), generator=g), minlength=G)
+    offs_d_host = [0] + torch.cumsum(counts_d, 0).tolist()
+    m_d = offs_d_host[-1]
+    offs_d = torch.tensor(offs_d_host, dtype=torch.int32, device=dev)
+    qd, sfd = nv.quantize_grouped(x[:m_d], gsx, offs_d)
+    dd = torch.empty(m_d, N, dtype=torch.bfloat16, device=dev)
+    active = [e for e in range(G) if counts_d[e] > 0]
+    w_bytes = len(active) * (N * K // 2 + nv.sf_bytes(N, K))
+    dec_ms = timed(lambda: nv.gemm_grouped(qd, sfd, bq, bsf, alphas, offs_d, out=dd))
+    blk0 = nv.grouped_sf_block0(offs_d_host)
+    alpha_h = alphas.cpu().tolist()
+    sf_blk = 128 * (K // 16)
+    per_expert = [(offs_d_host[e], offs_d_host[e + 1], blk0[e]) for e in active]
+
+    def loop():
+        for e, (a0, a1, b0) in zip(active, per_expert):
+            nv.gemm(qd[a0:a1], sfd[b0 * sf_blk:], bq[e * N:(e + 1) * N],
+                    bsf[e * nv.sf_bytes(N, K):(e + 1) * nv.sf_bytes(N, K)], alpha_h[e], out=dd[a0:a1])
+
+    loop_ms = timed(loop)
+    nv.device_status()
+    out["decode"] = {"what": "grouped NVFP4 GEMM, 8 experts N=14336 K=4096, 64 routed rows (32 tokens x top-2)",
+                     "rows_per_expert": counts_d.tolist(), "ms": dec_ms, "weight_bytes": w_bytes,
+                     "hbm_gbs": w_bytes / (dec_ms / 1e3) / 1e9,
+                     "per_expert_decode_calls_ms": loop_ms, "per_expert_hbm_gbs": w_bytes / (loop_ms / 1e3) / 1e9}
+    return out
 
 
 def epilogue_section(nv, sets, M, N, K, reps=30):

@@ -20,6 +20,10 @@ int decode_trace_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B
 int gather_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, int M,
                     int N, int K, const uint64_t *dst, int n_dst, int multicast, int64_t ld, int col_off,
                     cudaStream_t stream);
+size_t decode_grouped_workspace_bytes(int m_total, int N, int groups);
+int decode_grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+                            const float *alphas, uint16_t *D, const int *m_offsets, int groups, int m_total, int N,
+                            int K, void *ws, size_t ws_bytes, cudaStream_t stream);
 int grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const float *alphas,
                      uint16_t *D, const int *m_offsets, int groups, int m_total, int N, int K, cudaStream_t stream);
 int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
@@ -56,12 +60,11 @@ static int decode_max_m() {
 // nvfp4_gemm's own decode workspace: one zero-initialised buffer per (device,
 // stream), grown on demand and kept for the life of the process.  Calls on the
 // same stream are ordered, so they may share it.
-static int internal_workspace(int M, int N, cudaStream_t stream, void **ws, size_t *bytes) {
+static int internal_workspace(size_t need, cudaStream_t stream, void **ws, size_t *bytes) {
     static std::mutex mu;
     static std::map<std::pair<int, cudaStream_t>, std::pair<void *, size_t>> cache;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return NVFP4_ERR_CUDA;
-    const size_t need = decode_workspace_bytes(M, N);
     if (!need) return NVFP4_ERR_CUDA;
     std::lock_guard<std::mutex> lock(mu);
     auto &slot = cache[{dev, stream}];
@@ -94,7 +97,7 @@ int nvfp4_gemm(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uin
     if (M <= decode_max_m()) {
         void *ws = nullptr;
         size_t bytes = 0;
-        st = internal_workspace(M, N, s, &ws, &bytes);
+        st = internal_workspace(decode_workspace_bytes(M, N), s, &ws, &bytes);
         if (st) return st;
         return decode_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, ws, bytes, s);
     }
@@ -125,7 +128,7 @@ int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, 
     if (M <= decode_max_m()) {
         void *ws = nullptr;
         size_t bytes = 0;
-        if ((st = internal_workspace(M, N, s, &ws, &bytes))) return st;
+        if ((st = internal_workspace(decode_workspace_bytes(M, N), s, &ws, &bytes))) return st;
         st = decode_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, ws, bytes, s, e);
     } else {
         st = gemm_dispatch_epi(A, SFA, B, SFB, alpha, D, M, N, K, s, false, e);
@@ -138,8 +141,17 @@ int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, 
 
 int nvfp4_gemm_grouped(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const float *alpha,
                        uint16_t *D, const int32_t *m_offsets, int groups, int m_total, int N, int K, void *stream) {
-    return grouped_dispatch(A, SFA, B, SFB, alpha, D, m_offsets, groups, m_total, N, K,
-                            static_cast<cudaStream_t>(stream));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // at most 128 rows in all (decode): the stream-K kernel that reads only the active
+    // experts' weights; otherwise the CTA-pair kernel's grouped scheduler
+    if (m_total >= 1 && m_total <= decode_max_m() && groups >= 1 && groups <= 256 && N >= 128 && N % 128 == 0) {
+        void *ws = nullptr;
+        size_t bytes = 0;
+        int st = internal_workspace(decode_grouped_workspace_bytes(m_total, N, groups), s, &ws, &bytes);
+        if (st) return st;
+        return decode_grouped_dispatch(A, SFA, B, SFB, alpha, D, m_offsets, groups, m_total, N, K, ws, bytes, s);
+    }
+    return grouped_dispatch(A, SFA, B, SFB, alpha, D, m_offsets, groups, m_total, N, K, s);
 }
 
 int nvfp4_gemm_gather(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, int M,

@@ -27,6 +27,7 @@
 #include <mutex>
 
 #include "gemm_common.cuh"
+#include "grouped.cuh"
 
 namespace nvfp4 {
 namespace decode {
@@ -37,21 +38,26 @@ constexpr int kKGroups = 4;
 constexpr int kThreads = 32 * 6;     // producer, MMA, 4 epilogue warps
 constexpr int kSmemBudget = 225 * 1024;
 
-template <int MPAD>
+// GROUPED: the mixture-of-experts form (active experts' weight tiles only); its
+// group tables take 4 KB of shared memory from the ring's budget.
+template <int MPAD, bool GROUPED = false>
 struct Layout {
     static constexpr int kW = kTileN * kBlockKBytes;     // 16 KB
     static constexpr int kX = MPAD * kBlockKBytes;       // 1..16 KB
     static constexpr int kSfw = kKGroups * 512;          // 2 KB
     static constexpr int kSfx = kKGroups * 512;          // 2 KB (one 128-row scale block)
     static constexpr int kStage = kW + kX + kSfw + kSfx;
-    static constexpr int STAGES = (kSmemBudget - 2048) / kStage > 10 ? 10 : (kSmemBudget - 2048) / kStage;
+    static constexpr int kGroupBytes = GROUPED ? 4 * (gemm::kMaxGroups + 1) * 4 : 0;
+    static constexpr int STAGES = (kSmemBudget - 2048 - kGroupBytes) / kStage > 10 ? 10
+                                                                                   : (kSmemBudget - 2048 - kGroupBytes) / kStage;
     static constexpr int kOffW = 0;
     static constexpr int kOffX = kOffW + STAGES * kW;
     static constexpr int kOffSfw = kOffX + STAGES * kX;
     static constexpr int kOffSfx = kOffSfw + STAGES * kSfw;
     static constexpr int kOffBar = kOffSfx + STAGES * kSfx;
     static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 32;  // full, empty, acc_full x2, acc_empty x2, drain
-    static constexpr int kDynamicSmem = kOffBar + kBarBytes + 1024;
+    static constexpr int kOffGroups = (kOffBar + kBarBytes + 15) / 16 * 16;
+    static constexpr int kDynamicSmem = kOffGroups + kGroupBytes + 1024;
     static constexpr int kSfColsPerStage = kKGroups * 8;  // SFw 4 + SFx 4 per k-group
     // TMEM: two accumulators of MPAD columns (the MMAs of the next tile segment run
     // while the epilogue drains this one), then two sets of scale columns
@@ -80,6 +86,12 @@ struct Params {
     int grid;
     KernelCtl ctl;
     Epi epi;  // fused epilogue (plain: alpha and bf16 rounding only)
+    // grouped (mixture-of-experts) form: B stacked [groups * N, K/2], A's rows grouped
+    // by m_offsets, A's scales in the per-group layout (grouped.cuh)
+    const int *m_offsets;
+    const float *alphas;
+    int groups;     // 0: not grouped
+    int m_total;
     // Optional per-CTA %globaltimer stamps (nullptr = off), kDecodeTraceSlots u64 per
     // CTA: [0] entry [1] dependency wait released [2] first slot full (MMA thread)
     // [3] last slot full [4] epilogue done [5] iterations
@@ -87,19 +99,41 @@ struct Params {
 };
 constexpr int kDecodeTraceSlots = 6;
 
-// Stream-K range of CTA c over the cut tiles' k-blocks: [range_begin(c), range_begin(c+1)).
-__device__ __forceinline__ int64_t range_begin(int64_t c, const Params &p) { return c * p.sk_iters / p.grid; }
+// The tile schedule: host-computed for one weight matrix, computed on the device from
+// the active groups in the grouped form (tiles = active experts x weight tiles).
+struct Sched {
+    int n_tiles;
+    int64_t total_iters;
+    int sk_tiles;
+    int64_t sk_iters;
+    int dp_per_cta;
+    int grid;
+};
 
-// CTA whose range holds iteration `it` (ranges are [begin(c), begin(c+1))).
-__device__ __forceinline__ int owner_of(int64_t it, const Params &p) {
-    return (int)(((it + 1) * p.grid - 1) / p.sk_iters);
+__device__ __forceinline__ Sched make_sched(int n_tiles, int num_kb, int grid) {
+    Sched s;
+    s.n_tiles = n_tiles;
+    s.total_iters = (int64_t)n_tiles * num_kb;
+    s.grid = grid;
+    s.dp_per_cta = grid > 0 ? n_tiles / grid : 0;
+    s.sk_tiles = n_tiles - s.dp_per_cta * grid;
+    s.sk_iters = (int64_t)s.sk_tiles * num_kb;
+    return s;
 }
 
-template <int MPAD>
+// Stream-K range of CTA c over the cut tiles' k-blocks: [range_begin(c), range_begin(c+1)).
+__device__ __forceinline__ int64_t range_begin(int64_t c, const Sched &q) { return c * q.sk_iters / q.grid; }
+
+// CTA whose range holds iteration `it` (ranges are [begin(c), begin(c+1))).
+__device__ __forceinline__ int owner_of(int64_t it, const Sched &q) {
+    return (int)(((it + 1) * q.grid - 1) / q.sk_iters);
+}
+
+template <int MPAD, bool GROUPED>
 __global__ void __launch_bounds__(kThreads, 1)
     nvfp4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                         const Params p) {
-    using L = Layout<MPAD>;
+    using L = Layout<MPAD, GROUPED>;
     constexpr int S = L::STAGES;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -138,25 +172,91 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const uint64_t tmo = p.ctl.wait_timeout_ns;
-    const int64_t it_begin = range_begin(blockIdx.x, p), it_end = range_begin(blockIdx.x + 1, p);
     const int64_t rest_k = p.K >> 6;
+
+    // Grouped form: the schedule depends on the row offsets, an input, so wait for the
+    // preceding kernel first; then one warp tabulates each group's rows and first scale
+    // block and lists the groups that have rows (only their weights are read).
+    int *g_r0 = reinterpret_cast<int *>(base_ptr + L::kOffGroups);
+    int *g_r1 = g_r0 + (gemm::kMaxGroups + 1);
+    int *g_b0 = g_r1 + (gemm::kMaxGroups + 1);
+    int *g_act = g_b0 + (gemm::kMaxGroups + 1);  // [0] = number of active groups, then their ids
+    const int tiles_per_group = (p.N + kTileN - 1) / kTileN;
+    Sched q;
+    if constexpr (GROUPED) {
+        grid_dependency_wait();
+        if (warp == 0) {
+            build_group_tables(p.m_offsets, p.groups, p.m_total, 0, lane, g_r0, g_r1, g_b0, nullptr);
+            __syncwarp();
+            int count = 0;
+            for (int base0 = 0; base0 < p.groups; base0 += 32) {
+                const int g = base0 + lane;
+                const bool act = g < p.groups && g_r1[g] > g_r0[g];
+                const uint32_t mask = __ballot_sync(0xffffffffu, act);
+                if (act) g_act[1 + count + __popc(mask & ((1u << lane) - 1u))] = g;
+                count += __popc(mask);
+            }
+            if (lane == 0) g_act[0] = count;
+        }
+        __syncthreads();
+        q = make_sched(g_act[0] * tiles_per_group, p.num_kb, (int)gridDim.x);
+    } else {
+        q.n_tiles = p.n_tiles;
+        q.total_iters = p.total_iters;
+        q.sk_tiles = p.sk_tiles;
+        q.sk_iters = p.sk_iters;
+        q.dp_per_cta = p.dp_per_cta;
+        q.grid = p.grid;
+    }
+    // Where tile T's operands and output live.
+    struct DTile {
+        int w_row, x_row, d_row0, rows, ncol0;
+        int64_t sfw_block, sfx_block;
+        float alpha;
+    };
+    auto dtile = [&](int T) {
+        DTile d;
+        if constexpr (GROUPED) {
+            const int g = g_act[1 + T / tiles_per_group], t = T % tiles_per_group;
+            d.w_row = g * p.N + t * kTileN;
+            d.sfw_block = (int64_t)g * tiles_per_group + t;
+            d.x_row = g_r0[g];
+            d.sfx_block = g_b0[g];
+            d.d_row0 = g_r0[g];
+            d.rows = g_r1[g] - g_r0[g];
+            d.ncol0 = t * kTileN;
+            d.alpha = p.alphas[g];
+        } else {
+            d.w_row = T * kTileN;
+            d.sfw_block = T;
+            d.x_row = 0;
+            d.sfx_block = 0;
+            d.d_row0 = 0;
+            d.rows = p.M;
+            d.ncol0 = T * kTileN;
+            d.alpha = p.alpha;
+        }
+        return d;
+    };
+    const int64_t it_begin = range_begin(blockIdx.x, q), it_end = range_begin(blockIdx.x + 1, q);
     // Processing order of this CTA's work: its stream-K range [it_begin, it_end) over
     // the cut tiles — a last tile that is cut (shared with the next CTA) first, then
     // the range from its start — and then its whole tiles.  The cut tiles are thus
     // reduced across CTAs early, and a CTA with whole tiles ends on a plain store.
     // v in [0, n_iters) is the position in that order, iter(v) the k-block.
     const int64_t sk_len = it_end - it_begin;
-    const int64_t n_iters = sk_len + (int64_t)p.dp_per_cta * p.num_kb;
-    const int64_t dp_first = ((int64_t)p.sk_tiles + (int64_t)blockIdx.x * p.dp_per_cta) * p.num_kb;
+    const int64_t n_iters = sk_len + (int64_t)q.dp_per_cta * p.num_kb;
+    const int64_t dp_first = ((int64_t)q.sk_tiles + (int64_t)blockIdx.x * q.dp_per_cta) * p.num_kb;
     const int64_t last_tile0 = sk_len ? ((it_end - 1) / p.num_kb) * p.num_kb : 0;
+    const bool rotate = GROUPED ? q.dp_per_cta > 0 : p.rotate != 0;
     const int64_t head =
-        (p.rotate && sk_len && it_end % p.num_kb != 0 && last_tile0 > it_begin) ? it_end - last_tile0 : 0;
+        (rotate && sk_len && it_end % p.num_kb != 0 && last_tile0 > it_begin) ? it_end - last_tile0 : 0;
     auto iter = [&](int64_t v) {
         return v < head ? last_tile0 + v : (v < sk_len ? it_begin + (v - head) : dp_first + (v - sk_len));
     };
     // end (exclusive, in k-blocks) of the contiguous piece that k-block `it` belongs to
     auto piece_end = [&](int64_t it) {
-        if (it >= p.sk_iters) return dp_first + (int64_t)p.dp_per_cta * p.num_kb;
+        if (it >= q.sk_iters) return dp_first + (int64_t)q.dp_per_cta * p.num_kb;
         return (head && it >= last_tile0) ? it_end : (head ? last_tile0 : it_end);
     };
 
@@ -165,13 +265,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // weight tiles (a prefetch only fills L2, which stays coherent with any write the
     // previous kernel still makes), then wait for the previous kernel before touching
     // any input or output.
-    if (warp == 0 && lane == 0) {
-        for (int64_t v = 0; v < n_iters && v < L::STAGES; v++) {
-            const int64_t it = iter(v);
-            tma_prefetch_2d(&tmap_w, (int)(it % p.num_kb) * kBlockKBytes, (int)(it / p.num_kb) * kTileN);
+    if constexpr (!GROUPED) {
+        if (warp == 0 && lane == 0) {
+            for (int64_t v = 0; v < n_iters && v < L::STAGES; v++) {
+                const int64_t it = iter(v);
+                tma_prefetch_2d(&tmap_w, (int)(it % p.num_kb) * kBlockKBytes, (int)(it / p.num_kb) * kTileN);
+            }
         }
+        grid_dependency_wait();
     }
-    grid_dependency_wait();
     if (trace && threadIdx.x == 0) {
         trace[1] = global_timer_ns();
         trace[5] = (unsigned long long)n_iters;
@@ -192,16 +294,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 const int tile = (int)(it / p.num_kb), kb = (int)(it % p.num_kb);
+                const DTile dt = dtile(tile);
                 const int kg = min(kKGroups, p.k_groups - kb * kKGroups);
                 mbar_arrive_expect_tx(bar_full + 8 * s, L::kW + L::kX + 2u * kg * 512u);
                 issued_mask |= 1u << s;
                 issued_parity = (issued_parity & ~(1u << s)) | (ph << s);
-                tma_load_2d_hint(sW + s * L::kW, &tmap_w, bar_full + 8 * s, kb * kBlockKBytes, tile * kTileN, pol_w);
-                tma_load_2d_hint(sX + s * L::kX, &tmap_x, bar_full + 8 * s, kb * kBlockKBytes, 0, pol_x);
-                bulk_load_hint(sSfw + s * L::kSfw, p.sfb + ((int64_t)tile * rest_k + kb * kKGroups) * 512, kg * 512u,
+                tma_load_2d_hint(sW + s * L::kW, &tmap_w, bar_full + 8 * s, kb * kBlockKBytes, dt.w_row, pol_w);
+                tma_load_2d_hint(sX + s * L::kX, &tmap_x, bar_full + 8 * s, kb * kBlockKBytes, dt.x_row, pol_x);
+                bulk_load_hint(sSfw + s * L::kSfw, p.sfb + (dt.sfw_block * rest_k + kb * kKGroups) * 512, kg * 512u,
                                bar_full + 8 * s, pol_w);
-                bulk_load_hint(sSfx + s * L::kSfx, p.sfa + (int64_t)kb * kKGroups * 512, kg * 512u, bar_full + 8 * s,
-                               pol_x);
+                bulk_load_hint(sSfx + s * L::kSfx, p.sfa + (dt.sfx_block * rest_k + kb * kKGroups) * 512, kg * 512u,
+                               bar_full + 8 * s, pol_x);
             }
             grid_launch_dependents();  // all loads issued: the next kernel may start its prologue
             if (!ok) {
@@ -277,7 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool whole = (it == tile_first) && (seg_end == tile_last + 1);
             // partials slot: 0 for the tile the range starts in, 1 for the one it ends in
             const int slot = (it == it_begin) ? 0 : 1;
-            v += seg_end - it;
+            const int seg_len = (int)(seg_end - it);
+            v += seg_len;
 
             bool ok = true;
             const uint32_t buf = (uint32_t)(seg & 1), use = (uint32_t)(seg >> 1);
@@ -295,7 +399,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_acc_empty + 8 * buf);
 
-            const int n = tile * kTileN + nl;
+            const DTile dt = dtile(tile);
+            const int n = dt.ncol0 + nl;
             float sum[MPAD];
             if (whole) {
 #pragma unroll
@@ -309,22 +414,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // 0's release-acquire increment, which publishes them to the other
                 // contributors and, for the last one, orders their partials before the
                 // loads that follow the second barrier: one L2 round trip instead of a
-                // fence per thread plus the atomic.
+                // fence per thread plus the atomic.  The counter adds k-blocks, not
+                // CTAs: with fewer cut k-blocks than CTAs some ranges are empty, so the
+                // CTAs between the tile's first and last owner need not all contribute.
                 named_barrier(1, 128);
                 if (etid == 0) {
-                    const int c_lo = owner_of(tile_first, p), c_hi = owner_of(tile_last, p);
-                    const int prev = atomic_add_acq_rel_gpu(p.counters + tile, 1);
-                    *last_flag = (prev + 1 == c_hi - c_lo + 1);
+                    const int prev = atomic_add_acq_rel_gpu(p.counters + tile, seg_len);
+                    *last_flag = (prev + seg_len == p.num_kb);
                 }
                 named_barrier(1, 128);
                 if (!*last_flag) continue;
                 // last contributor: add every partial (its own included, re-read from L2)
                 // in CTA order, so the result does not depend on who finished last
-                const int c_lo = owner_of(tile_first, p), c_hi = owner_of(tile_last, p);
+                const int c_lo = owner_of(tile_first, q), c_hi = owner_of(tile_last, q);
 #pragma unroll
                 for (int m = 0; m < MPAD; m++) sum[m] = 0.0f;
                 for (int c = c_lo; c <= c_hi; c++) {
-                    const int cslot = ((int)(range_begin(c, p) / p.num_kb) == tile) ? 0 : 1;
+                    const int64_t cb = range_begin(c, q);
+                    if (cb == range_begin(c + 1, q)) continue;  // empty range: no partial
+                    const int cslot = ((int)(cb / p.num_kb) == tile) ? 0 : 1;
                     const float *part = p.partials + ((int64_t)c * 2 + cslot) * MPAD * kTileN;
 #pragma unroll
                     for (int m = 0; m < MPAD; m++) sum[m] += __ldcg(part + m * kTileN + nl);
@@ -335,9 +443,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (n < p.N) {
 #pragma unroll
                     for (int m = 0; m < MPAD; m++)
-                        if (m < p.M) {
-                            __nv_bfloat16 v = __float2bfloat16_rn(sum[m] * p.alpha);
-                            p.d[(int64_t)m * p.N + n] = *reinterpret_cast<uint16_t *>(&v);
+                        if (m < dt.rows) {
+                            __nv_bfloat16 v = __float2bfloat16_rn(sum[m] * dt.alpha);
+                            p.d[(int64_t)(dt.d_row0 + m) * p.N + n] = *reinterpret_cast<uint16_t *>(&v);
                         }
                 }
             } else if (!p.epi.q) {
@@ -394,9 +502,9 @@ int mpad_for(int M) {
     return m;
 }
 
-size_t workspace_bytes(int M, int N, int sm_count) {
+size_t workspace_bytes(int M, int N, int sm_count, int groups = 1) {
     const int mpad = mpad_for(M);
-    const size_t n_tiles = (size_t)(N + kTileN - 1) / kTileN;
+    const size_t n_tiles = (size_t)(N + kTileN - 1) / kTileN * (size_t)groups;
     const size_t counters = (n_tiles * sizeof(int) + 255) / 256 * 256;
     return counters + (size_t)sm_count * 2 * mpad * kTileN * sizeof(float);
 }
@@ -411,20 +519,23 @@ static int decode_rotate(int dp_per_cta) {
     return forced >= 0 ? forced : (dp_per_cta > 0 ? 1 : 0);
 }
 
-template <int MPAD>
+template <int MPAD, bool GROUPED = false>
 static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                   uint16_t *D, int M, int N, int K, void *ws, cudaStream_t stream, const DeviceInfo &di,
-                  const Epi &epi, unsigned long long *trace = nullptr) {
-    using L = Layout<MPAD>;
-    auto kern = nvfp4_decode_kernel<MPAD>;
+                  const Epi &epi, unsigned long long *trace = nullptr, const int *m_offsets = nullptr,
+                  const float *alphas = nullptr, int groups = 0) {
+    using L = Layout<MPAD, GROUPED>;
+    auto kern = nvfp4_decode_kernel<MPAD, GROUPED>;
     static int configured[64] = {};
     if (!configured[di.device]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamicSmem) != cudaSuccess)
             return NVFP4_ERR_CUDA;
         configured[di.device] = 1;
     }
+    // grouped: B is [groups * N, K/2], A is [M = m_total, K/2] with groups of rows
+    const int w_rows = GROUPED ? groups * N : N;
     CUtensorMap tw, tx;
-    int st = gemm::operand_map(B, N, K, kTileN, kBlockKBytes, &tw);  // cached tensor maps
+    int st = gemm::operand_map(B, w_rows, K, kTileN, kBlockKBytes, &tw);  // cached tensor maps
     if (!st) st = gemm::operand_map(A, M, K, MPAD, kBlockKBytes, &tx);
     if (st) return st;
     Params p;
@@ -438,17 +549,22 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     p.n_tiles = (N + kTileN - 1) / kTileN;
     p.num_kb = (K + 255) / 256;
     p.k_groups = K / 64;
-    p.total_iters = (int64_t)p.n_tiles * p.num_kb;
+    // grouped: the tile count is only known on the device; size the grid for the most
+    p.total_iters = (int64_t)p.n_tiles * (GROUPED ? groups : 1) * p.num_kb;
     p.grid = (int)std::min<int64_t>(di.sm_count, p.total_iters);
     p.dp_per_cta = p.n_tiles / p.grid;  // whole tiles per CTA (0 when tiles are fewer than CTAs)
     p.sk_tiles = p.n_tiles - p.dp_per_cta * p.grid;
     p.sk_iters = (int64_t)p.sk_tiles * p.num_kb;
     p.rotate = decode_rotate(p.dp_per_cta);
-    const size_t counters = ((size_t)p.n_tiles * sizeof(int) + 255) / 256 * 256;
+    const size_t counters = ((size_t)p.n_tiles * (GROUPED ? groups : 1) * sizeof(int) + 255) / 256 * 256;
     p.counters = static_cast<int *>(ws);
     p.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + counters);
     p.epi = epi;
     p.trace = trace;
+    p.m_offsets = m_offsets;
+    p.alphas = alphas;
+    p.groups = GROUPED ? groups : 0;
+    p.m_total = M;
     if ((st = kernel_ctl(&p.ctl))) return st;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -495,6 +611,47 @@ int decode_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, cons
         case 32: return decode::launch<32>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi);
         case 64: return decode::launch<64>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi);
         default: return decode::launch<128>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi);
+    }
+}
+
+size_t decode_grouped_workspace_bytes(int m_total, int N, int groups) {
+    DeviceInfo di;
+    if (device_info(&di)) return 0;
+    return decode::workspace_bytes(m_total, N, di.sm_count, groups);
+}
+
+// Grouped (mixture-of-experts) GEMM for m_total <= 128 rows in all: the swap-AB
+// stream-K kernel over (active expert, 128-row weight tile) tiles, reading only the
+// weights of experts that have rows.  Same arguments as the CTA-pair grouped GEMM plus
+// the split-K workspace (decode_grouped_workspace_bytes, zero-filled once).
+int decode_grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+                            const float *alphas, uint16_t *D, const int *m_offsets, int groups, int m_total, int N,
+                            int K, void *ws, size_t ws_bytes, cudaStream_t stream) {
+    if (!A || !SFA || !B || !SFB || !alphas || !D || !m_offsets) return NVFP4_ERR_INVALID;
+    if (groups < 1 || groups > gemm::kMaxGroups || m_total < 1 || m_total > 128 || N < 128 || N % 128 || K < 64 ||
+        K % 64)
+        return NVFP4_ERR_SHAPE;
+    if (!aligned16(A) || !aligned16(SFA) || !aligned16(B) || !aligned16(SFB) || !aligned16(D) ||
+        (reinterpret_cast<uintptr_t>(alphas) & 3u) || (reinterpret_cast<uintptr_t>(m_offsets) & 3u))
+        return NVFP4_ERR_ALIGN;
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    if (!ws || ws_bytes < decode::workspace_bytes(m_total, N, di.sm_count, groups) ||
+        (reinterpret_cast<uintptr_t>(ws) & 255u))
+        return NVFP4_ERR_WORKSPACE;
+    switch (decode::mpad_for(m_total)) {
+#define NVFP4_GROUPED_DECODE(MP)                                                                                   \
+    case MP:                                                                                                       \
+        return decode::launch<MP, true>(A, SFA, B, SFB, 1.0f, D, m_total, N, K, ws, stream, di, Epi(), nullptr,   \
+                                        m_offsets, alphas, groups);
+        NVFP4_GROUPED_DECODE(8)
+        NVFP4_GROUPED_DECODE(16)
+        NVFP4_GROUPED_DECODE(32)
+        NVFP4_GROUPED_DECODE(64)
+        NVFP4_GROUPED_DECODE(128)
+#undef NVFP4_GROUPED_DECODE
+        default: return NVFP4_ERR_SHAPE;
     }
 }
 

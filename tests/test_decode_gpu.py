@@ -53,6 +53,7 @@ def rel_err(oracle, out, a, sfa, b, sfb, alpha, M, N, K):
     (3, 136, 320),       # ragged N, odd M, partial last k-stage
     (9, 8, 64),          # smallest legal shape
     (33, 4096, 1024),
+    (16, 149 * 128, 512),  # one cut tile of 2 k-blocks over 148 CTAs: most stream-K ranges empty
 ])
 def test_decode_parity(nv, oracle, cuda_dev, M, N, K):
     a, sfa, b, sfb, alpha = operands(oracle, M, N, K, seed=M * 31 + N)

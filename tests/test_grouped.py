@@ -10,6 +10,8 @@ per-expert scale factors).  The oracle is applied group by group:
     max|D - D_ref| / max|D_ref| <= 1e-2; rows outside every group untouched;
   * device-side routing: one captured CUDA graph replayed after the offsets change
     in place follows the new routing.
+With at most 128 rows in all (decode) the stream-K kernel runs over the active
+experts' weight tiles only; above that the CTA-pair kernel's grouped scheduler.
 """
 import numpy as np
 import pytest
@@ -49,6 +51,11 @@ CASES = [
     ([0, 600, 640, 1500], 1500, 384, 512),
     # eight experts, one of them holding most rows
     ([0, 7, 300, 301, 2400, 2401, 2402, 2600, 3000], 3072, 1024, 2048),
+    # decode sizes (m_total <= 128: the stream-K kernel over active experts only):
+    # empty experts, a one-row expert, rows outside every group
+    ([0, 3, 3, 10, 40], 48, 512, 1024),
+    ([0, 0, 9, 9, 9, 30, 31, 31, 64], 64, 1024, 2048),
+    ([0, 128], 128, 256, 512),
 ]
 
 
