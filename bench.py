@@ -624,6 +624,15 @@ def gather_section(nv, dev, world, rank, reps=10):
     flops = 2.0 * M * N * K
     for k in [k for k in res if k.endswith("_ms") and res[k]]:
         res[k.replace("_ms", "_tflops")] = flops / (res[k] / 1e3) / 1e12
+    # Roofline of the fused form: the slower of this rank's shard GEMM and the NVLink
+    # bytes every rank must receive ((P-1)/P of the output) at the measured 770 GB/s
+    # per direction of a peer copy on this pool.
+    in_bytes = M * N * 2 * (world - 1) / world
+    link_ms = in_bytes / 770e9 * 1e3
+    bound_ms = max(link_ms, res["shard_gemm_ms"])
+    res["roofline"] = {"bound": "nvlink" if link_ms >= res["shard_gemm_ms"] else "tensor",
+                       "nvlink_in_bytes_per_rank": in_bytes, "nvlink_gbs_basis": 770.0, "bound_ms": bound_ms,
+                       "frac_fused_stores": bound_ms / res["fused_nvlink_stores_ms"]}
     return res
 
 

@@ -100,12 +100,14 @@ class FusedGather:
     same order.
     """
 
-    # Ranks from which the multicast form is the default.  Measured for a 940 MB output
-    # (M=16384, N=28672): 2 ranks 0.86 ms with per-rank stores vs 1.47 ms multicast, 4
-    # ranks 1.11 vs 1.36 ms.  Per-rank stores send P-1 copies of the shard near the
-    # NVLink rate; the multicast form sends one copy but stores through the switch at
-    # about a third of that rate, so it pays from about 8 ranks on.
-    MULTICAST_MIN_RANKS = 8
+    # Ranks from which the multicast form is the default: none within one node.
+    # Measured for a 940 MB output (M=16384, N=28672): 2 ranks 0.86 ms with per-rank
+    # stores vs 1.47 ms multicast, 4 ranks 1.11 vs 1.36 ms, 8 ranks 1.28 vs 1.35 ms.
+    # Every rank must receive (P-1)/P of the output whichever form sends it, so the
+    # incoming NVLink traffic bounds both (8 ranks: 822 MB at 770 GB/s = 1.07 ms);
+    # multicast only saves outgoing traffic, and its stores through the switch run
+    # slower than plain NVLink stores.
+    MULTICAST_MIN_RANKS = 9
 
     def __init__(self, M: int, N: int, device: torch.device, group=None, multicast: Optional[bool] = None):
         import torch.distributed._symmetric_memory as symm_mem

@@ -62,7 +62,7 @@ def _rank(rank, world, port, M, N, K, q):
 
 @pytest.mark.parametrize("M,N,K", [(512, 3072, 1024), (300, 1288, 2048)])
 def test_column_parallel_nccl_matches_single_gpu(M, N, K):
-    world = min(torch.cuda.device_count(), 4)
+    world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs at least two GPUs")
     ctx = mp.get_context("spawn")
@@ -130,7 +130,7 @@ def _rank_fused(rank, world, port, M, N, K, q):
 
 @pytest.mark.parametrize("M,N,K", [(512, 3072, 1024), (300, 1280, 2048)])
 def test_fused_gather_matches_single_gpu(M, N, K):
-    world = min(torch.cuda.device_count(), 4)
+    world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs at least two GPUs")
     ctx = mp.get_context("spawn")
