@@ -97,14 +97,22 @@ class ClockSampler:
         self._stop = threading.Event()
 
         def loop():
+            power, n = 0.0, 0
             while not self._stop.is_set():
                 try:
-                    self.samples.append((nvml.nvmlDeviceGetClockInfo(h, nvml.NVML_CLOCK_SM),
-                                         nvml.nvmlDeviceGetPowerUsage(h) / 1000.0, int(get_reasons(h))))
+                    if n % 8 == 0:  # power is the slowest query and only reported as a maximum
+                        power = nvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    self.samples.append((nvml.nvmlDeviceGetClockInfo(h, nvml.NVML_CLOCK_SM), power,
+                                         int(get_reasons(h))))
+                    n += 1
                 except Exception:
                     pass
-                self._stop.wait(0.001)
+                self._stop.wait(0.0005)
 
+        # The launching thread releases the GIL only briefly (ctypes calls); a short
+        # switch interval lets the sampler run every ~0.5 ms instead of every 5 ms.
+        self._switch = sys.getswitchinterval()
+        sys.setswitchinterval(1e-4)
         self._thread = threading.Thread(target=loop, daemon=True)
         self._thread.start()
         return self
@@ -113,6 +121,7 @@ class ClockSampler:
         if self._stop is not None:
             self._stop.set()
             self._thread.join(timeout=2)
+            sys.setswitchinterval(self._switch)
 
     def summary(self):
         if not self.samples:

@@ -38,9 +38,15 @@ constexpr int kKGroups = 4;
 constexpr int kThreads = 32 * 6;     // producer, MMA, 4 epilogue warps
 constexpr int kSmemBudget = 225 * 1024;
 
+// Two CTAs per SM (COLOC): 228 KB of shared memory per SM, 1 KB of it reserved per CTA.
+constexpr int kColocSmemMax = (233472 - 2 * 1024) / 2;
+
 // GROUPED: the mixture-of-experts form (active experts' weight tiles only); its
 // group tables take 4 KB of shared memory from the ring's budget.
-template <int MPAD, bool GROUPED = false>
+// COLOC: a ring of half the size, so that two CTAs fit on an SM: the CTAs of the next
+// call in the stream (a programmatic dependent) become resident while this call's
+// CTAs still stream, and prefetch their first weight tiles into L2 before they wait.
+template <int MPAD, bool GROUPED = false, bool COLOC = false>
 struct Layout {
     static constexpr int kW = kTileN * kBlockKBytes;     // 16 KB
     static constexpr int kX = MPAD * kBlockKBytes;       // 1..16 KB
@@ -48,8 +54,9 @@ struct Layout {
     static constexpr int kSfx = kKGroups * 512;          // 2 KB (one 128-row scale block)
     static constexpr int kStage = kW + kX + kSfw + kSfx;
     static constexpr int kGroupBytes = GROUPED ? 4 * (gemm::kMaxGroups + 1) * 4 : 0;
-    static constexpr int STAGES = (kSmemBudget - 2048 - kGroupBytes) / kStage > 10 ? 10
-                                                                                   : (kSmemBudget - 2048 - kGroupBytes) / kStage;
+    static constexpr int kBudget = COLOC ? kColocSmemMax - 1024 : kSmemBudget;
+    static constexpr int STAGES = (kBudget - 2048 - kGroupBytes) / kStage > 10 ? 10
+                                                                               : (kBudget - 2048 - kGroupBytes) / kStage;
     static constexpr int kOffW = 0;
     static constexpr int kOffX = kOffW + STAGES * kW;
     static constexpr int kOffSfw = kOffX + STAGES * kX;
@@ -66,7 +73,9 @@ struct Layout {
     static constexpr int kTmemCols = kTmemNeed <= 128 ? 128 : (kTmemNeed <= 256 ? 256 : 512);
     static_assert(MPAD % 8 == 0 && MPAD <= 128, "MPAD");
     static_assert(kTmemNeed <= kTmemCols, "tensor memory budget");
-    static_assert(kDynamicSmem <= 232448, "shared memory budget");
+    static_assert(kDynamicSmem <= (COLOC ? kColocSmemMax : 232448), "shared memory budget");
+    static_assert(!COLOC || 2 * kTmemCols <= 512, "two CTAs' tensor memory on one SM");
+    static_assert(STAGES >= 2, "ring depth");
 };
 
 struct Params {
@@ -84,6 +93,7 @@ struct Params {
     int dp_per_cta;       // whole tiles per CTA: tiles sk_tiles + c * dp_per_cta + j
     int rotate;           // process a cut last tile of the stream-K range first
     int grid;
+    int prefetch;  // weight tiles prefetched into L2 before the dependency wait
     KernelCtl ctl;
     Epi epi;  // fused epilogue (plain: alpha and bf16 rounding only)
     // grouped (mixture-of-experts) form: B stacked [groups * N, K/2], A's rows grouped
@@ -129,11 +139,11 @@ __device__ __forceinline__ int owner_of(int64_t it, const Sched &q) {
     return (int)(((it + 1) * q.grid - 1) / q.sk_iters);
 }
 
-template <int MPAD, bool GROUPED>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int MPAD, bool GROUPED, bool COLOC>
+__global__ void __launch_bounds__(kThreads, COLOC ? 2 : 1)
     nvfp4_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                         const Params p) {
-    using L = Layout<MPAD, GROUPED>;
+    using L = Layout<MPAD, GROUPED, COLOC>;
     constexpr int S = L::STAGES;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -267,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // any input or output.
     if constexpr (!GROUPED) {
         if (warp == 0 && lane == 0) {
-            for (int64_t v = 0; v < n_iters && v < L::STAGES; v++) {
+            for (int64_t v = 0; v < n_iters && v < p.prefetch; v++) {
                 const int64_t it = iter(v);
                 tma_prefetch_2d(&tmap_w, (int)(it % p.num_kb) * kBlockKBytes, (int)(it / p.num_kb) * kTileN);
             }
@@ -519,13 +529,38 @@ static int decode_rotate(int dp_per_cta) {
     return forced >= 0 ? forced : (dp_per_cta > 0 ? 1 : 0);
 }
 
-template <int MPAD, bool GROUPED = false>
-static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
-                  uint16_t *D, int M, int N, int K, void *ws, cudaStream_t stream, const DeviceInfo &di,
-                  const Epi &epi, unsigned long long *trace = nullptr, const int *m_offsets = nullptr,
-                  const float *alphas = nullptr, int groups = 0) {
-    using L = Layout<MPAD, GROUPED>;
-    auto kern = nvfp4_decode_kernel<MPAD, GROUPED>;
+// Two CTAs per SM (half-size ring) for MPAD <= 32, on by default;
+// NVFP4_DECODE_COLOC=0 keeps one CTA per SM with the full ring.  Measured per call
+// from a CUDA graph, W1 [28672, 8192]: M=1 26.9 -> 24.8 us, M=16 27.3 -> 25.2 us;
+// at MPAD=64 the half ring holds 3 slots and is slower (29.3 -> 30.5 us).
+static bool decode_coloc() {
+    static int on = [] {
+        const char *e = std::getenv("NVFP4_DECODE_COLOC");
+        return e ? (std::atoi(e) ? 1 : 0) : 1;
+    }();
+    return on != 0;
+}
+
+// Weight tiles each CTA prefetches into L2 before waiting on the preceding kernel, or
+// NVFP4_DECODE_PREFETCH (0..32).  Two CTAs per SM: the ring depth (the CTA is resident
+// while the previous call still streams; 5 tiles measured best of 0/2/3/5/10/16).  One
+// CTA per SM: 2 (the CTA only starts once the previous call's CTA on that SM has left,
+// and a deeper prefetch measured slower: M=64 28.6 us with 2, 29.3 with 7).
+static int decode_prefetch(int stages, bool coloc) {
+    static int forced = [] {
+        const char *e = std::getenv("NVFP4_DECODE_PREFETCH");
+        return e ? std::min(32, std::max(0, std::atoi(e))) : -1;
+    }();
+    return forced >= 0 ? forced : (coloc ? stages : std::min(stages, 2));
+}
+
+template <int MPAD, bool GROUPED, bool COLOC>
+static int launch_ring(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                       uint16_t *D, int M, int N, int K, void *ws, cudaStream_t stream, const DeviceInfo &di,
+                       const Epi &epi, unsigned long long *trace, const int *m_offsets, const float *alphas,
+                       int groups) {
+    using L = Layout<MPAD, GROUPED, COLOC>;
+    auto kern = nvfp4_decode_kernel<MPAD, GROUPED, COLOC>;
     static int configured[64] = {};
     if (!configured[di.device]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamicSmem) != cudaSuccess)
@@ -556,6 +591,7 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     p.sk_tiles = p.n_tiles - p.dp_per_cta * p.grid;
     p.sk_iters = (int64_t)p.sk_tiles * p.num_kb;
     p.rotate = decode_rotate(p.dp_per_cta);
+    p.prefetch = decode_prefetch(L::STAGES, COLOC);
     const size_t counters = ((size_t)p.n_tiles * (GROUPED ? groups : 1) * sizeof(int) + 255) / 256 * 256;
     p.counters = static_cast<int *>(ws);
     p.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + counters);
@@ -579,6 +615,20 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     if (cudaLaunchKernelEx(&cfg, kern, tw, tx, p) != cudaSuccess) return NVFP4_ERR_CUDA;
     count_launch();
     return cuda_status(cudaGetLastError());
+}
+
+template <int MPAD, bool GROUPED = false>
+static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                  uint16_t *D, int M, int N, int K, void *ws, cudaStream_t stream, const DeviceInfo &di,
+                  const Epi &epi, unsigned long long *trace = nullptr, const int *m_offsets = nullptr,
+                  const float *alphas = nullptr, int groups = 0) {
+    if constexpr (MPAD <= 32) {
+        if (decode_coloc())
+            return launch_ring<MPAD, GROUPED, true>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi, trace,
+                                                    m_offsets, alphas, groups);
+    }
+    return launch_ring<MPAD, GROUPED, false>(A, SFA, B, SFB, alpha, D, M, N, K, ws, stream, di, epi, trace,
+                                             m_offsets, alphas, groups);
 }
 
 }  // namespace decode
