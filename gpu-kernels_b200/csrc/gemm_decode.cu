@@ -554,6 +554,16 @@ static int decode_prefetch(int stages, bool coloc) {
     return forced >= 0 ? forced : (coloc ? stages : std::min(stages, 2));
 }
 
+// CTAs per call: one per SM, or at most NVFP4_DECODE_GRID (a diagnostic of how the
+// streaming rate depends on the number of SMs that stream).
+static int decode_max_ctas(int sm_count) {
+    static int forced = [] {
+        const char *e = std::getenv("NVFP4_DECODE_GRID");
+        return e ? std::atoi(e) : 0;
+    }();
+    return forced > 0 ? std::min(forced, sm_count) : sm_count;
+}
+
 template <int MPAD, bool GROUPED, bool COLOC>
 static int launch_ring(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                        uint16_t *D, int M, int N, int K, void *ws, cudaStream_t stream, const DeviceInfo &di,
@@ -586,7 +596,7 @@ static int launch_ring(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     p.k_groups = K / 64;
     // grouped: the tile count is only known on the device; size the grid for the most
     p.total_iters = (int64_t)p.n_tiles * (GROUPED ? groups : 1) * p.num_kb;
-    p.grid = (int)std::min<int64_t>(di.sm_count, p.total_iters);
+    p.grid = (int)std::min<int64_t>(decode_max_ctas(di.sm_count), p.total_iters);
     p.dp_per_cta = p.n_tiles / p.grid;  // whole tiles per CTA (0 when tiles are fewer than CTAs)
     p.sk_tiles = p.n_tiles - p.dp_per_cta * p.grid;
     p.sk_iters = (int64_t)p.sk_tiles * p.num_kb;

@@ -115,13 +115,16 @@ def decode_trace(M: int, N: int, K: int, calls: int = 8, sets: int = 3):
         with torch.cuda.graph(g, stream=s):
             for c in range(calls):
                 launch(c)
-    g.replay()
+    with torch.cuda.stream(s):
+        g.replay()
     torch.cuda.synchronize()
     tr.zero_()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    g.replay()
-    e1.record(s)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        g.replay()
+        e1.record(s)
     torch.cuda.synchronize()
     del g
     t = tr.view(calls, grid, 6).cpu()
