@@ -34,7 +34,7 @@ int decode_noalloc_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t 
 int gemm_host(const uint8_t *hA, const uint8_t *hSFA, const uint8_t *hB, const uint8_t *hSFB, float alpha,
               uint16_t *hD, int M, int N, int K, cudaStream_t stream);
 int gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D, int M,
-               int N, int K, unsigned long long *trace, cudaStream_t stream);
+               int N, int K, unsigned long long *trace, cudaStream_t stream, const Epi &epi);
 int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const void *D, int M,
                   int N, int K);
 int decode_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
@@ -104,10 +104,10 @@ int nvfp4_gemm(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uin
     return gemm_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, s, false);
 }
 
-int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
-                        uint16_t *D, int M, int N, int K, const nvfp4_epilogue *epi, void *stream) {
-    if (!epi) return nvfp4_gemm(A, SFA, B, SFB, alpha, D, M, N, K, stream);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
+}  // extern "C"
+
+// The C epilogue description as the kernels' Epi, with its argument checks.
+static int epilogue_from(const nvfp4_epilogue *epi, int N, Epi *out) {
     Epi e;
     e.bias = epi->bias;
     e.act = epi->activation;
@@ -123,7 +123,20 @@ int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, 
             (reinterpret_cast<uintptr_t>(e.gs) & 3u))
             return NVFP4_ERR_ALIGN;
     }
-    int st = gemm_validate(A, SFA, B, SFB, e.q ? static_cast<const void *>(e.q) : D, M, N, K);
+    *out = e;
+    return NVFP4_OK;
+}
+
+extern "C" {
+
+int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
+                        uint16_t *D, int M, int N, int K, const nvfp4_epilogue *epi, void *stream) {
+    if (!epi) return nvfp4_gemm(A, SFA, B, SFB, alpha, D, M, N, K, stream);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    Epi e;
+    int st = epilogue_from(epi, N, &e);
+    if (st) return st;
+    st = gemm_validate(A, SFA, B, SFB, e.q ? static_cast<const void *>(e.q) : D, M, N, K);
     if (st) return st;
     if (M <= decode_max_m()) {
         void *ws = nullptr;
@@ -211,7 +224,19 @@ int nvfp4_gemm_decode_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t 
 int nvfp4_gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                      uint16_t *D, int M, int N, int K, uint64_t *trace, void *stream) {
     return gemm_trace(A, SFA, B, SFB, alpha, D, M, N, K, reinterpret_cast<unsigned long long *>(trace),
-                      static_cast<cudaStream_t>(stream));
+                      static_cast<cudaStream_t>(stream), Epi());
+}
+
+int nvfp4_gemm_trace_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+                              float alpha, uint16_t *D, int M, int N, int K, const nvfp4_epilogue *epi,
+                              uint64_t *trace, void *stream) {
+    Epi e;
+    if (epi) {
+        int st = epilogue_from(epi, N, &e);
+        if (st) return st;
+    }
+    return gemm_trace(A, SFA, B, SFB, alpha, e.q ? static_cast<void *>(e.q) : D, M, N, K,
+                      reinterpret_cast<unsigned long long *>(trace), static_cast<cudaStream_t>(stream), e);
 }
 
 }  // extern "C"

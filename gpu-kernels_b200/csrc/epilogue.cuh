@@ -6,9 +6,8 @@
 // then either D = bf16_rn(y), or the bf16_rn(y) row segment quantized to NVFP4 with
 // a given global scale (the standalone quantizer's arithmetic, quant_common.cuh),
 // so a fused NVFP4 output equals nvfp4_quantize of the fused bf16 output byte for byte.
-// silu and gelu use the hardware approximations ex2.approx, rcp.approx and
-// tanh.approx (relative error below 2^-10 for tanh): the epilogue runs in the shadow
-// of the next tile's MMAs only while it stays this cheap.
+// silu and gelu use the hardware tanh.approx (relative error below 2^-10): the
+// epilogue runs in the shadow of the next tile's MMAs only while it stays this cheap.
 #pragma once
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -38,22 +37,45 @@ __device__ __forceinline__ float tanh_approx(float x) {
     return y;
 }
 
+// act(y) for a compile-time activation.
+//   silu: y * sigmoid(y) = h + h * tanh(h) with h = y / 2 (one tanh.approx)
+//   gelu: 0.5 y (1 + tanh(sqrt(2/pi) (y + 0.044715 y^3))) = h + h * tanh(u)
+template <int ACT>
+__device__ __forceinline__ float activate(float y) {
+    if constexpr (ACT == kActRelu) {
+        return fmaxf(y, 0.0f);
+    } else if constexpr (ACT == kActSilu) {
+        const float h = 0.5f * y;
+        return fmaf(h, tanh_approx(h), h);
+    } else if constexpr (ACT == kActGeluTanh) {
+        const float h = 0.5f * y;
+        const float u = 0.7978845608028654f * fmaf(0.044715f * y * y, y, y);
+        return fmaf(h, tanh_approx(u), h);
+    } else {
+        return y;
+    }
+}
+
+// act(alpha * acc + bias) for one element with the epilogue fixed at compile time
+// (straight-line code: the per-tile epilogue of the persistent kernels).
+template <int ACT, bool BIAS>
+__device__ __forceinline__ float epi_t(float acc, float alpha, float bias) {
+    float y = __fmul_rn(acc, alpha);
+    if constexpr (BIAS) y = __fadd_rn(y, bias);
+    return activate<ACT>(y);
+}
+
 // act(alpha * acc + bias) for one element; `bias` is the element's bf16 bias as fp32
-// (not added when the epilogue has no bias).
+// (not added when the epilogue has no bias).  Same arithmetic as epi_t.
 __device__ __forceinline__ float epi_value(float acc, float alpha, const Epi &e, float bias) {
     float y = __fmul_rn(acc, alpha);
     if (e.bias) y = __fadd_rn(y, bias);
-    if (e.act == kActRelu) {
-        y = fmaxf(y, 0.0f);
-    } else if (e.act == kActSilu) {
-        // y * sigmoid(y) = y / (1 + exp(-y))
-        y = __fdividef(y, 1.0f + __expf(-y));
-    } else if (e.act == kActGeluTanh) {
-        // 0.5 y (1 + tanh(sqrt(2/pi) (y + 0.044715 y^3)))
-        const float u = 0.7978845608028654f * (y + 0.044715f * (y * y * y));
-        y = (0.5f * y) * (1.0f + tanh_approx(u));
+    switch (e.act) {
+        case kActRelu: return activate<kActRelu>(y);
+        case kActSilu: return activate<kActSilu>(y);
+        case kActGeluTanh: return activate<kActGeluTanh>(y);
+        default: return y;
     }
-    return y;
 }
 
 }  // namespace nvfp4

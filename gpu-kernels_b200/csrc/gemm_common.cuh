@@ -191,6 +191,140 @@ __device__ __forceinline__ void store_row_epi(const uint32_t (&acc)[kCols], cons
     }
 }
 
+// Bias of columns c .. c+7 (c % 8 == 0; N % 8 == 0, so the 16 bytes are inside the
+// bias whenever c < N): the same address in every lane, one broadcast load.
+__device__ __forceinline__ uint4 bias8(const uint16_t *bias, int N, int c) {
+    return c < N ? __ldg(reinterpret_cast<const uint4 *>(bias + c)) : make_uint4(0u, 0u, 0u, 0u);
+}
+
+// Element j (0..7) of a bias8 vector as fp32.
+__device__ __forceinline__ float bias_elem(const uint4 &b, int j) {
+    const uint32_t w = (j >> 1) == 0 ? b.x : (j >> 1) == 1 ? b.y : (j >> 1) == 2 ? b.z : b.w;
+    return (j & 1) ? __uint_as_float(w & 0xFFFF0000u) : __uint_as_float(w << 16);
+}
+
+// store_row_epi with the activation and the bias fixed at compile time, bf16 output:
+// straight-line code per 16-column chunk.  Lanes need not agree on anything here.
+template <int kCols, int ACT, bool BIAS>
+__device__ __forceinline__ void store_row_act(const uint32_t (&acc)[kCols], const Params &p, int row, int col0,
+                                              int row_end, float alpha) {
+    const uint16_t *bias = p.epi.bias;
+    const bool row_ok = row < row_end;
+    uint8_t *drow = static_cast<uint8_t *>(p.d) + ((int64_t)row * p.N + col0) * 2;
+#pragma unroll
+    for (int c = 0; c < kCols / 16; c++) {
+        uint4 b0 = make_uint4(0u, 0u, 0u, 0u), b1 = b0;
+        if constexpr (BIAS) {
+            b0 = bias8(bias, p.N, col0 + c * 16);
+            b1 = bias8(bias, p.N, col0 + c * 16 + 8);
+        }
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint4 &b = i < 4 ? b0 : b1;
+            w[i] = pack2(epi_t<ACT, BIAS>(__uint_as_float(acc[c * 16 + 2 * i]), alpha, bias_elem(b, (2 * i) & 7)),
+                         epi_t<ACT, BIAS>(__uint_as_float(acc[c * 16 + 2 * i + 1]), alpha,
+                                          bias_elem(b, (2 * i + 1) & 7)),
+                         false);
+        }
+        if (row_ok) {
+            if (p.vec32_store) {
+                if (col0 + c * 16 < p.N) st_global_v8(drow + c * 32, w);
+            } else {
+                if (col0 + c * 16 < p.N)
+                    *reinterpret_cast<uint4 *>(drow + c * 32) = make_uint4(w[0], w[1], w[2], w[3]);
+                if (col0 + c * 16 + 8 < p.N)
+                    *reinterpret_cast<uint4 *>(drow + c * 32 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+            }
+        }
+    }
+}
+
+// The NVFP4-output form of store_row_act: per 16-element block the bf16-rounded
+// values, their amax, the scale code from the per-CTA tables (no division) and the
+// codes — the bytes store_row_epi (and nvfp4_quantize of the bf16 values) gives.
+// col0 and N multiples of 64.
+template <int kCols, int ACT, bool BIAS>
+__device__ __forceinline__ void store_row_act_nvfp4(const uint32_t (&acc)[kCols], const Params &p, int row,
+                                                    int col0, int row_end, float alpha, const ScaleTables *tab,
+                                                    float guess, bool gs_ok) {
+    static_assert(kCols % 64 == 0, "whole 64-column k-groups");
+    const Epi &e = p.epi;
+    const bool row_ok = row < row_end;
+    const int64_t rest = p.N >> 6;
+#pragma unroll
+    for (int g = 0; g < kCols / 64; g++) {
+        const int c0 = col0 + g * 64;
+        uint32_t codes[8], scales = 0;
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            uint4 b0 = make_uint4(0u, 0u, 0u, 0u), b1 = b0;
+            if constexpr (BIAS) {
+                b0 = bias8(e.bias, p.N, c0 + b * 16);
+                b1 = bias8(e.bias, p.N, c0 + b * 16 + 8);
+            }
+            uint32_t pk[8];
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int k = g * 64 + b * 16 + 2 * i;
+                const uint4 &bb = i < 4 ? b0 : b1;
+                pk[i] = pack2(epi_t<ACT, BIAS>(__uint_as_float(acc[k]), alpha, bias_elem(bb, (2 * i) & 7)),
+                              epi_t<ACT, BIAS>(__uint_as_float(acc[k + 1]), alpha, bias_elem(bb, (2 * i + 1) & 7)),
+                              false);
+                amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(pk[i] << 16)),
+                                         fabsf(__uint_as_float(pk[i] & 0xFFFF0000u))));
+            }
+            const uint32_t code = table_scale_code(amax, guess, tab, gs_ok);
+            const float inv = tab->inv[code];
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                lo |= e2m1x2(__fmul_rn(__uint_as_float(pk[i] << 16), inv),
+                             __fmul_rn(__uint_as_float(pk[i] & 0xFFFF0000u), inv)) << (8 * i);
+                hi |= e2m1x2(__fmul_rn(__uint_as_float(pk[4 + i] << 16), inv),
+                             __fmul_rn(__uint_as_float(pk[4 + i] & 0xFFFF0000u), inv)) << (8 * i);
+            }
+            codes[2 * b] = lo;
+            codes[2 * b + 1] = hi;
+            scales |= code << (8 * b);
+        }
+        if (row_ok && c0 < p.N) {
+            st_global_v8(e.q + (int64_t)row * (p.N >> 1) + (c0 >> 1), codes);
+            *reinterpret_cast<uint32_t *>(e.sf + sf_group_offset(row, c0 >> 6, rest)) = scales;
+        }
+    }
+}
+
+// The fused epilogue of one row, dispatched once per tile to the body compiled for
+// this launch's activation, bias and output type.  tab / guess / gs_ok: the NVFP4
+// output's scale tables (unused for bf16 output).  NVFP4 output needs kCols % 64 == 0
+// (the launch rejects it otherwise).
+template <int kCols>
+__device__ __forceinline__ void store_row_epi_fast(const uint32_t (&acc)[kCols], const Params &p, int row, int col0,
+                                                   int row_end, float alpha, const ScaleTables *tab, float guess,
+                                                   bool gs_ok) {
+    const Epi &e = p.epi;
+    const bool bias = e.bias != nullptr;
+#define NVFP4_EPI_BODY(A)                                                                                         \
+    if (e.q) {                                                                                                    \
+        if constexpr (kCols % 64 == 0) {                                                                          \
+            if (bias) store_row_act_nvfp4<kCols, A, true>(acc, p, row, col0, row_end, alpha, tab, guess, gs_ok); \
+            else store_row_act_nvfp4<kCols, A, false>(acc, p, row, col0, row_end, alpha, tab, guess, gs_ok);     \
+        }                                                                                                         \
+    } else {                                                                                                      \
+        if (bias) store_row_act<kCols, A, true>(acc, p, row, col0, row_end, alpha);                               \
+        else store_row_act<kCols, A, false>(acc, p, row, col0, row_end, alpha);                                   \
+    }
+    switch (e.act) {
+        case kActRelu: NVFP4_EPI_BODY(kActRelu) break;
+        case kActSilu: NVFP4_EPI_BODY(kActSilu) break;
+        case kActGeluTanh: NVFP4_EPI_BODY(kActGeluTanh) break;
+        default: NVFP4_EPI_BODY(kActNone) break;
+    }
+#undef NVFP4_EPI_BODY
+}
+
 // The gather form of store_row (bf16 output): each 16-column chunk of this row goes
 // to every destination of p.gather (32-byte stores, or two 16-byte multimem stores to
 // the multicast address).  Rows >= row_end and columns >= N are not stored.

@@ -69,7 +69,9 @@ struct PairLayout {
     static constexpr int kOffGroups = kOffStage;
     static constexpr bool kHasStage = kOffStage + kStageNeed + 1024 <= 232448;
     static constexpr int kRegion = (kHasStage && kStageNeed > kGroupBytes) ? kStageNeed : kGroupBytes;
-    static constexpr int kDynamicSmem = kOffStage + kRegion + 1024;
+    // the NVFP4 output's scale-code tables (quant_common.cuh), built by the epilogue warps
+    static constexpr int kOffTable = kOffStage + kRegion;
+    static constexpr int kDynamicSmem = kOffTable + (int)sizeof(ScaleTables) + 1024;
     static constexpr uint32_t kTxBytes = 2u * kStage;    // both CTAs complete on the leader's barrier
     // shared-memory matrix descriptor: 128B or 64B swizzle, 8-row core groups
     static constexpr uint32_t kLayout = BKB == 128 ? 2 : 4;
@@ -87,6 +89,7 @@ struct PairLayout {
     static_assert(kSfSets >= 1 && kSfBase + kSfSets * kSfCols <= kTmemCols, "tensor memory budget");
     static_assert(kB % 1024 == 0, "B slot must keep 1024-byte alignment for the swizzle");
     static_assert(kOffSched % 16 == 0, "the cluster-launch-control response is read as 16 bytes");
+    static_assert(kDynamicSmem <= 232448, "shared memory budget");
     static_assert(kDynamicSmem <= 232448, "shared memory budget");
 };
 
@@ -478,6 +481,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const int half = (warp - 2) >> 2;
         constexpr int kCols = BN / 2;
         const uint32_t lead_acc_empty = map_to_cta(bar_acc_empty, 0);
+        // NVFP4 output: the scale-code tables of this launch's global scale, built once
+        // by the epilogue warps while the first tile's MMAs run
+        ScaleTables *tab = reinterpret_cast<ScaleTables *>(base_ptr + L::kOffTable);
+        float guess = 0.0f;
+        bool gs_ok = false;
+        if constexpr (!F16) {
+            if (p.epi.q) {
+                const float gs = *p.epi.gs;
+                gs_ok = gs_usable(gs);
+                guess = scale_guess_factor(gs);
+                build_scale_tables(tab, gs, (int)threadIdx.x - 64, 32 * kEpiWarps);
+                named_barrier(1, 32 * kEpiWarps);
+            }
+        }
         int local = 0;
         uint32_t chunk = 0;  // TMA-store boxes issued by this warp (two staging boxes alternate)
         long long t_accw = 0, t_store = 0, c_ready = 0;
@@ -556,16 +573,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     }
                 } else if (p.epi.plain()) {
                     store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha);
-                } else {
-                    store_row_epi<kCols>(acc, p, row, col0, ti.row_end, ti.alpha,
-                                         load_bias_lane(p.epi, p.N, col0, lane));
+                } else if constexpr (!F16) {
+                    store_row_epi_fast<kCols>(acc, p, row, col0, ti.row_end, ti.alpha, tab, guess, gs_ok);
                 }
             } else {
                 if (p.epi.plain())
                     store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha);
-                else
-                    store_row_epi<kCols>(acc, p, row, col0, ti.row_end, ti.alpha,
-                                         load_bias_lane(p.epi, p.N, col0, lane));
+                else if constexpr (!F16)
+                    store_row_epi_fast<kCols>(acc, p, row, col0, ti.row_end, ti.alpha, tab, guess, gs_ok);
             }
             if (TRACE && warp == 2 && lane == 0) t_store += clock64() - c_ready;
         }
@@ -648,6 +663,7 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
                        unsigned long long *trace, const Epi &epi, const Grouped &grp = Grouped(),
                        const Gather &gat = Gather()) {
     if (epi.q && BN % 128 != 0) return NVFP4_ERR_UNSUPPORTED;  // NVFP4 output wants 64-column aligned halves
+    if (F16 && !epi.plain()) return NVFP4_ERR_UNSUPPORTED;     // the fused epilogue writes bf16 / NVFP4
     using L = PairLayout<STAGES, BKB, BN>;
     auto kern = trace ? nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, true>
                       : nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, false>;
@@ -819,13 +835,13 @@ int gather_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, cons
 
 // Pair kernel with the per-CTA cycle trace on (trace: 148 x kTraceSlots u64 on the device).
 int gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D, int M,
-               int N, int K, unsigned long long *trace, cudaStream_t stream) {
+               int N, int K, unsigned long long *trace, cudaStream_t stream, const Epi &epi) {
     int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
     if (st) return st;
     if (!trace) return NVFP4_ERR_INVALID;
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
-    return gemm::launch_pair_cfg<false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace, Epi());
+    return gemm::launch_pair_cfg<false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace, epi);
 }
 
 }  // namespace nvfp4

@@ -52,6 +52,64 @@ __device__ __forceinline__ void block_codes(const float (&v)[16], float inv, uin
     }
 }
 
+// Scale codes without divisions, for kernels that quantize many blocks with one
+// global scale gs.  The code is a non-decreasing step function of the block's
+// amax (each step of block_scale_code is monotone), and amax is a bf16 value, so
+//   thr[c] = the smallest non-negative bf16 amax whose code is >= c   (c = 1..126)
+// determines it exactly: code = max{c : amax >= thr[c]}.  thr[0] = 0; thr[c] is NaN
+// where no amax reaches c (every comparison with it is false), thr[127] likewise.
+// inv[c] = block_inverse(c).  A first guess amax * (1 / (6 gs)) rounded to e4m3 is
+// within one code of the exact one (its relative error is a few fp32 ulps, an e4m3
+// step 2^-3), so two table comparisons correct it.
+struct ScaleTables {
+    float thr[128];
+    float inv[128];
+};
+
+// Fill the tables for gs; thread `tid` of `nthreads` (>= 1) threads, followed by a
+// barrier of the caller's before any use.
+__device__ __forceinline__ void build_scale_tables(ScaleTables *t, float gs, int tid, int nthreads) {
+    const bool ok = gs_usable(gs);
+    for (int i = tid; i < 256; i += nthreads) {
+        const int c = i & 127;
+        if (i < 128) {
+            float thr;
+            if (c == 0) {
+                thr = 0.0f;
+            } else if (!ok || c == 127) {
+                thr = __uint_as_float(0x7FC00000u);
+            } else {
+                // bf16 bit patterns [0, +inf]; code(+inf) = 126 (saturated)
+                uint32_t lo = 0, hi = 0x7F80u;
+                while (lo < hi) {
+                    const uint32_t mid = (lo + hi) >> 1;
+                    if (block_scale_code(__uint_as_float(mid << 16), gs, ok) >= (uint32_t)c) hi = mid;
+                    else lo = mid + 1;
+                }
+                thr = __uint_as_float(lo << 16);
+            }
+            t->thr[c] = thr;
+        } else {
+            t->inv[c] = block_inverse((uint32_t)c, gs, ok);
+        }
+    }
+}
+
+// 1 / (6 gs) for the first guess (0 when gs is unusable).
+__device__ __forceinline__ float scale_guess_factor(float gs) {
+    return gs_usable(gs) ? 1.0f / (6.0f * gs) : 0.0f;
+}
+
+// block_scale_code(amax, gs, gs_ok) from the tables (amax >= 0, not NaN).
+__device__ __forceinline__ uint32_t table_scale_code(float amax, float guess_factor, const ScaleTables *t,
+                                                     bool gs_ok) {
+    uint32_t c = static_cast<uint32_t>(__nv_cvt_float_to_fp8(amax * guess_factor, __NV_SATFINITE, __NV_E4M3));
+    c = c > 126u ? 126u : c;  // an inf * 0 guess (unusable gs) converts to the NaN code
+    const float below = t->thr[c], above = t->thr[c + 1];
+    c = amax < below ? c - 1 : (amax >= above ? c + 1 : c);
+    return gs_ok ? c : 0u;
+}
+
 // Byte offset of the scale of (row r, 64-element k-group kg) in the blocked layout
 // of a [pad128(rows), K/16] scale tensor with rest_k = K / 64; the k-group's four
 // scales are the four bytes from there.

@@ -1,7 +1,8 @@
 """Diagnostics for the NVFP4 kernels on a B200.
 
     python -m nvfp4_b200.diag probe [iters]        measured mxf4nvf4 tensor rate per issue mode
-    python -m nvfp4_b200.diag trace M N K [reps]    per-CTA cycle breakdown of the CTA-pair GEMM (last of reps)
+    python -m nvfp4_b200.diag trace M N K [reps] [epi]  per-CTA cycle breakdown of the CTA-pair GEMM (last
+                                                   of reps); epi: one of EPILOGUES (fused epilogue)
     python -m nvfp4_b200.diag decode M N K          timeline of back-to-back decode GEMMs (graph replay)
 
 (run with gpu-kernels_b200/ on sys.path).  Each prints JSON lines.
@@ -35,10 +36,20 @@ def probe(iters: int = 20000):
     return out
 
 
-def trace(M: int, N: int, K: int, reps: int = 3):
+# Fused epilogues the trace can run: (activation, bias, NVFP4 output)
+EPILOGUES = {"none": ("none", False, False), "relu_bf16": ("relu", False, False),
+             "silu_bf16": ("silu", False, False), "bias_silu_bf16": ("silu", True, False),
+             "gelu_bf16": ("gelu_tanh", False, False), "fp4": ("none", False, True),
+             "bias_silu_fp4": ("silu", True, True)}
+
+
+def trace(M: int, N: int, K: int, reps: int = 3, epi: str = "none"):
     """Per-CTA cycle breakdown of the CTA-pair kernel (the last of `reps` launches),
-    plus the kernel's event time and where the time outside the MMA span goes."""
+    plus the kernel's event time and where the time outside the MMA span goes; with
+    `epi`, the same launch with that fused epilogue."""
+    from ._lib import ACTIVATIONS, Epilogue
     from ._lib import lib as _l
+    from .layout import sf_bytes
     from .ops import create_tensors
     slots = 12
     dev = torch.device("cuda", 0)
@@ -46,14 +57,22 @@ def trace(M: int, N: int, K: int, reps: int = 3):
     sfa = torch.full_like(sfa, 0x38)
     sfb = torch.full_like(sfb, 0x38)
     d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    act, with_bias, fp4 = EPILOGUES[epi]
+    bias = torch.zeros(N, dtype=torch.bfloat16, device=dev)
+    q = torch.empty(M, N // 2, dtype=torch.uint8, device=dev)
+    sfo = torch.empty(sf_bytes(M, N), dtype=torch.uint8, device=dev)
+    gs = torch.tensor([1e-3], dtype=torch.float32, device=dev)
+    E = Epilogue(bias=bias.data_ptr() if with_bias else None, activation=ACTIVATIONS[act],
+                 q_out=q.data_ptr() if fp4 else None, sf_out=sfo.data_ptr() if fp4 else None,
+                 out_global_scale=gs.data_ptr() if fp4 else None)
     tr = torch.zeros(148 * slots, dtype=torch.int64, device=dev)
     s = torch.cuda.current_stream().cuda_stream
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for i in range(reps):
         if i == reps - 1:
             e0.record()
-        check(_l().nvfp4_gemm_trace(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), 1.0, d.data_ptr(),
-                                    M, N, K, tr.data_ptr(), s), "trace")
+        check(_l().nvfp4_gemm_trace_epilogue(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), 1.0,
+                                             d.data_ptr(), M, N, K, C.byref(E), tr.data_ptr(), s), "trace")
     e1.record()
     torch.cuda.synchronize()
     t = tr.view(148, slots).cpu()
@@ -63,7 +82,7 @@ def trace(M: int, N: int, K: int, reps: int = 3):
     span = leaders[:, 6].double()
     rows = {"mma_wait_full": leaders[:, 0], "mma_wait_acc": leaders[:, 1], "producer_wait_empty": t[:, 2],
             "epi_wait_acc_full": t[:, 3], "epi_drain_store": t[:, 4]}
-    res = {"M": M, "N": N, "K": K, "event_us": e0.elapsed_time(e1) * 1e3,
+    res = {"M": M, "N": N, "K": K, "epilogue": epi, "event_us": e0.elapsed_time(e1) * 1e3,
            "tiles_per_pair": statistics.mean(leaders[:, 5].tolist()),
            "mma_span_cycles": statistics.mean(span.tolist()),
            "sm_clock_mhz": statistics.mean((leaders[:, 6].double() / leaders[:, 7].double() * 1e3).tolist())}
@@ -176,7 +195,7 @@ def main(argv):
     else:
         M, N, K = (int(x) for x in argv[1:4])
         reps = int(argv[4]) if len(argv) > 4 else 3
-        print(json.dumps(trace(M, N, K, reps)))
+        print(json.dumps(trace(M, N, K, reps, argv[5] if len(argv) > 5 else "none")))
     return 0
 
 

@@ -285,6 +285,11 @@ NVFP4_API int nvfp4_gemm_decode_noalloc(const uint8_t *A, const uint8_t *SFA, co
  */
 NVFP4_API int nvfp4_gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
                float alpha, uint16_t *D, int M, int N, int K, uint64_t *trace, void *stream);
+/* nvfp4_gemm_trace with a fused epilogue (nvfp4_gemm_epilogue's arguments; epi may be
+ * NULL): the same trace, for the cost of the epilogue per tile ([3], [4]). */
+NVFP4_API int nvfp4_gemm_trace_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B,
+                                        const uint8_t *SFB, float alpha, uint16_t *D, int M, int N, int K,
+                                        const nvfp4_epilogue *epi, uint64_t *trace, void *stream);
 NVFP4_API int nvfp4_probe_mma_rate(int mode, int iters, double *tflops, double *cycles_per_mma);
 /* nvfp4_gemm_decode with per-CTA %globaltimer stamps in `trace` (device, grid x 6
  * uint64, grid = min(#SMs, ceil(N/128) * ceil(K/256))): [0] CTA entry, [1] release of
