@@ -247,7 +247,7 @@ __device__ __forceinline__ void store_row_act(const uint32_t (&acc)[kCols], cons
 template <int kCols, int ACT, bool BIAS>
 __device__ __forceinline__ void store_row_act_nvfp4(const uint32_t (&acc)[kCols], const Params &p, int row,
                                                     int col0, int row_end, float alpha, const ScaleTables *tab,
-                                                    float guess, bool gs_ok) {
+                                                    ScaleGuess guess, bool gs_ok) {
     static_assert(kCols % 64 == 0, "whole 64-column k-groups");
     const Epi &e = p.epi;
     const bool row_ok = row < row_end;
@@ -302,7 +302,7 @@ __device__ __forceinline__ void store_row_act_nvfp4(const uint32_t (&acc)[kCols]
 // (the launch rejects it otherwise).
 template <int kCols>
 __device__ __forceinline__ void store_row_epi_fast(const uint32_t (&acc)[kCols], const Params &p, int row, int col0,
-                                                   int row_end, float alpha, const ScaleTables *tab, float guess,
+                                                   int row_end, float alpha, const ScaleTables *tab, ScaleGuess guess,
                                                    bool gs_ok) {
     const Epi &e = p.epi;
     const bool bias = e.bias != nullptr;

@@ -484,7 +484,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         // NVFP4 output: the scale-code tables of this launch's global scale, built once
         // by the epilogue warps while the first tile's MMAs run
         ScaleTables *tab = reinterpret_cast<ScaleTables *>(base_ptr + L::kOffTable);
-        float guess = 0.0f;
+        ScaleGuess guess{0.0f, 1.0f};
         bool gs_ok = false;
         if constexpr (!F16) {
             if (p.epi.q) {

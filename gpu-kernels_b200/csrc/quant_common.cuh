@@ -60,11 +60,38 @@ __device__ __forceinline__ void block_codes(const float (&v)[16], float inv, uin
 // where no amax reaches c (every comparison with it is false), thr[127] likewise.
 // inv[c] = block_inverse(c).  A first guess amax * (1 / (6 gs)) rounded to e4m3 is
 // within one code of the exact one (its relative error is a few fp32 ulps, an e4m3
-// step 2^-3), so two table comparisons correct it.
+// step 2^-3; where it underflows the exact code is 0 too), so two table comparisons
+// correct it.
 struct ScaleTables {
     float thr[128];
     float inv[128];
 };
+
+// thr[c] for 1 <= c <= 126 and a usable gs, as bf16 bits: the smallest bf16 pattern
+// in [0, +inf] whose code is >= c (code(+inf) = 126, saturated).  Starts from the
+// amax whose quotient is the midpoint between the e4m3 values of codes c-1 and c and
+// steps one bf16 value at a time (a few steps); a binary search over all patterns
+// if that has not settled after 64 steps.
+__device__ __forceinline__ uint32_t scale_threshold_bits(uint32_t c, float gs) {
+    auto reaches = [&](uint32_t bits) { return block_scale_code(__uint_as_float(bits << 16), gs, true) >= c; };
+    const float mid = 0.5f * (e4m3_to_float((uint8_t)(c - 1)) + e4m3_to_float((uint8_t)c));
+    const float x = mid * 6.0f * gs;  // >= 0, possibly +inf
+    uint32_t b = x >= __uint_as_float(0x7F800000u) ? 0x7F80u : (__float_as_uint(x) >> 16);
+    int steps = 0;
+    if (reaches(b)) {
+        while (b > 0 && steps < 64 && reaches(b - 1)) b--, steps++;
+    } else {
+        while (steps < 64 && !reaches(b)) b++, steps++;  // stops at 0x7F80 at the latest
+    }
+    if (steps < 64) return b;
+    uint32_t lo = 0, hi = 0x7F80u;
+    while (lo < hi) {
+        const uint32_t m = (lo + hi) >> 1;
+        if (reaches(m)) hi = m;
+        else lo = m + 1;
+    }
+    return lo;
+}
 
 // Fill the tables for gs; thread `tid` of `nthreads` (>= 1) threads, followed by a
 // barrier of the caller's before any use.
@@ -74,20 +101,9 @@ __device__ __forceinline__ void build_scale_tables(ScaleTables *t, float gs, int
         const int c = i & 127;
         if (i < 128) {
             float thr;
-            if (c == 0) {
-                thr = 0.0f;
-            } else if (!ok || c == 127) {
-                thr = __uint_as_float(0x7FC00000u);
-            } else {
-                // bf16 bit patterns [0, +inf]; code(+inf) = 126 (saturated)
-                uint32_t lo = 0, hi = 0x7F80u;
-                while (lo < hi) {
-                    const uint32_t mid = (lo + hi) >> 1;
-                    if (block_scale_code(__uint_as_float(mid << 16), gs, ok) >= (uint32_t)c) hi = mid;
-                    else lo = mid + 1;
-                }
-                thr = __uint_as_float(lo << 16);
-            }
+            if (c == 0) thr = 0.0f;
+            else if (!ok || c == 127) thr = __uint_as_float(0x7FC00000u);
+            else thr = __uint_as_float(scale_threshold_bits((uint32_t)c, gs) << 16);
             t->thr[c] = thr;
         } else {
             t->inv[c] = block_inverse((uint32_t)c, gs, ok);
@@ -95,15 +111,29 @@ __device__ __forceinline__ void build_scale_tables(ScaleTables *t, float gs, int
     }
 }
 
-// 1 / (6 gs) for the first guess (0 when gs is unusable).
-__device__ __forceinline__ float scale_guess_factor(float gs) {
-    return gs_usable(gs) ? 1.0f / (6.0f * gs) : 0.0f;
+// 1 / (6 gs) for the first guess as k * s with gs = m * 2^e (m in [0.5, 1)):
+// k = 1 / (6 m), s = 2^-e, exact for every usable gs (e in [-99, 128]), so the guess
+// neither overflows (6 gs can) nor loses precision in a subnormal factor.  k = 0
+// when gs is unusable.
+struct ScaleGuess {
+    float k, s;
+};
+__device__ __forceinline__ ScaleGuess scale_guess_factor(float gs) {
+    ScaleGuess g{0.0f, 1.0f};
+    if (gs_usable(gs)) {
+        int e;
+        const float m = frexpf(gs, &e);
+        g.k = 1.0f / (6.0f * m);
+        g.s = ldexpf(1.0f, -e);
+    }
+    return g;
 }
 
 // block_scale_code(amax, gs, gs_ok) from the tables (amax >= 0, not NaN).
-__device__ __forceinline__ uint32_t table_scale_code(float amax, float guess_factor, const ScaleTables *t,
+__device__ __forceinline__ uint32_t table_scale_code(float amax, ScaleGuess guess, const ScaleTables *t,
                                                      bool gs_ok) {
-    uint32_t c = static_cast<uint32_t>(__nv_cvt_float_to_fp8(amax * guess_factor, __NV_SATFINITE, __NV_E4M3));
+    const float approx = (amax * guess.k) * guess.s;
+    uint32_t c = static_cast<uint32_t>(__nv_cvt_float_to_fp8(approx, __NV_SATFINITE, __NV_E4M3));
     c = c > 126u ? 126u : c;  // an inf * 0 guess (unusable gs) converts to the NaN code
     const float below = t->thr[c], above = t->thr[c + 1];
     c = amax < below ? c - 1 : (amax >= above ? c + 1 : c);

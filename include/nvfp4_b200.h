@@ -291,6 +291,13 @@ NVFP4_API int nvfp4_gemm_trace_epilogue(const uint8_t *A, const uint8_t *SFA, co
                                         const uint8_t *SFB, float alpha, uint16_t *D, int M, int N, int K,
                                         const nvfp4_epilogue *epi, uint64_t *trace, void *stream);
 NVFP4_API int nvfp4_probe_mma_rate(int mode, int iters, double *tflops, double *cycles_per_mma);
+/* nvfp4_scale_codes: the e4m3 scale code of n blocks given each block's bf16 amax
+ * (device, sign ignored) and the device fp32 global scale, computed the way the fused
+ * GEMM epilogue computes them for NVFP4 output — from per-launch threshold tables,
+ * without a division per block — so that path can be checked against the
+ * specification for every bf16 amax. */
+NVFP4_API int nvfp4_scale_codes(const uint16_t *amax_bf16, int64_t n, const float *global_scale, uint8_t *codes,
+                                void *stream);
 /* nvfp4_gemm_decode with per-CTA %globaltimer stamps in `trace` (device, grid x 6
  * uint64, grid = min(#SMs, ceil(N/128) * ceil(K/256))): [0] CTA entry, [1] release of
  * the wait on the preceding kernel, [2] first and [3] last ring slot reaching the

@@ -53,6 +53,68 @@ def test_ties_and_saturation_bit_exact(nv, oracle, cuda_dev):
     assert np.array_equal(sf, sf_ref)
 
 
+def _every_amax_blocks():
+    """One 16-element block per non-negative bf16 value from +0 to +inf (32641 blocks):
+    the block holds +v, -v and fifteenths of v, so its amax is exactly v."""
+    vals = np.arange(0, 0x7F81, dtype=np.uint32)
+    K = 1024
+    per_row = K // 16
+    rows = (len(vals) + per_row - 1) // per_row
+    blocks = np.zeros((rows * per_row, 16), dtype=np.uint16)
+    v = vals.astype(np.uint16)
+    blocks[: len(vals), 0] = v
+    blocks[: len(vals), 1] = v | 0x8000
+    f = (vals << 16).view(np.float32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        small = (f / 15.0).astype(np.float32)
+    small_bits = (small.view(np.uint32) >> 16).astype(np.uint16)  # truncation keeps it below v
+    blocks[: len(vals), 2:] = small_bits[:, None]
+    return blocks.reshape(rows, K)
+
+
+GS_SWEEP = [1.0, 1.0 / 2688.0, 3.7e-5, 0.123, 1e30, 2.0 ** -100, 3.0e38]
+
+
+@pytest.mark.parametrize("gs", GS_SWEEP)
+def test_scale_code_of_every_bf16_amax(nv, oracle, cuda_dev, gs):
+    """Every possible bf16 block amax, +inf included, over global scales from 2^-100
+    to 3e38: the quantizer's scale codes (and, for finite blocks, element codes)
+    equal the specification's."""
+    x = _every_amax_blocks()
+    q, sf, q_ref, sf_ref = quantize_both(nv, oracle, x, gs, cuda_dev)
+    assert np.array_equal(sf, sf_ref)
+    # Codes of the +inf block (block 0x7F80: row 510, bytes 0-7) are outside the
+    # specification, which wants finite inputs: at gs = 3e38 its reciprocal underflows
+    # to 0 and inf * 0 is NaN.  Every finite block must match.
+    finite = np.ones(q.shape, dtype=bool)
+    finite[0x7F80 // 64, 0:8] = False
+    assert np.array_equal(q[finite], q_ref[finite])
+
+
+@pytest.mark.parametrize("gs", GS_SWEEP + [0.0, float("nan"), -1.0, 2.0 ** -120])
+def test_table_scale_codes_every_bf16_amax(nv, oracle, cuda_dev, gs):
+    """The fused GEMM epilogue's division-free scale codes (threshold tables built per
+    launch, a first guess corrected by two comparisons; nvfp4_scale_codes runs that
+    arithmetic) against the specification's code for every bf16 amax from +0 to +inf,
+    negative zero and negative values (the sign is ignored) included."""
+    x = _every_amax_blocks()
+    _, sf_ref = oracle.quantize(x, gs)
+    rows, K = x.shape
+    ref = oracle.sf_unpack(sf_ref, rows, K).reshape(-1)[: 0x7F81]
+    vals = np.arange(0, 0x7F81, dtype=np.uint16)
+    for amax in (vals, vals | np.uint16(0x8000)):
+        t = torch.from_numpy(amax.view(np.int16)).to(cuda_dev)
+        codes = torch.empty(len(vals), dtype=torch.uint8, device=cuda_dev)
+        g = torch.tensor([gs], dtype=torch.float32, device=cuda_dev)
+        st = nv.lib().nvfp4_scale_codes(t.data_ptr(), len(vals), g.data_ptr(), codes.data_ptr(),
+                                        torch.cuda.current_stream(cuda_dev).cuda_stream)
+        assert st == 0
+        torch.cuda.synchronize()
+        got = codes.cpu().numpy()
+        bad = np.nonzero(got != ref)[0]
+        assert bad.size == 0, [(hex(int(amax[i])), int(got[i]), int(ref[i])) for i in bad[:8]]
+
+
 @pytest.mark.parametrize("gs", [0.0, float("nan"), -1.0, 2.0 ** -120])
 def test_unusable_global_scale(nv, oracle, cuda_dev, gs):
     x = oracle.normal_bf16((128, 128), seed=9)
