@@ -166,13 +166,14 @@ def in_kernel_clock(nv, operands, d, M, N, K, dev):
     """SM clock the GEMM itself runs at: one launch of the traced CTA-pair kernel on
     the bench's operands, clock64 cycles over globaltimer ns of each pair's MMA thread."""
     a, sfa, b, sfb, alpha = operands
-    tr = torch.zeros(148 * 12, dtype=torch.int64, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count  # one trace row per CTA, grid <= #SMs
+    tr = torch.zeros(sms * 12, dtype=torch.int64, device=dev)
     st = nv.lib().nvfp4_gemm_trace(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), alpha, d.data_ptr(),
                                    M, N, K, tr.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
     torch.cuda.synchronize()
     if st != 0:
         return None
-    t = tr.view(148, 12)[0::2].double().cpu()
+    t = tr.view(sms, 12)[0::2].double().cpu()
     ok = t[:, 7] > 0
     return float((t[ok, 6] / t[ok, 7]).mean() * 1e3) if ok.any() else None
 

@@ -65,7 +65,8 @@ def trace(M: int, N: int, K: int, reps: int = 3, epi: str = "none"):
     E = Epilogue(bias=bias.data_ptr() if with_bias else None, activation=ACTIVATIONS[act],
                  q_out=q.data_ptr() if fp4 else None, sf_out=sfo.data_ptr() if fp4 else None,
                  out_global_scale=gs.data_ptr() if fp4 else None)
-    tr = torch.zeros(148 * slots, dtype=torch.int64, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count  # one trace row per CTA, grid <= #SMs
+    tr = torch.zeros(sms * slots, dtype=torch.int64, device=dev)
     s = torch.cuda.current_stream().cuda_stream
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for i in range(reps):
@@ -75,7 +76,7 @@ def trace(M: int, N: int, K: int, reps: int = 3, epi: str = "none"):
                                              d.data_ptr(), M, N, K, C.byref(E), tr.data_ptr(), s), "trace")
     e1.record()
     torch.cuda.synchronize()
-    t = tr.view(148, slots).cpu()
+    t = tr.view(sms, slots).cpu()
     ctas = int((t[:, 8] > 0).sum())
     t = t[:ctas]
     leaders = t[0::2]
@@ -116,7 +117,7 @@ def decode_trace(M: int, N: int, K: int, calls: int = 8, sets: int = 3):
     d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
     ws_bytes = _l().nvfp4_gemm_decode_workspace_size(M, N)
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
-    grid = 148
+    grid = torch.cuda.get_device_properties(dev).multi_processor_count  # grid <= #SMs
     tr = torch.zeros(calls, grid * 6, dtype=torch.int64, device=dev)
     s = torch.cuda.Stream()
 

@@ -269,7 +269,8 @@ NVFP4_API int nvfp4_gemm_decode_noalloc(const uint8_t *A, const uint8_t *SFA, co
  * an unused per-SM event recorder, matmul/sm100_nvfp4/profiler.cuh:4-72).
  *
  * nvfp4_gemm_trace: the CTA-pair GEMM with a per-CTA cycle trace written to
- * `trace` (device, 148 x 12 uint64): [0] MMA wait on full stages, [1] MMA wait on
+ * `trace` (device, #SMs x 12 uint64; the grid is at most one CTA per SM): [0] MMA
+ * wait on full stages, [1] MMA wait on
  * a free accumulator, [2] producer wait on empty stages, [3] epilogue wait on a
  * full accumulator, [4] epilogue drain + stores, [5] tiles, [6] MMA-thread span
  * in cycles, [7] the same in ns, [8]/[9] %globaltimer at CTA entry/exit,
