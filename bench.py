@@ -534,6 +534,45 @@ def moe_section(nv, dev, reps=20):
                      "rows_per_expert": counts_d.tolist(), "ms": dec_ms, "weight_bytes": w_bytes,
                      "hbm_gbs": w_bytes / (dec_ms / 1e3) / 1e9,
                      "per_expert_decode_calls_ms": loop_ms, "per_expert_hbm_gbs": w_bytes / (loop_ms / 1e3) / 1e9}
+
+    # The expert FFN around the GEMM: up-projection with SiLU and NVFP4 output in the
+    # grouped scale layout (one kernel), then the down-projection W_down [G*K, N]
+    # reading that output as its A operand; beside it the unfused sequence (bf16
+    # up-projection with SiLU, quantize_grouped, down-projection).
+    wdq = torch.empty(G * K, N // 2, dtype=torch.uint8, device=dev)
+    wdsf = torch.empty(G * nv.sf_bytes(K, N), dtype=torch.uint8, device=dev)
+    gs_down = torch.empty(G, dtype=torch.float32, device=dev)  # each expert's W_down global scale
+    for e in range(G):
+        w = (torch.randn(K, N, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        _, gw = nv.global_scale(w)
+        nv.quantize(w, gw, q_out=wdq[e * K:(e + 1) * K], sf_out=wdsf[e * nv.sf_bytes(K, N):(e + 1) * nv.sf_bytes(K, N)])
+        gs_down[e:e + 1] = gw
+        del w
+    ffn = {"what": "expert FFN up (N=14336, K=4096) + SiLU -> NVFP4 -> down (N=4096, K=14336), 8 experts"}
+    for name, (qq, ss, oo, mm) in (("prefill_8192_rows", (q, sf, offs, m_total)),
+                                   ("decode_64_rows", (qd, sfd, offs_d, m_d))):
+        h = nv.gemm_grouped_epilogue(qq, ss, bq, bsf, alphas, oo, activation="silu")
+        _, gh = nv.global_scale(h)  # the hidden activations' global scale (calibrated once)
+        alphas_d = gs_down * gh     # expert e's down-projection alpha: gs(h) * gs(W_down[e])
+        hq = torch.empty(mm, N // 2, dtype=torch.uint8, device=dev)
+        hsf = torch.empty(nv.grouped_sf_bytes(mm, G, N), dtype=torch.uint8, device=dev)
+        y = torch.empty(mm, K, dtype=torch.bfloat16, device=dev)
+
+        def fused():
+            nv.gemm_grouped_epilogue(qq, ss, bq, bsf, alphas, oo, activation="silu", out_global_scale=gh,
+                                     q_out=hq, sf_out=hsf)
+            nv.gemm_grouped(hq, hsf, wdq, wdsf, alphas_d, oo, out=y)
+
+        def unfused():
+            nv.gemm_grouped_epilogue(qq, ss, bq, bsf, alphas, oo, activation="silu", out=h)
+            nv.quantize_grouped(h, gh, oo, q_out=hq, sf_out=hsf)
+            nv.gemm_grouped(hq, hsf, wdq, wdsf, alphas_d, oo, out=y)
+
+        f_ms, u_ms = timed(fused), timed(unfused)
+        flops_ffn = 2.0 * 2 * mm * N * K
+        ffn[name] = {"fused_ms": f_ms, "unfused_ms": u_ms, "fused_tflops": flops_ffn / (f_ms / 1e3) / 1e12}
+    nv.device_status()
+    out["ffn"] = ffn
     return out
 
 

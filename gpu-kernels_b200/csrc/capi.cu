@@ -23,9 +23,11 @@ int gather_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, cons
 size_t decode_grouped_workspace_bytes(int m_total, int N, int groups);
 int decode_grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
                             const float *alphas, uint16_t *D, const int *m_offsets, int groups, int m_total, int N,
-                            int K, void *ws, size_t ws_bytes, cudaStream_t stream);
+                            int K, void *ws, size_t ws_bytes, cudaStream_t stream, const Epi &epi);
 int grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const float *alphas,
-                     uint16_t *D, const int *m_offsets, int groups, int m_total, int N, int K, cudaStream_t stream);
+                     uint16_t *D, const int *m_offsets, int groups, int m_total, int N, int K, cudaStream_t stream,
+                     const Epi &epi);
+int grouped_sf_pad_zero(uint8_t *SF, const int *m_offsets, int groups, int m_total, int K, cudaStream_t s);
 int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                   int M, int N, int K, cudaStream_t stream, bool f16);
 size_t decode_workspace_bytes(int M, int N);
@@ -152,19 +154,44 @@ int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, 
     return sf_pad_zero(e.sf, M, N, s, di);  // the output's scale padding rows
 }
 
-int nvfp4_gemm_grouped(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const float *alpha,
-                       uint16_t *D, const int32_t *m_offsets, int groups, int m_total, int N, int K, void *stream) {
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // at most 128 rows in all (decode): the stream-K kernel that reads only the active
-    // experts' weights; otherwise the CTA-pair kernel's grouped scheduler
+}  // extern "C"
+
+// Grouped GEMM with an optional fused epilogue (bias rows per group).  At most 128
+// rows in all (decode): the stream-K kernel that reads only the active experts'
+// weights; otherwise the CTA-pair kernel's grouped scheduler.
+static int gemm_grouped_epi(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+                            const float *alpha, uint16_t *D, const int32_t *m_offsets, int groups, int m_total, int N,
+                            int K, cudaStream_t s, const Epi &e) {
     if (m_total >= 1 && m_total <= decode_max_m() && groups >= 1 && groups <= 256 && N >= 128 && N % 128 == 0) {
         void *ws = nullptr;
         size_t bytes = 0;
         int st = internal_workspace(decode_grouped_workspace_bytes(m_total, N, groups), s, &ws, &bytes);
         if (st) return st;
-        return decode_grouped_dispatch(A, SFA, B, SFB, alpha, D, m_offsets, groups, m_total, N, K, ws, bytes, s);
+        return decode_grouped_dispatch(A, SFA, B, SFB, alpha, D, m_offsets, groups, m_total, N, K, ws, bytes, s, e);
     }
-    return grouped_dispatch(A, SFA, B, SFB, alpha, D, m_offsets, groups, m_total, N, K, s);
+    return grouped_dispatch(A, SFA, B, SFB, alpha, D, m_offsets, groups, m_total, N, K, s, e);
+}
+
+extern "C" {
+
+int nvfp4_gemm_grouped(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const float *alpha,
+                       uint16_t *D, const int32_t *m_offsets, int groups, int m_total, int N, int K, void *stream) {
+    return gemm_grouped_epi(A, SFA, B, SFB, alpha, D, m_offsets, groups, m_total, N, K,
+                            static_cast<cudaStream_t>(stream), Epi());
+}
+
+int nvfp4_gemm_grouped_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
+                                const float *alpha, uint16_t *D, const int32_t *m_offsets, int groups, int m_total,
+                                int N, int K, const nvfp4_epilogue *epi, void *stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    Epi e;
+    if (epi) {
+        int st = epilogue_from(epi, N, &e);
+        if (st) return st;
+    }
+    int st = gemm_grouped_epi(A, SFA, B, SFB, alpha, D, m_offsets, groups, m_total, N, K, s, e);
+    if (st || !e.q) return st;
+    return grouped_sf_pad_zero(e.sf, m_offsets, groups, m_total, N, s);  // each group's scale padding rows
 }
 
 int nvfp4_gemm_gather(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, int M,

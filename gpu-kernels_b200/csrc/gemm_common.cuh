@@ -207,8 +207,7 @@ __device__ __forceinline__ float bias_elem(const uint4 &b, int j) {
 // straight-line code per 16-column chunk.  Lanes need not agree on anything here.
 template <int kCols, int ACT, bool BIAS>
 __device__ __forceinline__ void store_row_act(const uint32_t (&acc)[kCols], const Params &p, int row, int col0,
-                                              int row_end, float alpha) {
-    const uint16_t *bias = p.epi.bias;
+                                              int row_end, float alpha, const uint16_t *bias) {
     const bool row_ok = row < row_end;
     uint8_t *drow = static_cast<uint8_t *>(p.d) + ((int64_t)row * p.N + col0) * 2;
 #pragma unroll
@@ -243,11 +242,13 @@ __device__ __forceinline__ void store_row_act(const uint32_t (&acc)[kCols], cons
 // The NVFP4-output form of store_row_act: per 16-element block the bf16-rounded
 // values, their amax, the scale code from the per-CTA tables (no division) and the
 // codes — the bytes store_row_epi (and nvfp4_quantize of the bf16 values) gives.
-// col0 and N multiples of 64.
+// col0 and N multiples of 64.  The row's scales go to row sf_row of the blocked
+// scale tensor (the row itself, or its place in a grouped layout).
 template <int kCols, int ACT, bool BIAS>
 __device__ __forceinline__ void store_row_act_nvfp4(const uint32_t (&acc)[kCols], const Params &p, int row,
-                                                    int col0, int row_end, float alpha, const ScaleTables *tab,
-                                                    ScaleGuess guess, bool gs_ok) {
+                                                    int col0, int row_end, float alpha, const uint16_t *bias,
+                                                    int64_t sf_row, const ScaleTables *tab, ScaleGuess guess,
+                                                    bool gs_ok) {
     static_assert(kCols % 64 == 0, "whole 64-column k-groups");
     const Epi &e = p.epi;
     const bool row_ok = row < row_end;
@@ -260,8 +261,8 @@ __device__ __forceinline__ void store_row_act_nvfp4(const uint32_t (&acc)[kCols]
         for (int b = 0; b < 4; b++) {
             uint4 b0 = make_uint4(0u, 0u, 0u, 0u), b1 = b0;
             if constexpr (BIAS) {
-                b0 = bias8(e.bias, p.N, c0 + b * 16);
-                b1 = bias8(e.bias, p.N, c0 + b * 16 + 8);
+                b0 = bias8(bias, p.N, c0 + b * 16);
+                b1 = bias8(bias, p.N, c0 + b * 16 + 8);
             }
             uint32_t pk[8];
             float amax = 0.0f;
@@ -291,7 +292,7 @@ __device__ __forceinline__ void store_row_act_nvfp4(const uint32_t (&acc)[kCols]
         }
         if (row_ok && c0 < p.N) {
             st_global_v8(e.q + (int64_t)row * (p.N >> 1) + (c0 >> 1), codes);
-            *reinterpret_cast<uint32_t *>(e.sf + sf_group_offset(row, c0 >> 6, rest)) = scales;
+            *reinterpret_cast<uint32_t *>(e.sf + sf_group_offset(sf_row, c0 >> 6, rest)) = scales;
         }
     }
 }
@@ -299,22 +300,27 @@ __device__ __forceinline__ void store_row_act_nvfp4(const uint32_t (&acc)[kCols]
 // The fused epilogue of one row, dispatched once per tile to the body compiled for
 // this launch's activation, bias and output type.  tab / guess / gs_ok: the NVFP4
 // output's scale tables (unused for bf16 output).  NVFP4 output needs kCols % 64 == 0
-// (the launch rejects it otherwise).
+// (the launch rejects it otherwise).  bias: the bias row of this tile (the expert's
+// in a grouped launch, nullptr for none); sf_row: the row's scale row.
 template <int kCols>
 __device__ __forceinline__ void store_row_epi_fast(const uint32_t (&acc)[kCols], const Params &p, int row, int col0,
-                                                   int row_end, float alpha, const ScaleTables *tab, ScaleGuess guess,
-                                                   bool gs_ok) {
+                                                   int row_end, float alpha, const uint16_t *bias_row, int64_t sf_row,
+                                                   const ScaleTables *tab, ScaleGuess guess, bool gs_ok) {
     const Epi &e = p.epi;
-    const bool bias = e.bias != nullptr;
+    const bool bias = bias_row != nullptr;
 #define NVFP4_EPI_BODY(A)                                                                                         \
     if (e.q) {                                                                                                    \
         if constexpr (kCols % 64 == 0) {                                                                          \
-            if (bias) store_row_act_nvfp4<kCols, A, true>(acc, p, row, col0, row_end, alpha, tab, guess, gs_ok); \
-            else store_row_act_nvfp4<kCols, A, false>(acc, p, row, col0, row_end, alpha, tab, guess, gs_ok);     \
+            if (bias)                                                                                             \
+                store_row_act_nvfp4<kCols, A, true>(acc, p, row, col0, row_end, alpha, bias_row, sf_row, tab,     \
+                                                    guess, gs_ok);                                                \
+            else                                                                                                  \
+                store_row_act_nvfp4<kCols, A, false>(acc, p, row, col0, row_end, alpha, bias_row, sf_row, tab,    \
+                                                     guess, gs_ok);                                               \
         }                                                                                                         \
     } else {                                                                                                      \
-        if (bias) store_row_act<kCols, A, true>(acc, p, row, col0, row_end, alpha);                               \
-        else store_row_act<kCols, A, false>(acc, p, row, col0, row_end, alpha);                                   \
+        if (bias) store_row_act<kCols, A, true>(acc, p, row, col0, row_end, alpha, bias_row);                     \
+        else store_row_act<kCols, A, false>(acc, p, row, col0, row_end, alpha, bias_row);                         \
     }
     switch (e.act) {
         case kActRelu: NVFP4_EPI_BODY(kActRelu) break;

@@ -64,7 +64,9 @@ struct Layout {
     static constexpr int kOffBar = kOffSfx + STAGES * kSfx;
     static constexpr int kBarBytes = (2 * STAGES + 5) * 8 + 32;  // full, empty, acc_full x2, acc_empty x2, drain
     static constexpr int kOffGroups = (kOffBar + kBarBytes + 15) / 16 * 16;
-    static constexpr int kDynamicSmem = kOffGroups + kGroupBytes + 1024;
+    // the NVFP4 output's scale-code tables (quant_common.cuh), built by the epilogue warps
+    static constexpr int kOffTable = kOffGroups + kGroupBytes;
+    static constexpr int kDynamicSmem = kOffTable + (int)sizeof(ScaleTables) + 1024;
     static constexpr int kSfColsPerStage = kKGroups * 8;  // SFw 4 + SFx 4 per k-group
     // TMEM: two accumulators of MPAD columns (the MMAs of the next tile segment run
     // while the epilogue drains this one), then two sets of scale columns
@@ -137,6 +139,86 @@ __device__ __forceinline__ int64_t range_begin(int64_t c, const Sched &q) { retu
 // CTA whose range holds iteration `it` (ranges are [begin(c), begin(c+1))).
 __device__ __forceinline__ int owner_of(int64_t it, const Sched &q) {
     return (int)(((it + 1) * q.grid - 1) / q.sk_iters);
+}
+
+// Fused epilogue of one output column n (this thread's weight row) over the tile's
+// activation rows m < rows, compiled per activation and bias.  bf16 output:
+template <int MPAD, int ACT, bool BIAS>
+__device__ __forceinline__ void store_col_act(const float (&sum)[MPAD], uint16_t *d, int N, int n, int rows,
+                                              int d_row0, float alpha, float bias_n) {
+    if (n >= N) return;
+#pragma unroll
+    for (int m = 0; m < MPAD; m++)
+        if (m < rows) {
+            __nv_bfloat16 v = __float2bfloat16_rn(epi_t<ACT, BIAS>(sum[m], alpha, bias_n));
+            d[(int64_t)(d_row0 + m) * N + n] = *reinterpret_cast<uint16_t *>(&v);
+        }
+}
+
+// NVFP4 output: a 16-element scale block of row m is 16 consecutive n, i.e. 16 lanes
+// of the warp (N % 64 == 0, so a block is all in or all out of range); its amax by
+// shuffles, its scale code from the per-CTA tables (no division).  Rows go in chunks
+// of 8 computed unconditionally (only the stores check m < rows), so the shuffle
+// chains of 8 rows overlap; `rows` is uniform over the warp, so every lane takes part
+// in every shuffle.
+template <int MPAD, int ACT, bool BIAS>
+__device__ __forceinline__ void store_col_act_nvfp4(const float (&sum)[MPAD], const Epi &e, int N, int n, int lane,
+                                                    int rows, int d_row0, int sf_row0, float alpha, float bias_n,
+                                                    const ScaleTables *tab, ScaleGuess guess, bool gs_ok) {
+    constexpr int kChunk = MPAD < 8 ? MPAD : 8;
+    const bool valid = n < N;
+    const int64_t rest = N >> 6;
+#pragma unroll
+    for (int m0 = 0; m0 < MPAD; m0 += kChunk) {
+        if (m0 >= rows) break;
+        float v[kChunk], amax[kChunk];
+#pragma unroll
+        for (int i = 0; i < kChunk; i++) {
+            v[i] = valid ? round_bf16(epi_t<ACT, BIAS>(sum[m0 + i], alpha, bias_n)) : 0.0f;
+            amax[i] = fabsf(v[i]);
+        }
+#pragma unroll
+        for (int o = 8; o; o >>= 1)
+#pragma unroll
+            for (int i = 0; i < kChunk; i++) amax[i] = fmaxf(amax[i], __shfl_xor_sync(0xffffffffu, amax[i], o));
+#pragma unroll
+        for (int i = 0; i < kChunk; i++) {
+            const int m = m0 + i;
+            const uint32_t code = table_scale_code(amax[i], guess, tab, gs_ok);
+            const uint32_t q4 = e2m1x2(__fmul_rn(v[i], tab->inv[code]), 0.0f) & 0xFu;
+            const uint32_t hi = __shfl_down_sync(0xffffffffu, q4, 1);
+            if (m < rows && valid && !(lane & 1))
+                e.q[(int64_t)(d_row0 + m) * (N >> 1) + (n >> 1)] = (uint8_t)(q4 | (hi << 4));
+            if (m < rows && valid && !(lane & 15))
+                e.sf[sf_group_offset(sf_row0 + m, n >> 6, rest) + ((n >> 4) & 3)] = (uint8_t)code;
+        }
+    }
+}
+
+template <int MPAD>
+__device__ __forceinline__ void store_col_epi(const float (&sum)[MPAD], const Epi &e, uint16_t *d, int N, int n,
+                                              int lane, int rows, int d_row0, int sf_row0, float alpha, float bias_n,
+                                              const ScaleTables *tab, ScaleGuess guess, bool gs_ok) {
+    const bool bias = e.bias != nullptr;
+#define NVFP4_DECODE_EPI_BODY(A)                                                                                 \
+    if (e.q) {                                                                                                   \
+        if (bias)                                                                                                \
+            store_col_act_nvfp4<MPAD, A, true>(sum, e, N, n, lane, rows, d_row0, sf_row0, alpha, bias_n, tab,    \
+                                               guess, gs_ok);                                                    \
+        else                                                                                                     \
+            store_col_act_nvfp4<MPAD, A, false>(sum, e, N, n, lane, rows, d_row0, sf_row0, alpha, bias_n, tab,   \
+                                                guess, gs_ok);                                                   \
+    } else {                                                                                                     \
+        if (bias) store_col_act<MPAD, A, true>(sum, d, N, n, rows, d_row0, alpha, bias_n);                       \
+        else store_col_act<MPAD, A, false>(sum, d, N, n, rows, d_row0, alpha, bias_n);                          \
+    }
+    switch (e.act) {
+        case kActRelu: NVFP4_DECODE_EPI_BODY(kActRelu) break;
+        case kActSilu: NVFP4_DECODE_EPI_BODY(kActSilu) break;
+        case kActGeluTanh: NVFP4_DECODE_EPI_BODY(kActGeluTanh) break;
+        default: NVFP4_DECODE_EPI_BODY(kActNone) break;
+    }
+#undef NVFP4_DECODE_EPI_BODY
 }
 
 template <int MPAD, bool GROUPED, bool COLOC>
@@ -223,6 +305,8 @@ __global__ void __launch_bounds__(kThreads, COLOC ? 2 : 1)
         int w_row, x_row, d_row0, rows, ncol0;
         int64_t sfw_block, sfx_block;
         float alpha;
+        int group;    // the tile's group (0 when not grouped): its bias row
+        int sf_row0;  // NVFP4 output: scale row of the tile's first output row
     };
     auto dtile = [&](int T) {
         DTile d;
@@ -236,6 +320,8 @@ __global__ void __launch_bounds__(kThreads, COLOC ? 2 : 1)
             d.rows = g_r1[g] - g_r0[g];
             d.ncol0 = t * kTileN;
             d.alpha = p.alphas[g];
+            d.group = g;
+            d.sf_row0 = g_b0[g] * 128;
         } else {
             d.w_row = T * kTileN;
             d.sfw_block = T;
@@ -245,6 +331,8 @@ __global__ void __launch_bounds__(kThreads, COLOC ? 2 : 1)
             d.rows = p.M;
             d.ncol0 = T * kTileN;
             d.alpha = p.alpha;
+            d.group = 0;
+            d.sf_row0 = 0;
         }
         return d;
     };
@@ -381,6 +469,18 @@ __global__ void __launch_bounds__(kThreads, COLOC ? 2 : 1)
         const int quarter = warp & 3;
         const int nl = quarter * 32 + lane;  // row of the weight tile this thread owns
         const int etid = threadIdx.x - 64;   // 0..127
+        // NVFP4 output: the scale-code tables of the output's global scale (read after
+        // the wait on the preceding kernel, which may have written it)
+        ScaleTables *tab = reinterpret_cast<ScaleTables *>(base_ptr + L::kOffTable);
+        ScaleGuess guess{0.0f, 1.0f};
+        bool gs_ok = false;
+        if (p.epi.q) {
+            const float gs = *p.epi.gs;
+            gs_ok = gs_usable(gs);
+            guess = scale_guess_factor(gs);
+            build_scale_tables(tab, gs, etid, 128);
+            named_barrier(1, 128);
+        }
         int seg = 0;
         for (int64_t v = 0; v < n_iters; seg++) {
             const int64_t it = iter(v);
@@ -458,40 +558,12 @@ __global__ void __launch_bounds__(kThreads, COLOC ? 2 : 1)
                             p.d[(int64_t)(dt.d_row0 + m) * p.N + n] = *reinterpret_cast<uint16_t *>(&v);
                         }
                 }
-            } else if (!p.epi.q) {
-                if (n < p.N) {
-                    const float bias_n = p.epi.bias ? bf16_bits_to_float(p.epi.bias[n]) : 0.0f;
-#pragma unroll
-                    for (int m = 0; m < MPAD; m++)
-                        if (m < p.M) {
-                            __nv_bfloat16 v = __float2bfloat16_rn(epi_value(sum[m], p.alpha, p.epi, bias_n));
-                            p.d[(int64_t)m * p.N + n] = *reinterpret_cast<uint16_t *>(&v);
-                        }
-                }
             } else {
-                // NVFP4 output: a 16-element scale block of row m is 16 consecutive n,
-                // i.e. 16 lanes of this warp (N % 64 == 0, so a block is all in or all
-                // out of range).  Every lane takes part in the shuffles.
-                const float gs = *p.epi.gs;
-                const bool gs_ok = gs_usable(gs);
-                const bool valid = n < p.N;
-                const float bias_n = (valid && p.epi.bias) ? bf16_bits_to_float(p.epi.bias[n]) : 0.0f;
-                const int64_t rest = p.N >> 6;
-#pragma unroll
-                for (int m = 0; m < MPAD; m++) {
-                    if (m < p.M) {
-                        const float v = valid ? round_bf16(epi_value(sum[m], p.alpha, p.epi, bias_n)) : 0.0f;
-                        float amax = fabsf(v);
-#pragma unroll
-                        for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-                        const uint32_t code = block_scale_code(amax, gs, gs_ok);
-                        const uint32_t q4 = e2m1x2(__fmul_rn(v, block_inverse(code, gs, gs_ok)), 0.0f) & 0xFu;
-                        const uint32_t hi = __shfl_down_sync(0xffffffffu, q4, 1);
-                        if (valid && !(lane & 1)) p.epi.q[(int64_t)m * (p.N >> 1) + (n >> 1)] = (uint8_t)(q4 | (hi << 4));
-                        if (valid && !(lane & 15))
-                            p.epi.sf[sf_group_offset(m, n >> 6, rest) + ((n >> 4) & 3)] = (uint8_t)code;
-                    }
-                }
+                const float bias_n = (n < p.N && p.epi.bias)
+                                         ? bf16_bits_to_float(p.epi.bias[(int64_t)dt.group * p.N + n])
+                                         : 0.0f;
+                store_col_epi<MPAD>(sum, p.epi, p.d, p.N, n, lane, dt.rows, dt.d_row0, dt.sf_row0, dt.alpha, bias_n,
+                                    tab, guess, gs_ok);
             }
         }
     }
@@ -686,12 +758,12 @@ size_t decode_grouped_workspace_bytes(int m_total, int N, int groups) {
 // the split-K workspace (decode_grouped_workspace_bytes, zero-filled once).
 int decode_grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
                             const float *alphas, uint16_t *D, const int *m_offsets, int groups, int m_total, int N,
-                            int K, void *ws, size_t ws_bytes, cudaStream_t stream) {
-    if (!A || !SFA || !B || !SFB || !alphas || !D || !m_offsets) return NVFP4_ERR_INVALID;
+                            int K, void *ws, size_t ws_bytes, cudaStream_t stream, const Epi &epi) {
+    if (!A || !SFA || !B || !SFB || !alphas || (!D && !epi.q) || !m_offsets) return NVFP4_ERR_INVALID;
     if (groups < 1 || groups > gemm::kMaxGroups || m_total < 1 || m_total > 128 || N < 128 || N % 128 || K < 64 ||
         K % 64)
         return NVFP4_ERR_SHAPE;
-    if (!aligned16(A) || !aligned16(SFA) || !aligned16(B) || !aligned16(SFB) || !aligned16(D) ||
+    if (!aligned16(A) || !aligned16(SFA) || !aligned16(B) || !aligned16(SFB) || (D && !aligned16(D)) ||
         (reinterpret_cast<uintptr_t>(alphas) & 3u) || (reinterpret_cast<uintptr_t>(m_offsets) & 3u))
         return NVFP4_ERR_ALIGN;
     DeviceInfo di;
@@ -703,7 +775,7 @@ int decode_grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t 
     switch (decode::mpad_for(m_total)) {
 #define NVFP4_GROUPED_DECODE(MP)                                                                                   \
     case MP:                                                                                                       \
-        return decode::launch<MP, true>(A, SFA, B, SFB, 1.0f, D, m_total, N, K, ws, stream, di, Epi(), nullptr,   \
+        return decode::launch<MP, true>(A, SFA, B, SFB, 1.0f, D, m_total, N, K, ws, stream, di, epi, nullptr,     \
                                         m_offsets, alphas, groups);
         NVFP4_GROUPED_DECODE(8)
         NVFP4_GROUPED_DECODE(16)

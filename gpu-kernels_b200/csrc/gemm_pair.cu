@@ -111,6 +111,8 @@ struct TileInfo {
     int b_row0;      // first B row of the tile's weight matrix
     int sfb_block0;  // its first 128-row scale block
     float alpha;
+    int group;       // grouped launch: the tile's group (else 0)
+    int sf_row_off;  // NVFP4 output: scale row of D row r is r + sf_row_off (per-group layout)
 };
 
 template <int STAGES, int BKB, int BN, bool F16, bool TRACE>
@@ -228,6 +230,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             ti.b_row0 = 0;
             ti.sfb_block0 = 0;
             ti.alpha = p.alpha;
+            ti.group = 0;
+            ti.sf_row_off = 0;
         } else {
             const int g = last_group_at_or_before(g_tile0, G, t);  // g_tile0[g] <= t < g_tile0[g + 1]
             const int r0 = g_row0[g], r1 = g_rend[g];
@@ -238,6 +242,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             ti.b_row0 = g * p.N;
             ti.sfb_block0 = g * (p.N >> 7);
             ti.alpha = p.grouped.alphas[g];
+            ti.group = g;
+            ti.sf_row_off = g_sfa0[g] * 128 - r0;
         }
         return ti;
     };
@@ -574,13 +580,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 } else if (p.epi.plain()) {
                     store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha);
                 } else if constexpr (!F16) {
-                    store_row_epi_fast<kCols>(acc, p, row, col0, ti.row_end, ti.alpha, tab, guess, gs_ok);
+                    store_row_epi_fast<kCols>(acc, p, row, col0, ti.row_end, ti.alpha,
+                                              p.epi.bias ? p.epi.bias + (int64_t)ti.group * p.N : nullptr,
+                                              row + ti.sf_row_off, tab, guess, gs_ok);
                 }
             } else {
                 if (p.epi.plain())
                     store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha);
                 else if constexpr (!F16)
-                    store_row_epi_fast<kCols>(acc, p, row, col0, ti.row_end, ti.alpha, tab, guess, gs_ok);
+                    store_row_epi_fast<kCols>(acc, p, row, col0, ti.row_end, ti.alpha,
+                                              p.epi.bias ? p.epi.bias + (int64_t)ti.group * p.N : nullptr,
+                                              row + ti.sf_row_off, tab, guess, gs_ok);
             }
             if (TRACE && warp == 2 && lane == 0) t_store += clock64() - c_ready;
         }
@@ -784,11 +794,12 @@ int pair_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
 
 // Grouped (mixture-of-experts) GEMM on the CTA-pair kernel, bf16 output.
 int grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const float *alphas,
-                     uint16_t *D, const int *m_offsets, int groups, int m_total, int N, int K, cudaStream_t stream) {
-    if (!A || !SFA || !B || !SFB || !alphas || !D || !m_offsets) return NVFP4_ERR_INVALID;
+                     uint16_t *D, const int *m_offsets, int groups, int m_total, int N, int K, cudaStream_t stream,
+                     const Epi &epi) {
+    if (!A || !SFA || !B || !SFB || !alphas || (!D && !epi.q) || !m_offsets) return NVFP4_ERR_INVALID;
     if (groups < 1 || groups > gemm::kMaxGroups || m_total < 1 || N < 128 || N % 128 || K < 64 || K % 64)
         return NVFP4_ERR_SHAPE;
-    if (!aligned16(A) || !aligned16(SFA) || !aligned16(B) || !aligned16(SFB) || !aligned16(D) ||
+    if (!aligned16(A) || !aligned16(SFA) || !aligned16(B) || !aligned16(SFB) || (D && !aligned16(D)) ||
         (reinterpret_cast<uintptr_t>(alphas) & 3u) || (reinterpret_cast<uintptr_t>(m_offsets) & 3u))
         return NVFP4_ERR_ALIGN;
     DeviceInfo di;
@@ -799,8 +810,8 @@ int grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, con
     grp.alphas = alphas;
     grp.groups = groups;
     grp.m_total = m_total;
-    return gemm::launch_pair<5, 128, 256, false>(A, SFA, B, SFB, 1.0f, D, m_total, N, K, stream, di, nullptr, Epi(),
-                                                 grp);
+    return gemm::launch_pair<5, 128, 256, false>(A, SFA, B, SFB, 1.0f, epi.q ? static_cast<void *>(epi.q) : D,
+                                                 m_total, N, K, stream, di, nullptr, epi, grp);
 }
 
 // Column-parallel GEMM with the all-gather fused into the epilogue (bf16 output):

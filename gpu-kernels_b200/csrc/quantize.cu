@@ -160,7 +160,10 @@ __global__ void __launch_bounds__(256) quantize_grouped_kernel(const __nv_bfloat
     }
 }
 
-// Zero the padding scale rows [M_g, pad128(M_g)) of every group (one CTA per group).
+// Zero the padding scale rows [M_g, pad128(M_g)) of every group: CTA (g, y) takes pad
+// rows y, y + kPadSlices, ... of group g; a row's k-group holds 4 contiguous scale
+// bytes, so each thread writes whole 32-bit words (32-bit index arithmetic only).
+constexpr int kPadSlices = 16;
 __global__ void grouped_sf_pad_zero_kernel(uint8_t *SF, const int *m_offsets, int G, int m_total, int64_t K) {
     __shared__ int g_r0[kQuantMaxGroups], g_r1[kQuantMaxGroups], g_b0[kQuantMaxGroups + 1];
     if (threadIdx.x < 32) build_group_tables(m_offsets, G, m_total, 0, threadIdx.x & 31, g_r0, g_r1, g_b0, nullptr);
@@ -168,22 +171,20 @@ __global__ void grouped_sf_pad_zero_kernel(uint8_t *SF, const int *m_offsets, in
     const int gr = blockIdx.x;
     const int mg = g_r1[gr] - g_r0[gr];
     const int pad = (mg + 127) / 128 * 128 - mg;
-    const int64_t rest_k = K >> 6, per_row = K >> 4;
-    for (int64_t i = threadIdx.x; i < (int64_t)pad * per_row; i += blockDim.x) {
-        const int64_t r = (int64_t)g_b0[gr] * 128 + mg + i / per_row, k16 = i % per_row;
-        SF[sf_group_offset(r, k16 >> 2, rest_k) + (k16 & 3)] = 0;
+    const int rest_k = (int)(K >> 6);
+    for (int pr = blockIdx.y; pr < pad; pr += gridDim.y) {
+        const int64_t r = (int64_t)g_b0[gr] * 128 + mg + pr;
+        for (int kg = threadIdx.x; kg < rest_k; kg += blockDim.x)
+            *reinterpret_cast<uint32_t *>(SF + sf_group_offset(r, kg, rest_k)) = 0u;
     }
 }
 
-// Zero the scale bytes of rows [M, pad128(M)) (the blocked layout's padding).
+// Zero the scale bytes of rows [M, pad128(M)): one CTA per padding row, 32-bit words.
 __global__ void sf_pad_zero_kernel(uint8_t *SF, int64_t M, int64_t K) {
-    const int64_t rest_k = K >> 6;
-    const int64_t pad_rows = ((M + 127) / 128) * 128 - M;
-    const int64_t total = pad_rows * (K >> 4);
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = M + i / (K >> 4), k16 = i % (K >> 4);
-        SF[((r >> 7) * rest_k + (k16 >> 2)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (k16 & 3)] = 0;
-    }
+    const int64_t r = M + blockIdx.x;
+    const int rest_k = (int)(K >> 6);
+    for (int kg = threadIdx.x; kg < rest_k; kg += blockDim.x)
+        *reinterpret_cast<uint32_t *>(SF + sf_group_offset(r, kg, rest_k)) = 0u;
 }
 
 // amax over n bf16 (n % 8 == 0 handled by the vector loop, the rest scalar).
@@ -236,11 +237,18 @@ __global__ void __launch_bounds__(256) scale_codes_kernel(const uint16_t *__rest
         codes[i] = (uint8_t)table_scale_code(fabsf(__uint_as_float((uint32_t)amax[i] << 16)), guess, &tab, ok);
 }
 
+// Zero the padding scale rows [M_g, pad128(M_g)) of every group of a grouped scale
+// tensor (the layout nvfp4_quantize_grouped writes).
+int grouped_sf_pad_zero(uint8_t *SF, const int *m_offsets, int groups, int m_total, int K, cudaStream_t s) {
+    grouped_sf_pad_zero_kernel<<<dim3(groups, kPadSlices), 256, 0, s>>>(SF, m_offsets, groups, m_total, K);
+    count_launch();
+    return cuda_status(cudaGetLastError());
+}
+
 // Zero the scale bytes of rows [M, pad128(M)) of a blocked [pad128(M), K/16] tensor.
 int sf_pad_zero(uint8_t *SF, int M, int K, cudaStream_t s, const DeviceInfo &di) {
     if (M % 128 == 0) return NVFP4_OK;
-    sf_pad_zero_kernel<<<(unsigned)std::min<int64_t>(di.sm_count, (128 * (int64_t)K / 16 + 255) / 256), 256, 0, s>>>(
-        SF, M, K);
+    sf_pad_zero_kernel<<<(unsigned)((M + 127) / 128 * 128 - M), 256, 0, s>>>(SF, M, K);
     count_launch();
     return cuda_status(cudaGetLastError());
 }
@@ -304,10 +312,9 @@ extern "C" int nvfp4_quantize_grouped(const uint16_t *X, uint8_t *Q, uint8_t *SF
     if (blocks > (int64_t)di.sm_count * 8) blocks = (int64_t)di.sm_count * 8;
     quantize_grouped_kernel<<<(unsigned)blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16 *>(X), Q, SF,
                                                              global_scale, m_offsets, groups, m_total, K);
-    grouped_sf_pad_zero_kernel<<<groups, 256, 0, s>>>(SF, m_offsets, groups, m_total, K);
     count_launch();
-    count_launch();
-    return cuda_status(cudaGetLastError());
+    if ((st = cuda_status(cudaGetLastError()))) return st;
+    return grouped_sf_pad_zero(SF, m_offsets, groups, m_total, K, s);
 }
 
 extern "C" int nvfp4_global_scale(const uint16_t *X, int64_t n, float *amax_out, float *gs_out, void *stream) {

@@ -50,6 +50,8 @@ SIGNATURES = {
                                             C.POINTER(Epilogue), _vp, _vp]),
     "nvfp4_gemm_grouped": (C.c_int, [_u8p, _u8p, _u8p, _u8p, _f32p, _u16p, _vp, C.c_int, C.c_int, C.c_int, C.c_int,
                                      _vp]),
+    "nvfp4_gemm_grouped_epilogue": (C.c_int, [_u8p, _u8p, _u8p, _u8p, _f32p, _u16p, _vp, C.c_int, C.c_int,
+                                              C.c_int, C.c_int, C.POINTER(Epilogue), _vp]),
     "nvfp4_quantize_grouped": (C.c_int, [_u16p, _u8p, _u8p, _f32p, _vp, C.c_int, C.c_int, C.c_int, _vp]),
     "nvfp4_gemm_gather": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, C.c_int, C.c_int, C.c_int,
                                     C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_int64, C.c_int, _vp]),

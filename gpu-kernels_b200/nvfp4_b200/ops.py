@@ -182,6 +182,56 @@ def gemm_grouped(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch
     return d
 
 
+def gemm_grouped_epilogue(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor,
+                          alphas: torch.Tensor, m_offsets: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                          activation: str = "none", out_global_scale: Union[torch.Tensor, float, None] = None,
+                          out: Optional[torch.Tensor] = None, q_out: Optional[torch.Tensor] = None,
+                          sf_out: Optional[torch.Tensor] = None):
+    """gemm_grouped with the fused epilogue (nvfp4_gemm_grouped_epilogue): D =
+    act(alphas[g] * A . B_g^T + bias[g]) per group, bias bf16 [groups, N] (optional).
+    Without `out_global_scale`: returns bf16 D [m_total, N].  With it: returns
+    (codes uint8 [m_total, N/2], scales in the grouped layout of
+    grouped_sf_bytes(m_total, groups, N) bytes) — what quantize_grouped makes of the
+    bf16 result, ready as the A operand of the next grouped GEMM (N % 128 == 0)."""
+    for t, n in ((a, "a"), (sfa, "sfa"), (b, "b"), (sfb, "sfb")):
+        _bytes_tensor(t, n)
+    offs = _offsets_tensor(m_offsets, a.device)
+    G = offs.numel() - 1
+    m_total, K = a.shape[0], a.shape[1] * 2
+    if b.shape[1] * 2 != K or b.shape[0] % G:
+        raise ValueError("B must be [groups * N, K/2] with A's K")
+    N = b.shape[0] // G
+    if sfa.numel() < grouped_sf_bytes(m_total, G, K) or sfb.numel() < G * sf_bytes(N, K):
+        raise ValueError("scale tensors too small for the grouped layout")
+    if alphas.dtype != torch.float32 or alphas.numel() != G or alphas.device != a.device:
+        raise ValueError("alphas must be a float32 tensor of groups entries on the device")
+    if activation not in ACTIVATIONS:
+        raise ValueError(f"activation must be one of {sorted(ACTIVATIONS)}")
+    e = Epilogue()
+    e.activation = ACTIVATIONS[activation]
+    if bias is not None:
+        if bias.dtype != torch.bfloat16 or bias.numel() != G * N or not bias.is_cuda or not bias.is_contiguous():
+            raise ValueError("bias must be a contiguous bf16 CUDA tensor of groups * N elements")
+        e.bias = bias.data_ptr()
+    d = None
+    if out_global_scale is None:
+        d = out if out is not None else torch.zeros(m_total, N, dtype=torch.bfloat16, device=a.device)
+        if d.dtype != torch.bfloat16 or d.shape != (m_total, N) or not d.is_contiguous():
+            raise ValueError("out must be a contiguous bf16 [m_total, N] tensor")
+        d_ptr = d.data_ptr()
+    else:
+        gs = _scale_tensor(out_global_scale, a.device)
+        q = q_out if q_out is not None else torch.zeros(m_total, N // 2, dtype=torch.uint8, device=a.device)
+        sf = sf_out if sf_out is not None else torch.zeros(grouped_sf_bytes(m_total, G, N), dtype=torch.uint8,
+                                                           device=a.device)
+        e.q_out, e.sf_out, e.out_global_scale = q.data_ptr(), sf.data_ptr(), gs.data_ptr()
+        d_ptr = None
+    check(lib().nvfp4_gemm_grouped_epilogue(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(),
+                                            alphas.data_ptr(), d_ptr, offs.data_ptr(), G, m_total, N, K, C.byref(e),
+                                            _stream(a.device)), "nvfp4_gemm_grouped_epilogue")
+    return d if d is not None else (q, sf)
+
+
 def gemm_host(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor, alpha: float,
               out: torch.Tensor, device: Optional[torch.device] = None) -> torch.Tensor:
     """D = alpha * A . B^T from and to HOST tensors (pin them for overlap): uploads,

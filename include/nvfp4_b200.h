@@ -177,6 +177,17 @@ NVFP4_API int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const ui
 NVFP4_API int nvfp4_gemm_grouped(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
                                  const float *alpha, uint16_t *D, const int32_t *m_offsets, int groups,
                                  int m_total, int N, int K, void *stream);
+/* nvfp4_gemm_grouped with the fused epilogue of nvfp4_gemm_epilogue (epi may be
+ * NULL): epi->bias, if given, is [G, N] bf16 (expert g's bias row g); with q_out the
+ * output is NVFP4 — codes [m_total, N/2] in stacked row order, scales in the grouped
+ * layout above (group g's blocked [pad128(M_g), N/16] tensor from 128-row block
+ * sum_{h<g} ceil(M_h/128), padding rows zeroed), i.e. exactly what
+ * nvfp4_quantize_grouped makes of the bf16 output, ready as the A operand of the next
+ * grouped GEMM.  D may then be NULL.  Rows outside every group are not written. */
+NVFP4_API int nvfp4_gemm_grouped_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B,
+                                          const uint8_t *SFB, const float *alpha, uint16_t *D,
+                                          const int32_t *m_offsets, int groups, int m_total, int N, int K,
+                                          const nvfp4_epilogue *epi, void *stream);
 /* bf16 X [m_total, K] -> codes Q [m_total, K/2] and the grouped scale layout above,
  * one global scale for all groups (padding scale rows of every group zeroed). */
 NVFP4_API int nvfp4_quantize_grouped(const uint16_t *X, uint8_t *Q, uint8_t *SF, const float *global_scale,

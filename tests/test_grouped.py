@@ -9,10 +9,15 @@ per-expert scale factors).  The oracle is applied group by group:
   * GEMM: each group's D rows against the oracle GEMM of (A_g, B_g, alpha_g) with
     max|D - D_ref| / max|D_ref| <= 1e-2; rows outside every group untouched;
   * device-side routing: one captured CUDA graph replayed after the offsets change
-    in place follows the new routing.
+    in place follows the new routing;
+  * fused epilogue (nvfp4_gemm_grouped_epilogue): per-expert bias + activation per
+    group against the oracle's epilogue; NVFP4 output byte-identical to
+    quantize_grouped of the fused bf16 output (the next grouped GEMM's operand).
 With at most 128 rows in all (decode) the stream-K kernel runs over the active
 experts' weight tiles only; above that the CTA-pair kernel's grouped scheduler.
 """
+import ctypes as C
+
 import numpy as np
 import pytest
 import torch
@@ -158,3 +163,79 @@ def test_gemm_grouped_graph_follows_device_routing(nv, oracle, cuda_dev):
     got, want = out.float(), ref.float()
     assert (got - want).abs().max().item() <= 1e-2 * want.abs().max().item()
     assert not torch.equal(first, out)
+
+
+def test_grouped_epilogue_host_checks(nv):
+    L = nv.lib()
+    f = 0x10000
+    E = nv._lib.Epilogue
+    call = lambda e, N=256: L.nvfp4_gemm_grouped_epilogue(f, f, f, f, f, f, f, 4, 256, N, 256,  # noqa: E731
+                                                          C.byref(e), None)
+    assert call(E(activation=9)) == -1                                                   # unknown activation
+    assert call(E(bias=f + 8)) == -3                                                     # bias 16-byte aligned
+    assert call(E(q_out=f, sf_out=None, out_global_scale=f)) == -1                       # scales missing
+    assert call(E(q_out=f + 16, sf_out=f, out_global_scale=f)) == -3                     # codes 32-byte aligned
+
+
+EPI_CASES = [CASES[0], CASES[2], CASES[3], CASES[4]]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("offsets,m_total,N,K", EPI_CASES)
+@pytest.mark.parametrize("act", ["relu", "silu", "gelu_tanh"])
+def test_gemm_grouped_epilogue_vs_oracle(nv, oracle, cuda_dev, offsets, m_total, N, K, act):
+    """Per-expert bias + activation fused into the grouped GEMM, each group against the
+    oracle's GEMM and epilogue (max relative error 1e-2)."""
+    x, gsa, offs, q, sf, bq, bsf, alphas = _make(oracle, nv, cuda_dev, offsets, m_total, N, K, seed=11)
+    G = len(offsets) - 1
+    bias = oracle.f32_to_bf16_bits(np.random.default_rng(3).standard_normal((G, N)).astype(np.float32))
+    out = torch.full((m_total, N), 7.0, dtype=torch.bfloat16, device=cuda_dev)
+    d = nv.gemm_grouped_epilogue(q, sf, torch.from_numpy(bq).to(cuda_dev), torch.from_numpy(bsf).to(cuda_dev),
+                                 torch.from_numpy(alphas).to(cuda_dev), offs,
+                                 bias=torch.from_numpy(bias.view(np.int16)).to(cuda_dev).view(torch.bfloat16),
+                                 activation=act, out=out)
+    torch.cuda.synchronize()
+    nv.device_status()
+    got = d.float().cpu().numpy()
+    qh, sfh = q.cpu().numpy(), sf.cpu().numpy()
+    blk = 128 * K // 16
+    block0 = 0
+    covered = np.zeros(m_total, dtype=bool)
+    for g, (a, z) in enumerate(_group_rows(offsets, m_total)):
+        if z == a:
+            continue
+        nb = (z - a + 127) // 128
+        acc, _ = oracle.gemm(qh[a:z], sfh[block0 * blk:(block0 + nb) * blk], bq[g * N:(g + 1) * N],
+                             bsf[g * (N // 128) * blk:(g + 1) * (N // 128) * blk], 1.0, z - a, N, K)
+        _, ref16 = oracle.epilogue(acc.reshape(z - a, N), float(alphas[g]), bias[g], act)
+        ref = oracle.bf16_bits_to_f32(ref16).reshape(z - a, N)
+        err = np.abs(got[a:z] - ref).max() / np.abs(ref).max()
+        assert err <= 1e-2, (g, err)
+        covered[a:z] = True
+        block0 += nb
+    assert (got[~covered] == 7.0).all()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("offsets,m_total,N,K", CASES)
+def test_gemm_grouped_nvfp4_out_equals_quantize_grouped(nv, oracle, cuda_dev, offsets, m_total, N, K):
+    """NVFP4 output of the grouped GEMM (silu, per-expert bias): codes and grouped
+    scales byte-identical to quantize_grouped of the fused bf16 output, so it can be
+    the A operand of the next grouped GEMM as it stands."""
+    x, gsa, offs, q, sf, bq, bsf, alphas = _make(oracle, nv, cuda_dev, offsets, m_total, N, K, seed=13)
+    G = len(offsets) - 1
+    b, sfb, al = (torch.from_numpy(t).to(cuda_dev) for t in (bq, bsf, alphas))
+    bias = torch.randn(G, N, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16).to(cuda_dev)
+    d = nv.gemm_grouped_epilogue(q, sf, b, sfb, al, offs, bias=bias, activation="silu")
+    _, gs = nv.global_scale(d)
+    q2, sf2 = nv.gemm_grouped_epilogue(q, sf, b, sfb, al, offs, bias=bias, activation="silu", out_global_scale=gs)
+    q_ref, sf_ref = nv.quantize_grouped(d, gs, offs)
+    torch.cuda.synchronize()
+    nv.device_status()
+    used = nv.grouped_sf_block0([min(max(o, 0), m_total) for o in offsets])[-1] * 128 * N // 16
+    rows = np.zeros(m_total, dtype=bool)
+    for a, z in _group_rows(offsets, m_total):
+        rows[a:z] = True
+    rows_t = torch.from_numpy(rows).to(cuda_dev)
+    assert torch.equal(q2[rows_t], q_ref[rows_t])
+    assert torch.equal(sf2[:used], sf_ref[:used])
