@@ -108,6 +108,9 @@ int nvfp4_gemm(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uin
 
 }  // extern "C"
 
+// Columns of the epilogue's output for a GEMM of N columns (SwiGLU halves them).
+static int epi_out_cols(const Epi &e, int N) { return e.act == NVFP4_ACT_SWIGLU ? N / 2 : N; }
+
 // The C epilogue description as the kernels' Epi, with its argument checks.
 static int epilogue_from(const nvfp4_epilogue *epi, int N, Epi *out) {
     Epi e;
@@ -116,7 +119,8 @@ static int epilogue_from(const nvfp4_epilogue *epi, int N, Epi *out) {
     e.q = epi->q_out;
     e.sf = epi->sf_out;
     e.gs = epi->out_global_scale;
-    if (e.act < NVFP4_ACT_NONE || e.act > NVFP4_ACT_GELU_TANH) return NVFP4_ERR_INVALID;
+    if (e.act < NVFP4_ACT_NONE || e.act > NVFP4_ACT_SWIGLU) return NVFP4_ERR_INVALID;
+    if (e.act == NVFP4_ACT_SWIGLU && N % 128) return NVFP4_ERR_SHAPE;  // whole 32-column gate / up blocks per warp
     if (e.bias && !aligned16(e.bias)) return NVFP4_ERR_ALIGN;
     if (e.q) {
         if (!e.sf || !e.gs) return NVFP4_ERR_INVALID;
@@ -151,7 +155,7 @@ int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, 
     if (st || !e.q) return st;
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
-    return sf_pad_zero(e.sf, M, N, s, di);  // the output's scale padding rows
+    return sf_pad_zero(e.sf, M, epi_out_cols(e, N), s, di);  // the output's scale padding rows
 }
 
 }  // extern "C"
@@ -191,7 +195,7 @@ int nvfp4_gemm_grouped_epilogue(const uint8_t *A, const uint8_t *SFA, const uint
     }
     int st = gemm_grouped_epi(A, SFA, B, SFB, alpha, D, m_offsets, groups, m_total, N, K, s, e);
     if (st || !e.q) return st;
-    return grouped_sf_pad_zero(e.sf, m_offsets, groups, m_total, N, s);  // each group's scale padding rows
+    return grouped_sf_pad_zero(e.sf, m_offsets, groups, m_total, epi_out_cols(e, N), s);  // padding rows
 }
 
 int nvfp4_gemm_gather(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, int M,

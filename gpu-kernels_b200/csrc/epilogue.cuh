@@ -16,7 +16,9 @@
 
 namespace nvfp4 {
 
-enum : int { kActNone = 0, kActRelu = 1, kActSilu = 2, kActGeluTanh = 3 };
+// kActSwiglu: silu(gate) * up over gate / up columns interleaved in blocks of 16
+// (columns 32j .. 32j+15 gate, 32j+16 .. 32j+31 up); the output has half the columns.
+enum : int { kActNone = 0, kActRelu = 1, kActSilu = 2, kActGeluTanh = 3, kActSwiglu = 4 };
 
 struct Epi {
     const uint16_t *bias = nullptr;  // bf16 [N] (16-byte aligned), or nullptr
@@ -54,6 +56,12 @@ __device__ __forceinline__ float activate(float y) {
     } else {
         return y;
     }
+}
+
+// SwiGLU of one gate / up pair (gate and up already alpha-scaled and biased):
+// silu(gate) * up, silu as in activate<kActSilu>.
+__device__ __forceinline__ float swiglu(float gate, float up) {
+    return __fmul_rn(activate<kActSilu>(gate), up);
 }
 
 // act(alpha * acc + bias) for one element with the epilogue fixed at compile time

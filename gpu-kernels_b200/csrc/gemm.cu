@@ -390,6 +390,7 @@ int gemm_dispatch_epi(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, co
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
     if (gemm_variant(M) == 2) return pair_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, stream, f16, di, epi);
+    if (epi.act == kActSwiglu) return NVFP4_ERR_UNSUPPORTED;  // the single-CTA epilogue has no SwiGLU
     if (f16) return gemm::launch<256, 4, true>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, epi);
     return gemm::launch<256, 4, false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, epi);
 }

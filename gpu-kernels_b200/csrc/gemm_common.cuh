@@ -297,6 +297,99 @@ __device__ __forceinline__ void store_row_act_nvfp4(const uint32_t (&acc)[kCols]
     }
 }
 
+// SwiGLU output of one row: accumulator columns [col0, col0 + kCols) (kCols % 32 == 0,
+// col0 % 32 == 0) hold blocks of 16 gate then 16 up columns and become the kCols/2
+// output columns from col0/2 of the [M, N/2] output: out = silu(gate) * up with
+// y = alpha * acc (+ bias) for each.  Gate and up value 2i / 2i+1 of a block:
+template <bool BIAS>
+__device__ __forceinline__ void swiglu_block(const uint32_t *acc32, float alpha, const uint16_t *bias, int N,
+                                             int c32, uint32_t (&pk)[8]) {
+    uint4 bg0 = make_uint4(0u, 0u, 0u, 0u), bg1 = bg0, bu0 = bg0, bu1 = bg0;
+    if constexpr (BIAS) {
+        bg0 = bias8(bias, N, c32);
+        bg1 = bias8(bias, N, c32 + 8);
+        bu0 = bias8(bias, N, c32 + 16);
+        bu1 = bias8(bias, N, c32 + 24);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint4 &bg = i < 4 ? bg0 : bg1, &bu = i < 4 ? bu0 : bu1;
+        const int j0 = (2 * i) & 7, j1 = (2 * i + 1) & 7;
+        const float g0 = epi_t<kActNone, BIAS>(__uint_as_float(acc32[2 * i]), alpha, bias_elem(bg, j0));
+        const float g1 = epi_t<kActNone, BIAS>(__uint_as_float(acc32[2 * i + 1]), alpha, bias_elem(bg, j1));
+        const float u0 = epi_t<kActNone, BIAS>(__uint_as_float(acc32[16 + 2 * i]), alpha, bias_elem(bu, j0));
+        const float u1 = epi_t<kActNone, BIAS>(__uint_as_float(acc32[16 + 2 * i + 1]), alpha, bias_elem(bu, j1));
+        pk[i] = pack2(swiglu(g0, u0), swiglu(g1, u1), false);
+    }
+}
+
+template <int kCols, bool BIAS>
+__device__ __forceinline__ void store_row_swiglu(const uint32_t (&acc)[kCols], const Params &p, int row, int col0,
+                                                 int row_end, float alpha, const uint16_t *bias) {
+    static_assert(kCols % 32 == 0, "whole gate / up blocks");
+    const int No = p.N >> 1;
+    const bool row_ok = row < row_end;
+    uint8_t *drow = static_cast<uint8_t *>(p.d) + ((int64_t)row * No + (col0 >> 1)) * 2;
+#pragma unroll
+    for (int j = 0; j < kCols / 32; j++) {
+        uint32_t w[8];
+        swiglu_block<BIAS>(&acc[32 * j], alpha, bias, p.N, col0 + 32 * j, w);
+        if (row_ok && col0 + 32 * j < p.N) {
+            if (p.vec32_store) {
+                st_global_v8(drow + j * 32, w);
+            } else {
+                *reinterpret_cast<uint4 *>(drow + j * 32) = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4 *>(drow + j * 32 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+            }
+        }
+    }
+}
+
+// SwiGLU with NVFP4 output: kCols/2 output columns = whole 64-column k-groups of the
+// [M, N/2] output (kCols % 128 == 0), the arithmetic of store_row_act_nvfp4.
+template <int kCols, bool BIAS>
+__device__ __forceinline__ void store_row_swiglu_nvfp4(const uint32_t (&acc)[kCols], const Params &p, int row,
+                                                       int col0, int row_end, float alpha, const uint16_t *bias,
+                                                       int64_t sf_row, const ScaleTables *tab, ScaleGuess guess,
+                                                       bool gs_ok) {
+    static_assert(kCols % 128 == 0, "whole 64-column output k-groups");
+    const Epi &e = p.epi;
+    const int No = p.N >> 1;
+    const bool row_ok = row < row_end;
+    const int64_t rest = No >> 6;
+#pragma unroll
+    for (int g = 0; g < kCols / 128; g++) {
+        const int o0 = (col0 >> 1) + g * 64;  // first output column of the k-group
+        uint32_t codes[8], scales = 0;
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            uint32_t pk[8];
+            swiglu_block<BIAS>(&acc[g * 128 + b * 32], alpha, bias, p.N, col0 + g * 128 + b * 32, pk);
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(pk[i] << 16)), fabsf(__uint_as_float(pk[i] & 0xFFFF0000u))));
+            const uint32_t code = table_scale_code(amax, guess, tab, gs_ok);
+            const float inv = tab->inv[code];
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                lo |= e2m1x2(__fmul_rn(__uint_as_float(pk[i] << 16), inv),
+                             __fmul_rn(__uint_as_float(pk[i] & 0xFFFF0000u), inv)) << (8 * i);
+                hi |= e2m1x2(__fmul_rn(__uint_as_float(pk[4 + i] << 16), inv),
+                             __fmul_rn(__uint_as_float(pk[4 + i] & 0xFFFF0000u), inv)) << (8 * i);
+            }
+            codes[2 * b] = lo;
+            codes[2 * b + 1] = hi;
+            scales |= code << (8 * b);
+        }
+        if (row_ok && o0 < No) {
+            st_global_v8(e.q + (int64_t)row * (No >> 1) + (o0 >> 1), codes);
+            *reinterpret_cast<uint32_t *>(e.sf + sf_group_offset(sf_row, o0 >> 6, rest)) = scales;
+        }
+    }
+}
+
 // The fused epilogue of one row, dispatched once per tile to the body compiled for
 // this launch's activation, bias and output type.  tab / guess / gs_ok: the NVFP4
 // output's scale tables (unused for bf16 output).  NVFP4 output needs kCols % 64 == 0
@@ -326,6 +419,21 @@ __device__ __forceinline__ void store_row_epi_fast(const uint32_t (&acc)[kCols],
         case kActRelu: NVFP4_EPI_BODY(kActRelu) break;
         case kActSilu: NVFP4_EPI_BODY(kActSilu) break;
         case kActGeluTanh: NVFP4_EPI_BODY(kActGeluTanh) break;
+        case kActSwiglu:  // the launch admits it only where kCols % 128 == 0
+            if constexpr (kCols % 128 == 0) {
+                if (e.q) {
+                    if (bias)
+                        store_row_swiglu_nvfp4<kCols, true>(acc, p, row, col0, row_end, alpha, bias_row, sf_row, tab,
+                                                            guess, gs_ok);
+                    else
+                        store_row_swiglu_nvfp4<kCols, false>(acc, p, row, col0, row_end, alpha, bias_row, sf_row,
+                                                             tab, guess, gs_ok);
+                } else {
+                    if (bias) store_row_swiglu<kCols, true>(acc, p, row, col0, row_end, alpha, bias_row);
+                    else store_row_swiglu<kCols, false>(acc, p, row, col0, row_end, alpha, bias_row);
+                }
+            }
+            break;
         default: NVFP4_EPI_BODY(kActNone) break;
     }
 #undef NVFP4_EPI_BODY

@@ -195,6 +195,68 @@ __device__ __forceinline__ void store_col_act_nvfp4(const float (&sum)[MPAD], co
     }
 }
 
+// SwiGLU: a warp's 32 weight rows are one block of 16 gate rows (lanes 0-15) and the
+// 16 matching up rows (lanes 16-31); lane l < 16 writes output column
+// 16 * (n / 32) + l of the [M, N/2] output = silu(gate) * up, the up value shuffled
+// down from lane l + 16 (N % 128 == 0, so a warp is all in or all out of range).
+template <int MPAD, bool BIAS>
+__device__ __forceinline__ void store_col_swiglu(const float (&sum)[MPAD], uint16_t *d, int N, int n, int lane,
+                                                 int rows, int d_row0, float alpha, float bias_n) {
+    const int No = N >> 1, o = (n >> 5) * 16 + (lane & 15);
+    const bool valid = n < N && lane < 16;
+#pragma unroll
+    for (int m = 0; m < MPAD; m++) {
+        if (m < rows) {  // uniform over the warp
+            const float y = epi_t<kActNone, BIAS>(sum[m], alpha, bias_n);
+            const float up = __shfl_down_sync(0xffffffffu, y, 16);
+            if (valid) {
+                __nv_bfloat16 v = __float2bfloat16_rn(swiglu(y, up));
+                d[(int64_t)(d_row0 + m) * No + o] = *reinterpret_cast<uint16_t *>(&v);
+            }
+        }
+    }
+}
+
+// SwiGLU with NVFP4 output: lanes 0-15 hold one 16-column scale block of the output
+// row (amax shuffles stay within each half-warp), rows in chunks of 8 as in
+// store_col_act_nvfp4.
+template <int MPAD, bool BIAS>
+__device__ __forceinline__ void store_col_swiglu_nvfp4(const float (&sum)[MPAD], const Epi &e, int N, int n, int lane,
+                                                       int rows, int d_row0, int sf_row0, float alpha, float bias_n,
+                                                       const ScaleTables *tab, ScaleGuess guess, bool gs_ok) {
+    constexpr int kChunk = MPAD < 8 ? MPAD : 8;
+    const int No = N >> 1, o = (n >> 5) * 16 + (lane & 15);
+    const bool valid = n < N && lane < 16;
+    const int64_t rest = No >> 6;
+#pragma unroll
+    for (int m0 = 0; m0 < MPAD; m0 += kChunk) {
+        if (m0 >= rows) break;
+        float v[kChunk], amax[kChunk];
+#pragma unroll
+        for (int i = 0; i < kChunk; i++) {
+            const float y = epi_t<kActNone, BIAS>(sum[m0 + i], alpha, bias_n);
+            const float up = __shfl_down_sync(0xffffffffu, y, 16);
+            v[i] = valid ? round_bf16(swiglu(y, up)) : 0.0f;
+            amax[i] = fabsf(v[i]);
+        }
+#pragma unroll
+        for (int s = 8; s; s >>= 1)
+#pragma unroll
+            for (int i = 0; i < kChunk; i++) amax[i] = fmaxf(amax[i], __shfl_xor_sync(0xffffffffu, amax[i], s));
+#pragma unroll
+        for (int i = 0; i < kChunk; i++) {
+            const int m = m0 + i;
+            const uint32_t code = table_scale_code(amax[i], guess, tab, gs_ok);
+            const uint32_t q4 = e2m1x2(__fmul_rn(v[i], tab->inv[code]), 0.0f) & 0xFu;
+            const uint32_t hi = __shfl_down_sync(0xffffffffu, q4, 1);
+            if (m < rows && valid && !(lane & 1))
+                e.q[(int64_t)(d_row0 + m) * (No >> 1) + (o >> 1)] = (uint8_t)(q4 | (hi << 4));
+            if (m < rows && valid && lane == 0)
+                e.sf[sf_group_offset(sf_row0 + m, o >> 6, rest) + ((o >> 4) & 3)] = (uint8_t)code;
+        }
+    }
+}
+
 template <int MPAD>
 __device__ __forceinline__ void store_col_epi(const float (&sum)[MPAD], const Epi &e, uint16_t *d, int N, int n,
                                               int lane, int rows, int d_row0, int sf_row0, float alpha, float bias_n,
@@ -216,6 +278,19 @@ __device__ __forceinline__ void store_col_epi(const float (&sum)[MPAD], const Ep
         case kActRelu: NVFP4_DECODE_EPI_BODY(kActRelu) break;
         case kActSilu: NVFP4_DECODE_EPI_BODY(kActSilu) break;
         case kActGeluTanh: NVFP4_DECODE_EPI_BODY(kActGeluTanh) break;
+        case kActSwiglu:
+            if (e.q) {
+                if (bias)
+                    store_col_swiglu_nvfp4<MPAD, true>(sum, e, N, n, lane, rows, d_row0, sf_row0, alpha, bias_n, tab,
+                                                       guess, gs_ok);
+                else
+                    store_col_swiglu_nvfp4<MPAD, false>(sum, e, N, n, lane, rows, d_row0, sf_row0, alpha, bias_n,
+                                                        tab, guess, gs_ok);
+            } else {
+                if (bias) store_col_swiglu<MPAD, true>(sum, d, N, n, lane, rows, d_row0, alpha, bias_n);
+                else store_col_swiglu<MPAD, false>(sum, d, N, n, lane, rows, d_row0, alpha, bias_n);
+            }
+            break;
         default: NVFP4_DECODE_EPI_BODY(kActNone) break;
     }
 #undef NVFP4_DECODE_EPI_BODY

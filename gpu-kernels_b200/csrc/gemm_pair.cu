@@ -674,6 +674,7 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
                        const Gather &gat = Gather()) {
     if (epi.q && BN % 128 != 0) return NVFP4_ERR_UNSUPPORTED;  // NVFP4 output wants 64-column aligned halves
     if (F16 && !epi.plain()) return NVFP4_ERR_UNSUPPORTED;     // the fused epilogue writes bf16 / NVFP4
+    if (epi.act == kActSwiglu && BN % 256 != 0) return NVFP4_ERR_UNSUPPORTED;  // 128-column halves
     using L = PairLayout<STAGES, BKB, BN>;
     auto kern = trace ? nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, true>
                       : nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, false>;

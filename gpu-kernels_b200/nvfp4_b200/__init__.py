@@ -7,7 +7,7 @@ on sys.path (the repository's conftest, bench.py and __graft_entry__ do).
 """
 from ._lib import LIB_PATH, NVFP4Error, SIGNATURES, lib  # noqa: F401
 from .layout import (from_blocked, grouped_sf_block0, grouped_sf_bytes, pad128, sf_bytes, sf_offset,  # noqa: F401
-                     to_blocked)
+                     swiglu_interleave, to_blocked)
 from .ops import (create_tensors, device_status, gemm, gemm_epilogue, gemm_grouped,  # noqa: F401
                   gemm_grouped_epilogue, gemm_host, global_scale, launch_count, matmul_nvfp4, quantize,
                   quantize_grouped, selftest_wait_timeout, set_wait_timeout_ns)

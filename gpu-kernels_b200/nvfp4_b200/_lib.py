@@ -23,7 +23,7 @@ class Epilogue(C.Structure):
                 ("out_global_scale", C.c_void_p)]
 
 
-ACTIVATIONS = {"none": 0, "relu": 1, "silu": 2, "gelu_tanh": 3}
+ACTIVATIONS = {"none": 0, "relu": 1, "silu": 2, "gelu_tanh": 3, "swiglu": 4}
 
 SIGNATURES = {
     "nvfp4_status_string": (C.c_char_p, [C.c_int]),

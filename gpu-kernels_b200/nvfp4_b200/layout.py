@@ -58,3 +58,24 @@ def grouped_sf_block0(m_offsets):
         b += (max(0, m_offsets[g + 1] - m_offsets[g]) + 127) // 128
     out.append(b)
     return out
+
+
+def swiglu_interleave(gate, up, block: int = 16):
+    """Interleave the rows of a gate and an up weight (or bias) of F rows each into the
+    [2F, ...] order the "swiglu" epilogue reads: rows 32j .. 32j+15 = gate rows
+    16j .. 16j+15, rows 32j+16 .. 32j+31 = the matching up rows.  Works on torch
+    tensors or numpy arrays; quantize the interleaved bf16 weight as usual."""
+    if gate.shape != up.shape or gate.shape[0] % block:
+        raise ValueError(f"gate and up must have the same shape with rows a multiple of {block}")
+    F = gate.shape[0]
+    rest = tuple(gate.shape[1:])
+    try:
+        import torch
+        if isinstance(gate, torch.Tensor):
+            return torch.stack((gate.reshape(F // block, block, *rest), up.reshape(F // block, block, *rest)),
+                               dim=1).reshape(2 * F, *rest)
+    except ImportError:
+        pass
+    import numpy as np
+    return np.stack((gate.reshape(F // block, block, *rest), up.reshape(F // block, block, *rest)),
+                    axis=1).reshape(2 * F, *rest)

@@ -94,7 +94,9 @@ def gemm_epilogue(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torc
     Without `out_global_scale`: returns bf16 D [M, N].  With it: D is quantized to
     NVFP4 in the epilogue (N % 64 == 0) and (codes uint8 [M, N/2], blocked scales
     uint8 [pad128(M) * N/16]) are returned — the bytes nvfp4_quantize would give
-    for the bf16 result."""
+    for the bf16 result.  activation "swiglu": B's rows are gate / up weights
+    interleaved in blocks of 16 (swiglu_interleave), bias likewise, and the output
+    has N/2 columns, silu(gate) * up (N % 128 == 0)."""
     for t, n in ((a, "a"), (sfa, "sfa"), (b, "b"), (sfb, "sfb")):
         _bytes_tensor(t, n)
     M, K, N = a.shape[0], a.shape[1] * 2, b.shape[0]
@@ -110,16 +112,17 @@ def gemm_epilogue(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torc
         if bias.dtype != torch.bfloat16 or bias.numel() != N or not bias.is_cuda or not bias.is_contiguous():
             raise ValueError("bias must be a contiguous bf16 CUDA tensor of N elements")
         e.bias = bias.data_ptr()
+    No = N // 2 if activation == "swiglu" else N  # output columns
     d = None
     if out_global_scale is None:
-        d = out if out is not None else torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
-        if d.dtype != torch.bfloat16 or d.shape != (M, N) or not d.is_contiguous():
-            raise ValueError("out must be a contiguous bf16 [M, N] tensor")
+        d = out if out is not None else torch.empty(M, No, dtype=torch.bfloat16, device=a.device)
+        if d.dtype != torch.bfloat16 or d.shape != (M, No) or not d.is_contiguous():
+            raise ValueError(f"out must be a contiguous bf16 [M, {No}] tensor")
         d_ptr = d.data_ptr()
     else:
         gs = _scale_tensor(out_global_scale, a.device)
-        q = q_out if q_out is not None else torch.empty(M, N // 2, dtype=torch.uint8, device=a.device)
-        sf = sf_out if sf_out is not None else torch.empty(sf_bytes(M, N), dtype=torch.uint8, device=a.device)
+        q = q_out if q_out is not None else torch.empty(M, No // 2, dtype=torch.uint8, device=a.device)
+        sf = sf_out if sf_out is not None else torch.empty(sf_bytes(M, No), dtype=torch.uint8, device=a.device)
         e.q_out, e.sf_out, e.out_global_scale = q.data_ptr(), sf.data_ptr(), gs.data_ptr()
         d_ptr = None
     check(lib().nvfp4_gemm_epilogue(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), float(alpha), d_ptr,
@@ -192,7 +195,8 @@ def gemm_grouped_epilogue(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, s
     Without `out_global_scale`: returns bf16 D [m_total, N].  With it: returns
     (codes uint8 [m_total, N/2], scales in the grouped layout of
     grouped_sf_bytes(m_total, groups, N) bytes) — what quantize_grouped makes of the
-    bf16 result, ready as the A operand of the next grouped GEMM (N % 128 == 0)."""
+    bf16 result, ready as the A operand of the next grouped GEMM (N % 128 == 0).
+    activation "swiglu" as in gemm_epilogue: N/2 output columns."""
     for t, n in ((a, "a"), (sfa, "sfa"), (b, "b"), (sfb, "sfb")):
         _bytes_tensor(t, n)
     offs = _offsets_tensor(m_offsets, a.device)
@@ -213,16 +217,17 @@ def gemm_grouped_epilogue(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, s
         if bias.dtype != torch.bfloat16 or bias.numel() != G * N or not bias.is_cuda or not bias.is_contiguous():
             raise ValueError("bias must be a contiguous bf16 CUDA tensor of groups * N elements")
         e.bias = bias.data_ptr()
+    No = N // 2 if activation == "swiglu" else N  # output columns
     d = None
     if out_global_scale is None:
-        d = out if out is not None else torch.zeros(m_total, N, dtype=torch.bfloat16, device=a.device)
-        if d.dtype != torch.bfloat16 or d.shape != (m_total, N) or not d.is_contiguous():
-            raise ValueError("out must be a contiguous bf16 [m_total, N] tensor")
+        d = out if out is not None else torch.zeros(m_total, No, dtype=torch.bfloat16, device=a.device)
+        if d.dtype != torch.bfloat16 or d.shape != (m_total, No) or not d.is_contiguous():
+            raise ValueError(f"out must be a contiguous bf16 [m_total, {No}] tensor")
         d_ptr = d.data_ptr()
     else:
         gs = _scale_tensor(out_global_scale, a.device)
-        q = q_out if q_out is not None else torch.zeros(m_total, N // 2, dtype=torch.uint8, device=a.device)
-        sf = sf_out if sf_out is not None else torch.zeros(grouped_sf_bytes(m_total, G, N), dtype=torch.uint8,
+        q = q_out if q_out is not None else torch.zeros(m_total, No // 2, dtype=torch.uint8, device=a.device)
+        sf = sf_out if sf_out is not None else torch.zeros(grouped_sf_bytes(m_total, G, No), dtype=torch.uint8,
                                                            device=a.device)
         e.q_out, e.sf_out, e.out_global_scale = q.data_ptr(), sf.data_ptr(), gs.data_ptr()
         d_ptr = None

@@ -52,7 +52,8 @@ def gemm_epilogue(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torc
 
 @gemm_epilogue.register_fake
 def _gemm_epilogue_fake(a, sfa, b, sfb, alpha, bias=None, activation="none"):
-    return a.new_empty((a.shape[0], b.shape[0]), dtype=torch.bfloat16)
+    N = b.shape[0] // 2 if activation == "swiglu" else b.shape[0]
+    return a.new_empty((a.shape[0], N), dtype=torch.bfloat16)
 
 
 @torch.library.custom_op("nvfp4_b200::gemm_nvfp4_out", mutates_args=(), device_types="cuda")
@@ -67,5 +68,5 @@ def gemm_nvfp4_out(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: tor
 
 @gemm_nvfp4_out.register_fake
 def _gemm_nvfp4_out_fake(a, sfa, b, sfb, alpha, out_global_scale, bias=None, activation="none"):
-    M, N = a.shape[0], b.shape[0]
+    M, N = a.shape[0], b.shape[0] // 2 if activation == "swiglu" else b.shape[0]
     return (a.new_empty((M, N // 2), dtype=torch.uint8), a.new_empty((sf_bytes(M, N),), dtype=torch.uint8))

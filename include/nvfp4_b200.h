@@ -132,18 +132,26 @@ NVFP4_API int nvfp4_gemm_f16(const uint8_t *A, const uint8_t *SFA, const uint8_t
  * with act one of
  *   NVFP4_ACT_NONE, NVFP4_ACT_RELU (max(y, 0)), NVFP4_ACT_SILU (y / (1 + exp(-y))),
  *   NVFP4_ACT_GELU_TANH (0.5 y (1 + tanh(sqrt(2/pi) (y + 0.044715 y^3)))),
- * silu and gelu with the GPU's approximate exp / reciprocal / tanh instructions.
+ * silu and gelu with the GPU's tanh instruction (tanh.approx).
+ * NVFP4_ACT_SWIGLU gates one half of the columns with the other: B's rows hold gate
+ * and up weights interleaved in blocks of 16 (rows 32j .. 32j+15 gate, 32j+16 ..
+ * 32j+31 up; bias in the same order), and output column c of the N/2 output columns
+ * is silu(y[32*(c/16) + c%16]) * y[32*(c/16) + 16 + c%16] — the SwiGLU FFN's
+ * silu(x W1^T) * (x W3^T) from one GEMM over the interleaved weight.  N % 128 == 0;
+ * D (or q_out / sf_out) then has N/2 columns.
  * Output: bf16(y) into D, or — when q_out is given — the bf16(y) rows quantized to
- * NVFP4 for the next layer: codes [M, N/2] into q_out and blocked e4m3 scales
- * [pad128(M), N/16] into sf_out with the fp32 global scale *out_global_scale
- * (device), byte-identical to nvfp4_quantize applied to the bf16 output.  NVFP4
- * output needs N % 64 == 0; D is then not written and may be NULL.
+ * NVFP4 for the next layer: codes [M, Nout/2] into q_out and blocked e4m3 scales
+ * [pad128(M), Nout/16] into sf_out (Nout = N, or N/2 with SwiGLU) with the fp32
+ * global scale *out_global_scale (device), byte-identical to nvfp4_quantize applied
+ * to the bf16 output.  NVFP4 output needs Nout % 64 == 0; D is then not written and
+ * may be NULL.
  */
 enum {
     NVFP4_ACT_NONE = 0,
     NVFP4_ACT_RELU = 1,
     NVFP4_ACT_SILU = 2,
-    NVFP4_ACT_GELU_TANH = 3
+    NVFP4_ACT_GELU_TANH = 3,
+    NVFP4_ACT_SWIGLU = 4
 };
 typedef struct nvfp4_epilogue {
     const uint16_t *bias;          /* bf16 [N] (16-byte aligned), or NULL */

@@ -385,6 +385,30 @@ void nvfp4o_epilogue(const float *acc, const uint16_t *bias, int act, float alph
     }
 }
 
+/* SwiGLU epilogue over gate / up columns interleaved in blocks of 16: output column
+ * c of [rows, N/2] (N % 32 == 0) takes gate column 32*(c/16) + c%16 and up column
+ * 32*(c/16) + 16 + c%16 of the accumulator; with y = alpha * acc (+ bias[col]) for
+ * each, out = silu(y_gate) * y_up = y_gate / (1 + exp(-y_gate)) * y_up in fp32, then
+ * bf16 (round to nearest even).  The GPU computes silu with tanh.approx, so the two
+ * agree within the GEMM tolerance, not bit for bit. */
+void nvfp4o_epilogue_swiglu(const float *acc, const uint16_t *bias, float alpha, int64_t rows, int64_t N,
+                            float *Y32, uint16_t *Y16, int nthreads) {
+    const int64_t half = N / 2, total = rows * half;
+#pragma omp parallel for schedule(static) num_threads(pick_threads(nthreads))
+    for (int64_t i = 0; i < total; i++) {
+        const int64_t r = i / half, c = i % half;
+        const int64_t g = 32 * (c / 16) + c % 16, u = g + 16;
+        float yg = alpha * acc[r * N + g], yu = alpha * acc[r * N + u];
+        if (bias) {
+            yg = yg + nvfp4o_bf16_to_f32(bias[g]);
+            yu = yu + nvfp4o_bf16_to_f32(bias[u]);
+        }
+        const float y = yg / (1.0f + expf(-yg)) * yu;
+        if (Y32) Y32[i] = y;
+        if (Y16) Y16[i] = nvfp4o_f32_to_bf16(y);
+    }
+}
+
 /* ---------------------------------------------------------------------------
  * Deterministic inputs: splitmix64 counter stream + Box-Muller in double.
  * ------------------------------------------------------------------------- */

@@ -77,6 +77,8 @@ void    nvfp4o_sgemm_nt(const float *A, const float *B, float alpha, int64_t mro
  * 1 relu, 2 silu, 3 gelu-tanh), fp32 and/or bf16 out. */
 void    nvfp4o_epilogue(const float *acc, const uint16_t *bias, int act, float alpha, int64_t rows,
                         int64_t N, float *Y32, uint16_t *Y16, int nthreads);
+void nvfp4o_epilogue_swiglu(const float *acc, const uint16_t *bias, float alpha, int64_t rows, int64_t N,
+                            float *Y32, uint16_t *Y16, int nthreads);
 
 /* ---- deterministic synthetic inputs -------------------------------------- */
 /* Counter-based (splitmix64) so that any slice can be generated alone. */

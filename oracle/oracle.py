@@ -56,6 +56,7 @@ def lib():
         L.nvfp4o_fill_student_t3_bf16.argtypes = [u16p, i64, i64, C.c_uint64, C.c_int, C.c_float,
                                                    C.c_int]
         L.nvfp4o_epilogue.argtypes = [f32p, u16p, C.c_int, C.c_float, i64, i64, f32p, u16p, C.c_int]
+        L.nvfp4o_epilogue_swiglu.argtypes = [f32p, u16p, C.c_float, i64, i64, f32p, u16p, C.c_int]
         L.nvfp4o_max_threads.restype = C.c_int
         _lib = L
     return _lib
@@ -185,22 +186,30 @@ def sgemm_nt(af: np.ndarray, bf: np.ndarray, alpha: float, nthreads: int = 0):
     return d32, d16
 
 
-ACTIVATIONS = {"none": 0, "relu": 1, "silu": 2, "gelu_tanh": 3}
+ACTIVATIONS = {"none": 0, "relu": 1, "silu": 2, "gelu_tanh": 3, "swiglu": 4}
 
 
 def epilogue(acc: np.ndarray, alpha: float, bias_bf16=None, activation: str = "none", nthreads: int = 0):
-    """act(alpha * acc + bias) over a [rows, N] fp32 accumulator -> (Y32, Y_bf16_bits)."""
+    """act(alpha * acc + bias) over a [rows, N] fp32 accumulator -> (Y32, Y_bf16_bits).
+    activation "swiglu": gate / up columns interleaved in blocks of 16, output
+    [rows, N/2] = silu(gate) * up (nvfp4o_epilogue_swiglu)."""
     acc = np.ascontiguousarray(acc, dtype=np.float32)
     rows, N = acc.shape
-    y32 = np.empty((rows, N), dtype=np.float32)
-    y16 = np.empty((rows, N), dtype=np.uint16)
+    out_n = N // 2 if activation == "swiglu" else N
+    y32 = np.empty((rows, out_n), dtype=np.float32)
+    y16 = np.empty((rows, out_n), dtype=np.uint16)
     bp = None
     if bias_bf16 is not None:
         bias_bf16 = np.ascontiguousarray(bias_bf16, dtype=np.uint16)
         assert bias_bf16.size == N
         bp = _p(bias_bf16, C.c_uint16)
-    lib().nvfp4o_epilogue(_p(acc, C.c_float), bp, ACTIVATIONS[activation], float(alpha), rows, N,
-                          _p(y32, C.c_float), _p(y16, C.c_uint16), nthreads)
+    if activation == "swiglu":
+        assert N % 32 == 0
+        lib().nvfp4o_epilogue_swiglu(_p(acc, C.c_float), bp, float(alpha), rows, N, _p(y32, C.c_float),
+                                     _p(y16, C.c_uint16), nthreads)
+    else:
+        lib().nvfp4o_epilogue(_p(acc, C.c_float), bp, ACTIVATIONS[activation], float(alpha), rows, N,
+                              _p(y32, C.c_float), _p(y16, C.c_uint16), nthreads)
     return y32, y16
 
 

@@ -31,6 +31,32 @@ def _ref_act(y, act):
     return y
 
 
+def test_oracle_swiglu_matches_formula(oracle):
+    rng = np.random.default_rng(4)
+    acc = (rng.standard_normal((6, 96)) * 3).astype(np.float32)
+    bias = oracle.f32_to_bf16_bits(rng.standard_normal(96).astype(np.float32))
+    y32, y16 = oracle.epilogue(acc, 0.5, bias, "swiglu")
+    y = acc.astype(np.float64) * 0.5 + oracle.bf16_bits_to_f32(bias).astype(np.float64)
+    g = np.concatenate([y[:, 32 * j:32 * j + 16] for j in range(3)], axis=1)
+    u = np.concatenate([y[:, 32 * j + 16:32 * j + 32] for j in range(3)], axis=1)
+    assert y32.shape == (6, 48)
+    assert np.allclose(y32, g / (1 + np.exp(-g)) * u, rtol=1e-5, atol=1e-6)
+    assert np.array_equal(y16, oracle.f32_to_bf16_bits(y32))
+
+
+def test_swiglu_interleave_layout(nv):
+    gate = torch.arange(64 * 3).reshape(64, 3)
+    up = -gate
+    w = nv.swiglu_interleave(gate, up)
+    assert w.shape == (128, 3)
+    assert torch.equal(w[0:16], gate[0:16]) and torch.equal(w[16:32], up[0:16])
+    assert torch.equal(w[96:112], gate[48:64]) and torch.equal(w[112:128], up[48:64])
+    b = nv.swiglu_interleave(np.arange(32), np.arange(32) + 100)
+    assert list(b[14:18]) == [14, 15, 100, 101]
+    with pytest.raises(ValueError):
+        nv.swiglu_interleave(gate[:10], up[:10])
+
+
 @pytest.mark.parametrize("act", ACTS)
 def test_oracle_epilogue_matches_formula(oracle, act):
     rng = np.random.default_rng(3)
@@ -57,6 +83,8 @@ def test_epilogue_host_checks(nv):
     assert call(256, 256, 256, E(q_out=fake, sf_out=fake + 2, out_global_scale=fake)) == -3
     assert call(256, 256, 256, E(q_out=fake + 16, sf_out=fake, out_global_scale=fake)) == -3  # q 32 B
     assert call(256, 256, 100, E()) == -2                                               # K % 64
+    assert call(256, 192, 256, E(activation=4)) == -2                                   # SwiGLU: N % 128
+    assert call(256, 256, 256, E(activation=5)) == -1                                   # unknown activation
 
 
 SHAPES = [(16, 1024, 512), (77, 512, 1024), (300, 768, 1024), (520, 1024, 512)]
@@ -138,3 +166,72 @@ def test_torch_ops_epilogue(nv, oracle, cuda_dev):
     q2, s2 = nv.quantize(d1, gs)
     torch.cuda.synchronize()
     assert torch.equal(d1, d2) and torch.equal(q1, q2) and torch.equal(s1, s2)
+
+
+SWIGLU_SHAPES = [(16, 1024, 512), (77, 512, 1024), (300, 768, 1024), (520, 1024, 512)]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", SWIGLU_SHAPES)
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_swiglu_vs_oracle(nv, oracle, cuda_dev, M, N, K, with_bias):
+    """SwiGLU over gate / up columns interleaved in blocks of 16: [M, N/2] output
+    against the oracle (max relative error 1e-2), decode and CTA-pair kernels."""
+    a, sfa, b, sfb = _operands(oracle, M, N, K, 51)
+    bias = oracle.f32_to_bf16_bits(np.random.default_rng(6).standard_normal(N).astype(np.float32))
+    alpha = 0.25
+    d = nv.gemm_epilogue(_dev(a, cuda_dev), _dev(sfa, cuda_dev), _dev(b, cuda_dev), _dev(sfb, cuda_dev), alpha,
+                         bias=_dev(bias, cuda_dev).view(torch.bfloat16) if with_bias else None, activation="swiglu")
+    torch.cuda.synchronize()
+    nv.device_status()
+    assert d.shape == (M, N // 2)
+    acc, _ = oracle.gemm(a, sfa, b, sfb, 1.0, M, N, K)
+    _, ref16 = oracle.epilogue(acc.reshape(M, N), alpha, bias if with_bias else None, "swiglu")
+    ref = oracle.bf16_bits_to_f32(ref16).reshape(M, N // 2)
+    got = d.float().cpu().numpy()
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err <= 1e-2, err
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", SWIGLU_SHAPES)
+def test_swiglu_nvfp4_output_equals_quantized_bf16(nv, oracle, cuda_dev, M, N, K):
+    a, sfa, b, sfb = (_dev(x, cuda_dev) for x in _operands(oracle, M, N, K, 61))
+    bias = torch.randn(N, generator=torch.Generator().manual_seed(8)).to(torch.bfloat16).to(cuda_dev)
+    d = nv.gemm_epilogue(a, sfa, b, sfb, 0.5, bias=bias, activation="swiglu")
+    _, gs = nv.global_scale(d)
+    q, sf = nv.gemm_epilogue(a, sfa, b, sfb, 0.5, bias=bias, activation="swiglu", out_global_scale=gs,
+                             sf_out=torch.full((nv.sf_bytes(M, N // 2),), 0x7E, dtype=torch.uint8, device=cuda_dev))
+    q_ref, sf_ref = nv.quantize(d, gs)
+    torch.cuda.synchronize()
+    nv.device_status()
+    assert q.shape == (M, N // 4)
+    assert torch.equal(q, q_ref)
+    assert torch.equal(sf, sf_ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [16, 300])
+def test_swiglu_equals_two_gemms(nv, cuda_dev, M):
+    """silu(x Wg^T) * (x Wu^T) from one GEMM over swiglu_interleave(Wg, Wu) equals the
+    same from two GEMMs: row-wise block scales make quantizing the interleaved weight
+    the same as interleaving the quantized weights."""
+    F, K = 512, 1024
+    g = torch.Generator(device=cuda_dev).manual_seed(12)
+    x = torch.randn(M, K, device=cuda_dev, generator=g).to(torch.bfloat16)
+    wg = (torch.randn(F, K, device=cuda_dev, generator=g) * 0.02).to(torch.bfloat16)
+    wu = (torch.randn(F, K, device=cuda_dev, generator=g) * 0.02).to(torch.bfloat16)
+    _, gx = nv.global_scale(x)
+    _, gw = nv.global_scale(torch.cat((wg, wu)))
+    xq, xsf = nv.quantize(x, gx)
+    wq, wsf = nv.quantize(nv.swiglu_interleave(wg, wu).contiguous(), gw)
+    gq, gsf = nv.quantize(wg, gw)
+    uq, usf = nv.quantize(wu, gw)
+    alpha = float(gx.item() * gw.item())
+    h = nv.gemm_epilogue(xq, xsf, wq, wsf, alpha, activation="swiglu")
+    dg = nv.gemm(xq, xsf, gq, gsf, alpha).float()
+    du = nv.gemm(xq, xsf, uq, usf, alpha).float()
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.silu(dg) * du
+    err = (h.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err <= 2e-2, err

@@ -182,14 +182,15 @@ EPI_CASES = [CASES[0], CASES[2], CASES[3], CASES[4]]
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("offsets,m_total,N,K", EPI_CASES)
-@pytest.mark.parametrize("act", ["relu", "silu", "gelu_tanh"])
+@pytest.mark.parametrize("act", ["relu", "silu", "gelu_tanh", "swiglu"])
 def test_gemm_grouped_epilogue_vs_oracle(nv, oracle, cuda_dev, offsets, m_total, N, K, act):
     """Per-expert bias + activation fused into the grouped GEMM, each group against the
     oracle's GEMM and epilogue (max relative error 1e-2)."""
     x, gsa, offs, q, sf, bq, bsf, alphas = _make(oracle, nv, cuda_dev, offsets, m_total, N, K, seed=11)
     G = len(offsets) - 1
     bias = oracle.f32_to_bf16_bits(np.random.default_rng(3).standard_normal((G, N)).astype(np.float32))
-    out = torch.full((m_total, N), 7.0, dtype=torch.bfloat16, device=cuda_dev)
+    No = N // 2 if act == "swiglu" else N
+    out = torch.full((m_total, No), 7.0, dtype=torch.bfloat16, device=cuda_dev)
     d = nv.gemm_grouped_epilogue(q, sf, torch.from_numpy(bq).to(cuda_dev), torch.from_numpy(bsf).to(cuda_dev),
                                  torch.from_numpy(alphas).to(cuda_dev), offs,
                                  bias=torch.from_numpy(bias.view(np.int16)).to(cuda_dev).view(torch.bfloat16),
@@ -208,7 +209,7 @@ def test_gemm_grouped_epilogue_vs_oracle(nv, oracle, cuda_dev, offsets, m_total,
         acc, _ = oracle.gemm(qh[a:z], sfh[block0 * blk:(block0 + nb) * blk], bq[g * N:(g + 1) * N],
                              bsf[g * (N // 128) * blk:(g + 1) * (N // 128) * blk], 1.0, z - a, N, K)
         _, ref16 = oracle.epilogue(acc.reshape(z - a, N), float(alphas[g]), bias[g], act)
-        ref = oracle.bf16_bits_to_f32(ref16).reshape(z - a, N)
+        ref = oracle.bf16_bits_to_f32(ref16).reshape(z - a, No)
         err = np.abs(got[a:z] - ref).max() / np.abs(ref).max()
         assert err <= 1e-2, (g, err)
         covered[a:z] = True
@@ -218,21 +219,25 @@ def test_gemm_grouped_epilogue_vs_oracle(nv, oracle, cuda_dev, offsets, m_total,
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("offsets,m_total,N,K", CASES)
-def test_gemm_grouped_nvfp4_out_equals_quantize_grouped(nv, oracle, cuda_dev, offsets, m_total, N, K):
-    """NVFP4 output of the grouped GEMM (silu, per-expert bias): codes and grouped
-    scales byte-identical to quantize_grouped of the fused bf16 output, so it can be
-    the A operand of the next grouped GEMM as it stands."""
+@pytest.mark.parametrize("act", ["silu", "swiglu"])
+def test_gemm_grouped_nvfp4_out_equals_quantize_grouped(nv, oracle, cuda_dev, offsets, m_total, N, K, act):
+    """NVFP4 output of the grouped GEMM (silu or swiglu, per-expert bias): codes and
+    grouped scales byte-identical to quantize_grouped of the fused bf16 output, so it
+    can be the A operand of the next grouped GEMM as it stands."""
+    if act == "swiglu" and N % 128:
+        pytest.skip("SwiGLU needs N % 128 == 0")
     x, gsa, offs, q, sf, bq, bsf, alphas = _make(oracle, nv, cuda_dev, offsets, m_total, N, K, seed=13)
     G = len(offsets) - 1
+    No = N // 2 if act == "swiglu" else N
     b, sfb, al = (torch.from_numpy(t).to(cuda_dev) for t in (bq, bsf, alphas))
     bias = torch.randn(G, N, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16).to(cuda_dev)
-    d = nv.gemm_grouped_epilogue(q, sf, b, sfb, al, offs, bias=bias, activation="silu")
+    d = nv.gemm_grouped_epilogue(q, sf, b, sfb, al, offs, bias=bias, activation=act)
     _, gs = nv.global_scale(d)
-    q2, sf2 = nv.gemm_grouped_epilogue(q, sf, b, sfb, al, offs, bias=bias, activation="silu", out_global_scale=gs)
+    q2, sf2 = nv.gemm_grouped_epilogue(q, sf, b, sfb, al, offs, bias=bias, activation=act, out_global_scale=gs)
     q_ref, sf_ref = nv.quantize_grouped(d, gs, offs)
     torch.cuda.synchronize()
     nv.device_status()
-    used = nv.grouped_sf_block0([min(max(o, 0), m_total) for o in offsets])[-1] * 128 * N // 16
+    used = nv.grouped_sf_block0([min(max(o, 0), m_total) for o in offsets])[-1] * 128 * No // 16
     rows = np.zeros(m_total, dtype=bool)
     for a, z in _group_rows(offsets, m_total):
         rows[a:z] = True
