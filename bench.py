@@ -535,42 +535,62 @@ def moe_section(nv, dev, reps=20):
                      "hbm_gbs": w_bytes / (dec_ms / 1e3) / 1e9,
                      "per_expert_decode_calls_ms": loop_ms, "per_expert_hbm_gbs": w_bytes / (loop_ms / 1e3) / 1e9}
 
-    # The expert FFN around the GEMM: up-projection with SiLU and NVFP4 output in the
-    # grouped scale layout (one kernel), then the down-projection W_down [G*K, N]
-    # reading that output as its A operand; beside it the unfused sequence (bf16
-    # up-projection with SiLU, quantize_grouped, down-projection).
-    wdq = torch.empty(G * K, N // 2, dtype=torch.uint8, device=dev)
-    wdsf = torch.empty(G * nv.sf_bytes(K, N), dtype=torch.uint8, device=dev)
-    gs_down = torch.empty(G, dtype=torch.float32, device=dev)  # each expert's W_down global scale
+    # The expert FFN around the GEMM, SwiGLU form y = W2 (silu(W1 x) * W3 x): W1 and W3
+    # interleaved in blocks of 16 rows into one [2 * 14336, 4096] weight per expert, so
+    # one grouped GEMM with the SwiGLU epilogue writes the [rows, 14336] hidden state as
+    # NVFP4 in the grouped scale layout, which the down-projection W2 [4096, 14336]
+    # reads as its A operand.  Beside it the unfused sequence (bf16 SwiGLU output,
+    # quantize_grouped, down-projection).
+    del bq, bsf
+    F = N
+    wgu = torch.empty(G * 2 * F, K // 2, dtype=torch.uint8, device=dev)
+    wgusf = torch.empty(G * nv.sf_bytes(2 * F, K), dtype=torch.uint8, device=dev)
+    alphas_gu = torch.empty(G, dtype=torch.float32, device=dev)
     for e in range(G):
-        w = (torch.randn(K, N, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        w1 = (torch.randn(F, K, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        w3 = (torch.randn(F, K, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        w = nv.swiglu_interleave(w1, w3).contiguous()
+        del w1, w3
         _, gw = nv.global_scale(w)
-        nv.quantize(w, gw, q_out=wdq[e * K:(e + 1) * K], sf_out=wdsf[e * nv.sf_bytes(K, N):(e + 1) * nv.sf_bytes(K, N)])
+        sfb_e = nv.sf_bytes(2 * F, K)
+        nv.quantize(w, gw, q_out=wgu[e * 2 * F:(e + 1) * 2 * F], sf_out=wgusf[e * sfb_e:(e + 1) * sfb_e])
+        alphas_gu[e:e + 1] = gsx * gw
+        del w
+    wdq = torch.empty(G * K, F // 2, dtype=torch.uint8, device=dev)
+    wdsf = torch.empty(G * nv.sf_bytes(K, F), dtype=torch.uint8, device=dev)
+    gs_down = torch.empty(G, dtype=torch.float32, device=dev)  # each expert's W2 global scale
+    for e in range(G):
+        w = (torch.randn(K, F, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+        _, gw = nv.global_scale(w)
+        nv.quantize(w, gw, q_out=wdq[e * K:(e + 1) * K], sf_out=wdsf[e * nv.sf_bytes(K, F):(e + 1) * nv.sf_bytes(K, F)])
         gs_down[e:e + 1] = gw
         del w
-    ffn = {"what": "expert FFN up (N=14336, K=4096) + SiLU -> NVFP4 -> down (N=4096, K=14336), 8 experts"}
+    ffn = {"what": "Mixtral-like expert FFN, 8 experts: [W1;W3] interleaved (N=2x14336, K=4096) + SwiGLU -> "
+                   "NVFP4 -> W2 (N=4096, K=14336)",
+           "weight_bytes": G * (2 * F * K // 2 + nv.sf_bytes(2 * F, K) + K * F // 2 + nv.sf_bytes(K, F))}
     for name, (qq, ss, oo, mm) in (("prefill_8192_rows", (q, sf, offs, m_total)),
                                    ("decode_64_rows", (qd, sfd, offs_d, m_d))):
-        h = nv.gemm_grouped_epilogue(qq, ss, bq, bsf, alphas, oo, activation="silu")
-        _, gh = nv.global_scale(h)  # the hidden activations' global scale (calibrated once)
-        alphas_d = gs_down * gh     # expert e's down-projection alpha: gs(h) * gs(W_down[e])
-        hq = torch.empty(mm, N // 2, dtype=torch.uint8, device=dev)
-        hsf = torch.empty(nv.grouped_sf_bytes(mm, G, N), dtype=torch.uint8, device=dev)
+        h = nv.gemm_grouped_epilogue(qq, ss, wgu, wgusf, alphas_gu, oo, activation="swiglu")
+        _, gh = nv.global_scale(h)  # the hidden state's global scale (calibrated once)
+        alphas_d = gs_down * gh     # expert e's down-projection alpha: gs(h) * gs(W2[e])
+        hq = torch.empty(mm, F // 2, dtype=torch.uint8, device=dev)
+        hsf = torch.empty(nv.grouped_sf_bytes(mm, G, F), dtype=torch.uint8, device=dev)
         y = torch.empty(mm, K, dtype=torch.bfloat16, device=dev)
 
         def fused():
-            nv.gemm_grouped_epilogue(qq, ss, bq, bsf, alphas, oo, activation="silu", out_global_scale=gh,
+            nv.gemm_grouped_epilogue(qq, ss, wgu, wgusf, alphas_gu, oo, activation="swiglu", out_global_scale=gh,
                                      q_out=hq, sf_out=hsf)
             nv.gemm_grouped(hq, hsf, wdq, wdsf, alphas_d, oo, out=y)
 
         def unfused():
-            nv.gemm_grouped_epilogue(qq, ss, bq, bsf, alphas, oo, activation="silu", out=h)
+            nv.gemm_grouped_epilogue(qq, ss, wgu, wgusf, alphas_gu, oo, activation="swiglu", out=h)
             nv.quantize_grouped(h, gh, oo, q_out=hq, sf_out=hsf)
             nv.gemm_grouped(hq, hsf, wdq, wdsf, alphas_d, oo, out=y)
 
         f_ms, u_ms = timed(fused), timed(unfused)
-        flops_ffn = 2.0 * 2 * mm * N * K
-        ffn[name] = {"fused_ms": f_ms, "unfused_ms": u_ms, "fused_tflops": flops_ffn / (f_ms / 1e3) / 1e12}
+        flops_ffn = 2.0 * mm * K * (2 * F + F)
+        ffn[name] = {"fused_ms": f_ms, "unfused_ms": u_ms, "fused_tflops": flops_ffn / (f_ms / 1e3) / 1e12,
+                     "fused_weight_gbs": ffn["weight_bytes"] / (f_ms / 1e3) / 1e9}
     nv.device_status()
     out["ffn"] = ffn
     return out
