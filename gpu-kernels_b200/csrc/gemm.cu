@@ -346,6 +346,7 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     p.clc = 0;
     p.tma_store = 0;
     p.spin = 0;
+    p.l2hint = 0;
     p.epi = epi;
     if ((st = kernel_ctl(&p.ctl))) return st;
     const int grid = p.num_tiles < di.sm_count ? p.num_tiles : di.sm_count;

@@ -63,6 +63,7 @@ struct Params {
     int clc;      // pair kernel: tiles handed out by cluster launch control (else static persistent)
     int tma_store;  // pair kernel: plain D stored through shared memory by TMA (else direct stores)
     int spin;       // pair kernel: MMA thread and epilogue poll their barriers (test_wait)
+    int l2hint;     // pair kernel: 1 = D stored evict-first in L2, 2 = also A/B loaded evict-last
     Epi epi;      // fused epilogue (plain: alpha and bf16/fp16 rounding only)
     Grouped grouped;
     Gather gather;
@@ -80,9 +81,10 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool f16) {
 
 // Convert this thread's kCols accumulator columns (one output row) with alpha and
 // store them to D[row, col0 .. col0+kCols), clipped to N; rows >= row_end are skipped.
+// With store_hint, the 32-byte stores carry the L2 policy `policy`.
 template <int kCols, bool F16>
 __device__ __forceinline__ void store_row(const uint32_t (&acc)[kCols], const Params &p, int row, int col0,
-                                          int row_end, float alpha) {
+                                          int row_end, float alpha, bool store_hint = false, uint64_t policy = 0) {
     if (row >= row_end) return;
     uint8_t *drow = static_cast<uint8_t *>(p.d) + ((int64_t)row * p.N + col0) * 2;
     if (p.vec32_store) {
@@ -94,7 +96,8 @@ __device__ __forceinline__ void store_row(const uint32_t (&acc)[kCols], const Pa
                 for (int i = 0; i < 8; i++)
                     v[i] = pack2(__uint_as_float(acc[c * 16 + 2 * i]) * alpha,
                                  __uint_as_float(acc[c * 16 + 2 * i + 1]) * alpha, F16);
-                st_global_v8(drow + c * 32, v);
+                if (store_hint) st_global_v8_hint(drow + c * 32, v, policy);
+                else st_global_v8(drow + c * 32, v);
             }
         }
     } else {

@@ -255,6 +255,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         if (elect_one()) {
             const bool ab = warp == 0;
             const int rest_k = p.K >> 6;
+            const uint64_t pol_ab = policy_evict_last();  // operands kept in L2 (l2hint >= 2)
             uint32_t stage = 0, phase = 0;
             uint32_t d0 = ab ? sA : sSfa, d1 = ab ? sB : sSfb, emp = bar_empty, fb = lead_full, own_full = bar_full;
             bool ok = true;
@@ -286,8 +287,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                             issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
                         }
                         const int x = kb * BKB;
-                        tma_load_2d_pair(d0, &tmap_a, fb, x, arow);
-                        tma_load_2d_pair(d1, &tmap_b, fb, x, brow);
+                        if (p.l2hint >= 2) {
+                            tma_load_2d_pair_hint(d0, &tmap_a, fb, x, arow, pol_ab);
+                            tma_load_2d_pair_hint(d1, &tmap_b, fb, x, brow, pol_ab);
+                        } else {
+                            tma_load_2d_pair(d0, &tmap_a, fb, x, arow);
+                            tma_load_2d_pair(d1, &tmap_b, fb, x, brow);
+                        }
                     } else {
                         const int ysf = kb * KG * 2;
                         tma_load_2d_pair(d0, &tmap_sfa, fb, 0, ysa + ysf);
@@ -501,6 +507,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 named_barrier(1, 32 * kEpiWarps);
             }
         }
+        const uint64_t pol_d = policy_evict_first();  // D stores leave L2 first (l2hint >= 1)
+        const bool d_hint = p.l2hint >= 1;
         int local = 0;
         uint32_t chunk = 0;  // TMA-store boxes issued by this warp (two staging boxes alternate)
         long long t_accw = 0, t_store = 0, c_ready = 0;
@@ -578,7 +586,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                         }
                     }
                 } else if (p.epi.plain()) {
-                    store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha);
+                    store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha, d_hint, pol_d);
                 } else if constexpr (!F16) {
                     store_row_epi_fast<kCols>(acc, p, row, col0, ti.row_end, ti.alpha,
                                               p.epi.bias ? p.epi.bias + (int64_t)ti.group * p.N : nullptr,
@@ -586,7 +594,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 }
             } else {
                 if (p.epi.plain())
-                    store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha);
+                    store_row<kCols, F16>(acc, p, row, col0, ti.row_end, ti.alpha, d_hint, pol_d);
                 else if constexpr (!F16)
                     store_row_epi_fast<kCols>(acc, p, row, col0, ti.row_end, ti.alpha,
                                               p.epi.bias ? p.epi.bias + (int64_t)ti.group * p.N : nullptr,
@@ -614,6 +622,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         tmem_dealloc_pair(tmem_base, L::kTmemCols);
     }
     if (TRACE && threadIdx.x == 0) p.trace[blockIdx.x * kTraceSlots + 9] = global_timer_ns();
+}
+
+// L2 eviction hints of the pair kernel: 0 none, 1 D stores evict-first, 2 also the A
+// and B tile loads evict-last; env NVFP4_PAIR_L2HINT.
+static int pair_l2hint() {
+    static int v = [] {
+        const char *e = std::getenv("NVFP4_PAIR_L2HINT");
+        return e ? std::atoi(e) : 0;
+    }();
+    return v;
 }
 
 // Epilogue stores of the pair kernel: through shared memory with TMA (1) or direct
@@ -724,6 +742,7 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     // to D's extent but not to the group)
     p.gather = gat;
     p.tma_store = (L::kHasStage && epi.plain() && G == 0 && gat.n_dst == 0 && pair_tma_store()) ? 1 : 0;
+    p.l2hint = pair_l2hint();
     p.spin = pair_spin();
     if (p.tma_store && (st = output_map(D, M, N, 32, &td))) return st;
     if ((st = kernel_ctl(&p.ctl))) return st;

@@ -422,6 +422,16 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
         : "memory");
 }
 
+// tma_load_2d_pair with an L2 eviction-priority hint (policy from createpolicy).
+__device__ __forceinline__ void tma_load_2d_pair_hint(uint32_t dst, const CUtensorMap *tmap, uint32_t bar_cluster,
+                                                      int32_t x, int32_t y, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar_cluster), "l"(policy)
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t dst, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst), "r"(ncols)
                  : "memory");
@@ -463,6 +473,14 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
 __device__ __forceinline__ void st_global_v8(void *p, const uint32_t (&v)[8]) {
     asm volatile("st.global.L1::no_allocate.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]),
                  "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+
+// st_global_v8 with an L2 eviction-priority hint (policy from createpolicy).
+__device__ __forceinline__ void st_global_v8_hint(void *p, const uint32_t (&v)[8], uint64_t policy) {
+    asm volatile("st.global.L1::no_allocate.L2::cache_hint.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8}, %9;"
+                 ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+                 "l"(policy)
                  : "memory");
 }
 
