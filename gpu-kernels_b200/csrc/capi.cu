@@ -4,6 +4,7 @@
 #include <atomic>
 #include <cstdlib>
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <utility>
 
@@ -28,6 +29,11 @@ int grouped_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, con
                      uint16_t *D, const int *m_offsets, int groups, int m_total, int N, int K, cudaStream_t stream,
                      const Epi &epi);
 int grouped_sf_pad_zero(uint8_t *SF, const int *m_offsets, int groups, int m_total, int K, cudaStream_t s);
+size_t quantize_dynamic_workspace_bytes();
+int quantize_dynamic_check(const uint16_t *X, const uint8_t *Q, const uint8_t *SF, const float *amax_out,
+                           const float *gs_out, int M, int K);
+int quantize_dynamic_dispatch(const uint16_t *X, uint8_t *Q, uint8_t *SF, float *amax_out, float *gs_out, int M,
+                              int K, void *ws, size_t ws_bytes, cudaStream_t s);
 int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                   int M, int N, int K, cudaStream_t stream, bool f16);
 size_t decode_workspace_bytes(int M, int N);
@@ -62,14 +68,16 @@ static int decode_max_m() {
 // nvfp4_gemm's own decode workspace: one zero-initialised buffer per (device,
 // stream), grown on demand and kept for the life of the process.  Calls on the
 // same stream are ordered, so they may share it.
-static int internal_workspace(size_t need, cudaStream_t stream, void **ws, size_t *bytes) {
+// kind separates users whose workspace contents must not meet (0: decode split-K
+// counters and partials, 1: the dynamic quantizer's barrier and amax partials).
+static int internal_workspace(size_t need, cudaStream_t stream, void **ws, size_t *bytes, int kind = 0) {
     static std::mutex mu;
-    static std::map<std::pair<int, cudaStream_t>, std::pair<void *, size_t>> cache;
+    static std::map<std::tuple<int, cudaStream_t, int>, std::pair<void *, size_t>> cache;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return NVFP4_ERR_CUDA;
     if (!need) return NVFP4_ERR_CUDA;
     std::lock_guard<std::mutex> lock(mu);
-    auto &slot = cache[{dev, stream}];
+    auto &slot = cache[{dev, stream, kind}];
     if (slot.second < need) {
         if (slot.first) {
             cudaStreamSynchronize(stream);
@@ -177,6 +185,18 @@ static int gemm_grouped_epi(const uint8_t *A, const uint8_t *SFA, const uint8_t 
 }
 
 extern "C" {
+
+int nvfp4_quantize_dynamic(const uint16_t *X, uint8_t *Q, uint8_t *SF, float *amax_out, float *gs_out, int M, int K,
+                           void *stream) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int st = quantize_dynamic_check(X, Q, SF, amax_out, gs_out, M, K);
+    if (st) return st;
+    void *ws = nullptr;
+    size_t bytes = 0;
+    st = internal_workspace(quantize_dynamic_workspace_bytes(), s, &ws, &bytes, 1);
+    if (st) return st;
+    return quantize_dynamic_dispatch(X, Q, SF, amax_out, gs_out, M, K, ws, bytes, s);
+}
 
 int nvfp4_gemm_grouped(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const float *alpha,
                        uint16_t *D, const int32_t *m_offsets, int groups, int m_total, int N, int K, void *stream) {

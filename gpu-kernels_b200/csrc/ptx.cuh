@@ -374,6 +374,13 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[COLS]
 }
 
 // Atomic add with release-acquire semantics at GPU scope; returns the old value.
+// 32-bit load with acquire semantics at GPU scope.
+__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const unsigned int *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ int atomic_add_acq_rel_gpu(int *p, int v) {
     int old;
     asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");

@@ -15,6 +15,7 @@
 // per-block reciprocal comes from a 256-entry table.
 #include "common.cuh"
 #include "grouped.cuh"
+#include "ptx.cuh"
 #include "quant_common.cuh"
 
 namespace nvfp4 {
@@ -41,14 +42,11 @@ __device__ __forceinline__ void ld_stream_v8(const void *p, uint32_t (&w)[8]) {
 // are contiguous in the blocked layout and leave as one 32-bit store.  The
 // reciprocal 1/(float(sf)*gs) takes only 256 values per launch, so each CTA
 // tabulates it once in shared memory with the same IEEE operations.
-__global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16 *__restrict__ X, uint8_t *__restrict__ Q,
-                                                       uint8_t *__restrict__ SF, const float *__restrict__ gs_ptr,
-                                                       int64_t n_blocks, int64_t K) {
-    __shared__ float inv_table[256];
-    const float gs = *gs_ptr;
-    const bool gs_ok = gs_usable(gs);
-    inv_table[threadIdx.x] = block_inverse(threadIdx.x, gs, gs_ok);  // blockDim.x == 256
-    __syncthreads();
+// The per-block loop shared by quantize_kernel and quantize_dynamic_kernel: blocks
+// g, g + stride, ... of X (one per lane), inv_table the 256 reciprocals of gs.
+__device__ __forceinline__ void quantize_blocks(const __nv_bfloat16 *__restrict__ X, uint8_t *__restrict__ Q,
+                                                uint8_t *__restrict__ SF, float gs, bool gs_ok,
+                                                const float *inv_table, int64_t n_blocks, int64_t K) {
     const int lane = threadIdx.x & 31;
     const int64_t rest_k = K >> 6;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -97,6 +95,90 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16 *__re
             }
         }
     }
+}
+
+__global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16 *__restrict__ X, uint8_t *__restrict__ Q,
+                                                       uint8_t *__restrict__ SF, const float *__restrict__ gs_ptr,
+                                                       int64_t n_blocks, int64_t K) {
+    __shared__ float inv_table[256];
+    const float gs = *gs_ptr;
+    const bool gs_ok = gs_usable(gs);
+    inv_table[threadIdx.x] = block_inverse(threadIdx.x, gs, gs_ok);  // blockDim.x == 256
+    __syncthreads();
+    quantize_blocks(X, Q, SF, gs, gs_ok, inv_table, n_blocks, K);
+}
+
+// amax, global scale and quantization in one cooperative launch (every CTA resident):
+// each CTA's amax of its blocks goes to partials[blockIdx.x]; a grid barrier (arrival
+// counter bar[0], exit counter bar[1], both back at zero when the kernel ends) orders
+// them before every CTA reduces all partials to the same amax and gs = amax / 2688
+// (the global_scale_kernel's operation), then quantizes its blocks — X, read once
+// from HBM in the first pass, is now mostly in L2.  Same outputs as
+// nvfp4_global_scale followed by nvfp4_quantize.  A barrier wait that outlasts the
+// timeout records it in the status word and the CTA returns.
+__global__ void __launch_bounds__(256) quantize_dynamic_kernel(const __nv_bfloat16 *__restrict__ X,
+                                                               uint8_t *__restrict__ Q, uint8_t *__restrict__ SF,
+                                                               float *amax_out, float *gs_out, unsigned int *bar,
+                                                               float *partials, int64_t n_blocks, int64_t K,
+                                                               KernelCtl ctl) {
+    __shared__ float inv_table[256];
+    __shared__ float wmax[8];
+    __shared__ int abort_cta;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    float m = 0.0f;
+    for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n_blocks; g += stride) {
+        uint32_t w[8];
+        ld_stream_v8(X + g * 16, w);
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[i] << 16)), fabsf(__uint_as_float(w[i] & 0xFFFF0000u))));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int i = 1; i < (int)(blockDim.x >> 5); i++) m = fmaxf(m, wmax[i]);
+        __stcg(partials + blockIdx.x, m);
+        __threadfence();
+        atomicAdd(bar, 1u);
+        // every CTA is resident (cooperative launch), so the count reaches the grid soon
+        const uint64_t t0 = global_timer_ns();
+        int ok = 1;
+        while (ld_acquire_gpu_u32(bar) < gridDim.x) {
+            if (global_timer_ns() - t0 > ctl.wait_timeout_ns) {
+                atomicOr(ctl.status, kDevTimeout);
+                ok = 0;
+                break;
+            }
+            __nanosleep(64);
+        }
+        abort_cta = !ok;
+        if (ok && atomicAdd(bar + 1, 1u) == gridDim.x - 1) {  // the last CTA past the barrier resets it
+            bar[0] = 0;
+            bar[1] = 0;
+        }
+    }
+    __syncthreads();
+    if (abort_cta) return;
+    m = 0.0f;
+    for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) m = fmaxf(m, __ldcg(partials + i));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    __syncthreads();  // wmax is reused
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = wmax[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); i++) m = fmaxf(m, wmax[i]);
+    const float gs = __fdiv_rn(m, 2688.0f);  // amax / (6 * 448), as global_scale_kernel
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        if (amax_out) *amax_out = m;
+        if (gs_out) *gs_out = gs;
+    }
+    const bool gs_ok = gs_usable(gs);
+    inv_table[threadIdx.x] = block_inverse(threadIdx.x, gs, gs_ok);  // blockDim.x == 256
+    __syncthreads();
+    quantize_blocks(X, Q, SF, gs, gs_ok, inv_table, n_blocks, K);
 }
 
 // Grouped quantizer: the same per-block arithmetic over a stacked [m_total, K]
@@ -235,6 +317,67 @@ __global__ void __launch_bounds__(256) scale_codes_kernel(const uint16_t *__rest
     const bool ok = gs_usable(gs);
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         codes[i] = (uint8_t)table_scale_code(fabsf(__uint_as_float((uint32_t)amax[i] << 16)), guess, &tab, ok);
+}
+
+int sf_pad_zero(uint8_t *SF, int M, int K, cudaStream_t s, const DeviceInfo &di);
+
+// Workspace of quantize_dynamic_dispatch: the barrier's two counters (zero between
+// calls) and one amax partial per CTA of the largest grid.
+static int dynamic_grid(const DeviceInfo &di) {
+    static int per_sm[64] = {};
+    if (!per_sm[di.device]) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, quantize_dynamic_kernel, 256, 0) != cudaSuccess || n < 1)
+            return 0;
+        per_sm[di.device] = n;
+    }
+    return per_sm[di.device] * di.sm_count;
+}
+
+size_t quantize_dynamic_workspace_bytes() {
+    DeviceInfo di;
+    if (device_info(&di)) return 0;
+    return 256 + (size_t)dynamic_grid(di) * sizeof(float);
+}
+
+// Argument checks of quantize_dynamic_dispatch (host only, no device call).
+int quantize_dynamic_check(const uint16_t *X, const uint8_t *Q, const uint8_t *SF, const float *amax_out,
+                           const float *gs_out, int M, int K) {
+    if (!X || !Q || !SF) return NVFP4_ERR_INVALID;
+    if (M < 1 || K < 64 || K % 64) return NVFP4_ERR_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(X) & 31u) || !aligned16(Q) || (reinterpret_cast<uintptr_t>(SF) & 3u) ||
+        (reinterpret_cast<uintptr_t>(amax_out) & 3u) || (reinterpret_cast<uintptr_t>(gs_out) & 3u))
+        return NVFP4_ERR_ALIGN;
+    return NVFP4_OK;
+}
+
+// bf16 X -> amax, global scale, NVFP4 codes and blocked scales in one cooperative
+// launch (ws: quantize_dynamic_workspace_bytes(), zero-filled once, one per stream).
+int quantize_dynamic_dispatch(const uint16_t *X, uint8_t *Q, uint8_t *SF, float *amax_out, float *gs_out, int M,
+                              int K, void *ws, size_t ws_bytes, cudaStream_t s) {
+    int st = quantize_dynamic_check(X, Q, SF, amax_out, gs_out, M, K);
+    if (st) return st;
+    DeviceInfo di;
+    if ((st = device_info(&di))) return st;
+    const int max_grid = dynamic_grid(di);
+    if (!max_grid) return NVFP4_ERR_CUDA;
+    if (!ws || ws_bytes < 256 + (size_t)max_grid * sizeof(float) || (reinterpret_cast<uintptr_t>(ws) & 255u))
+        return NVFP4_ERR_WORKSPACE;
+    KernelCtl ctl;
+    if ((st = kernel_ctl(&ctl))) return st;
+    const int64_t n_blocks = (int64_t)M * K / 16;
+    const unsigned grid = (unsigned)std::min<int64_t>(max_grid, (n_blocks + 255) / 256);
+    const __nv_bfloat16 *x = reinterpret_cast<const __nv_bfloat16 *>(X);
+    unsigned int *bar = static_cast<unsigned int *>(ws);
+    float *partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + 256);
+    int64_t nb = n_blocks, kk = K;
+    void *args[] = {&x, &Q, &SF, &amax_out, &gs_out, &bar, &partials, &nb, &kk, &ctl};
+    if (cudaLaunchCooperativeKernel((void *)quantize_dynamic_kernel, dim3(grid), dim3(256), args, 0, s) !=
+        cudaSuccess)
+        return NVFP4_ERR_CUDA;
+    count_launch();
+    if ((st = cuda_status(cudaGetLastError()))) return st;
+    return sf_pad_zero(SF, M, K, s, di);
 }
 
 // Zero the padding scale rows [M_g, pad128(M_g)) of every group of a grouped scale

@@ -10,6 +10,6 @@ from .layout import (from_blocked, grouped_sf_block0, grouped_sf_bytes, pad128, 
                      swiglu_interleave, to_blocked)
 from .ops import (create_tensors, device_status, gemm, gemm_epilogue, gemm_grouped,  # noqa: F401
                   gemm_grouped_epilogue, gemm_host, global_scale, launch_count, matmul_nvfp4, quantize,
-                  quantize_grouped, selftest_wait_timeout, set_wait_timeout_ns)
+                  quantize_dynamic, quantize_grouped, selftest_wait_timeout, set_wait_timeout_ns)
 from . import runner_io  # noqa: F401,E402
 from . import torch_ops  # noqa: F401,E402  (registers torch.ops.nvfp4_b200.gemm / .quantize)

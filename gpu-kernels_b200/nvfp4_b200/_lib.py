@@ -45,6 +45,7 @@ SIGNATURES = {
     "nvfp4_selftest_wait_timeout": (C.c_int, [C.c_uint64]),
     "nvfp4_launch_count": (C.c_uint64, []),
     "nvfp4_gemm_trace": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp, _vp]),
+    "nvfp4_quantize_dynamic": (C.c_int, [_u16p, _u8p, _u8p, _f32p, _f32p, C.c_int, C.c_int, _vp]),
     "nvfp4_scale_codes": (C.c_int, [_u16p, C.c_int64, _vp, _u8p, _vp]),
     "nvfp4_gemm_trace_epilogue": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int,
                                             C.POINTER(Epilogue), _vp, _vp]),

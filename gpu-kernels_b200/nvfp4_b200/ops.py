@@ -130,6 +130,22 @@ def gemm_epilogue(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torc
     return d if d is not None else (q, sf)
 
 
+def quantize_dynamic(x: torch.Tensor, q_out: Optional[torch.Tensor] = None,
+                     sf_out: Optional[torch.Tensor] = None):
+    """global_scale + quantize in one kernel (nvfp4_quantize_dynamic): bf16 [M, K] ->
+    (codes [M, K/2], blocked scales, gs fp32 [1] on the device), byte-identical to
+    quantize(x, global_scale(x)[1])."""
+    if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous 2-D bf16 CUDA tensor")
+    M, K = x.shape
+    q = q_out if q_out is not None else torch.empty(M, K // 2, dtype=torch.uint8, device=x.device)
+    sf = sf_out if sf_out is not None else torch.empty(sf_bytes(M, K), dtype=torch.uint8, device=x.device)
+    gs = torch.empty(1, dtype=torch.float32, device=x.device)
+    check(lib().nvfp4_quantize_dynamic(x.data_ptr(), q.data_ptr(), sf.data_ptr(), None, gs.data_ptr(), M, K,
+                                       _stream(x.device)), "nvfp4_quantize_dynamic")
+    return q, sf, gs
+
+
 def _offsets_tensor(m_offsets: torch.Tensor, device: torch.device) -> torch.Tensor:
     if m_offsets.dtype != torch.int32 or m_offsets.dim() != 1 or m_offsets.numel() < 2 or \
             m_offsets.device != device or not m_offsets.is_contiguous():

@@ -88,6 +88,15 @@ NVFP4_API int nvfp4_quantize(const uint16_t *X, uint8_t *Q, uint8_t *SF, const f
  */
 NVFP4_API int nvfp4_global_scale(const uint16_t *X, int64_t n, float *amax_out, float *gs_out,
                        void *stream);
+/* nvfp4_global_scale and nvfp4_quantize in one pass over X (M x K bf16, K % 64):
+ * amax and gs = amax / (6 * 448) into amax_out / gs_out (device fp32, either may be
+ * NULL), then Q and SF with that gs — byte-identical to the two calls in sequence.
+ * One cooperative launch: each CTA's amax, a grid barrier, then the quantization
+ * re-reads X while it is still in L2.  Uses a small library-owned workspace per
+ * (device, stream), allocated on the first call there.  No counterpart in the
+ * reference (it has no quantizer). */
+NVFP4_API int nvfp4_quantize_dynamic(const uint16_t *X, uint8_t *Q, uint8_t *SF, float *amax_out, float *gs_out,
+                                     int M, int K, void *stream);
 
 /*
  * NVFP4 GEMM, D = alpha * A . B^T, bf16 out.  Replaces the reference's best B200

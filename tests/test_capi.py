@@ -65,3 +65,13 @@ def test_no_gpu_call_fails_cleanly_without_device(nv):
     p = C.c_void_p(1 << 20)
     # valid arguments reach the device query, which reports an error (no crash, no exit)
     assert L.nvfp4_gemm(p, p, p, p, 1.0, p, 128, 256, 256, None) in (-4, -6)
+
+
+def test_quantize_dynamic_rejects_bad_arguments_on_host(nv):
+    L = nv.lib()
+    f = 0x10000  # never dereferenced: every case fails its host-side check first
+    assert L.nvfp4_quantize_dynamic(None, f, f, None, f, 128, 256, None) == -1      # no X
+    assert L.nvfp4_quantize_dynamic(f, f, f, None, f, 128, 100, None) == -2         # K % 64
+    assert L.nvfp4_quantize_dynamic(f, f, f, None, f, 0, 256, None) == -2           # M < 1
+    assert L.nvfp4_quantize_dynamic(f + 16, f, f, None, f, 128, 256, None) == -3    # X 32-byte aligned
+    assert L.nvfp4_quantize_dynamic(f, f, f, None, f + 2, 128, 256, None) == -3     # gs 4-byte aligned

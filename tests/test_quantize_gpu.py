@@ -155,3 +155,44 @@ def test_quantize_then_gemm_roundtrip(nv, oracle, cuda_dev):
     ref = oracle.bf16_bits_to_f32(d16).reshape(M, N)
     err = np.abs(d.float().cpu().numpy() - ref).max() / np.abs(ref).max()
     assert err <= 1e-2
+
+
+@pytest.mark.parametrize("M,K", [(1, 64), (200, 320), (513, 1024), (4096, 4096)])
+def test_quantize_dynamic_equals_global_scale_then_quantize(nv, oracle, cuda_dev, M, K):
+    """One cooperative kernel (amax, grid barrier, gs, quantize) against the two calls:
+    the same gs and the same bytes, twice in a row (the barrier resets itself)."""
+    x = oracle.student_t3_bf16(M, K, seed=M + 3, n_outlier_cols=1, gain=50.0)
+    xt = torch.from_numpy(x.view(np.int16)).to(cuda_dev).view(torch.bfloat16)
+    _, gs = nv.global_scale(xt)
+    q_ref, sf_ref = nv.quantize(xt, gs)
+    for _ in range(2):
+        q, sf, gs2 = nv.quantize_dynamic(xt)
+        torch.cuda.synchronize()
+        nv.device_status()
+        assert gs2.item() == gs.item()
+        assert torch.equal(q, q_ref) and torch.equal(sf, sf_ref)
+    q_o, sf_o = oracle.quantize(x, float(gs.item()))
+    assert np.array_equal(q.cpu().numpy(), q_o) and np.array_equal(sf.cpu().numpy(), sf_o)
+
+
+def test_quantize_dynamic_in_cuda_graph(nv, cuda_dev):
+    M, K = 1024, 2048
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(cuda_dev)
+    q = torch.empty(M, K // 2, dtype=torch.uint8, device=cuda_dev)
+    sf = torch.empty(nv.sf_bytes(M, K), dtype=torch.uint8, device=cuda_dev)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        nv.quantize_dynamic(x, q_out=q, sf_out=sf)  # the stream's workspace is made here
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            nv.quantize_dynamic(x, q_out=q, sf_out=sf)
+    x.mul_(3.0)  # new data, new global scale, same buffers
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    nv.device_status()
+    del g
+    _, gs = nv.global_scale(x)
+    q_ref, sf_ref = nv.quantize(x, gs)
+    assert torch.equal(q, q_ref) and torch.equal(sf, sf_ref)
