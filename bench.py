@@ -240,6 +240,74 @@ def cpu_reference_sample(a, sfa, b, sfb, alpha, M, N, K, target_s=12.0):
             "sample": ref.describe(rows) + f"; {dt:.1f} s"}, rows, dt
 
 
+def cpu_configs_section():
+    """The host reference (oracle/, all host threads) on the other BASELINE configs, each
+    in the unit the GPU section for it reports: configs[0] 256^3 (quantize both
+    operands + dequant GEMM), configs[2] decode against W1 [28672, 8192] for M in
+    {1, 16, 64, 128} (each call dequantises the weight and multiplies: HBM-metric GB/s
+    of the same algorithmic bytes), configs[4] (quantize the Student-t activations +
+    dequant GEMM of all 4096 rows against W [14336, 4096], whose dequantisation is
+    charged once)."""
+    from oracle import oracle as o
+    import numpy as np
+    T = o.max_threads()
+    out = {"cores": T, "kind": "port"}
+
+    def quantized(rows, cols, seed, std=1.0):
+        x = o.normal_bf16((rows, cols), seed=seed, std=std, nthreads=T)
+        gs = o.global_scale_for(o.amax_bf16(x))
+        q, sf = o.quantize(x, gs, nthreads=T)
+        return q, sf, gs
+
+    # configs[0]: 256^3 end to end from bf16
+    M = N = K = 256
+    xa = o.normal_bf16((M, K), seed=1, nthreads=T)
+    xb = o.normal_bf16((N, K), seed=2, nthreads=T)
+    t0 = time.perf_counter()
+    ga, gb = o.global_scale_for(o.amax_bf16(xa)), o.global_scale_for(o.amax_bf16(xb))
+    a, sfa = o.quantize(xa, ga, nthreads=T)
+    b, sfb = o.quantize(xb, gb, nthreads=T)
+    o.gemm(a, sfa, b, sfb, float(np.float32(ga) * np.float32(gb)), M, N, K, nthreads=T)
+    dt = time.perf_counter() - t0
+    out["c1_256"] = {"ms": dt * 1e3, "tflops": 2.0 * M * N * K / dt / 1e12,
+                     "what": "amax + quantize of both bf16 operands + dequant GEMM + bf16"}
+
+    # configs[2]: decode against W1
+    N, K = 28672, 8192
+    w, wsf, gw = quantized(N, K, 3, std=0.02)
+    rows = []
+    for M in (1, 16, 64, 128):
+        x, xsf, gx = quantized(M, K, 4 + M)
+        t0 = time.perf_counter()
+        wf = o.dequant_rows(w, wsf, 0, N, K, nthreads=T)
+        xf = o.dequant_rows(x, xsf, 0, M, K, nthreads=T)
+        o.sgemm_nt(xf, wf, float(np.float32(gx) * np.float32(gw)), nthreads=T)
+        dt = time.perf_counter() - t0
+        del wf
+        nbytes = N * K // 2 + N * K // 16 + M * K // 2 + M * K // 16 + 2 * M * N
+        rows.append({"M": M, "N": N, "K": K, "ms": dt * 1e3, "gbs": nbytes / dt / 1e9})
+    out["c3_decode_w1"] = rows
+    del w, wsf
+
+    # configs[4]: quantize X + GEMM against a pre-quantized W
+    M, N, K = 4096, 14336, 4096
+    x = o.student_t3_bf16(M, K, seed=9, n_outlier_cols=4, gain=50.0)
+    w, wsf, gw = quantized(N, K, 10, std=0.02)
+    t0 = time.perf_counter()
+    wf = o.dequant_rows(w, wsf, 0, N, K, nthreads=T)
+    t_w = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    gx = o.global_scale_for(o.amax_bf16(x, nthreads=T))
+    xq, xsf = o.quantize(x, gx, nthreads=T)
+    xf = o.dequant_rows(xq, xsf, 0, M, K, nthreads=T)
+    o.sgemm_nt(xf, wf, float(np.float32(gx) * np.float32(gw)), nthreads=T)
+    dt = time.perf_counter() - t0 + t_w
+    out["c5"] = {"ms": dt * 1e3, "tflops": 2.0 * M * N * K / dt / 1e12,
+                 "what": "amax + quantize of X [4096, 4096] + dequant GEMM against W [14336, 4096] "
+                         f"(W's dequantisation, {t_w:.2f} s, included)"}
+    return out
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -865,8 +933,10 @@ def run_ours(args):
         moe = moe_section(nv, dev)
         epi = epilogue_section(nv, sets, M, N, K)
     gath = gather_section(nv, dev, world, rank) if (world > 1 and not args.no_gather) else None
+    cpu_cfg = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu, _, _ = cpu_reference_sample(a, sfa, b, sfb, alpha, M, N, K, target_s=args.cpu_seconds)
+        cpu_cfg = cpu_configs_section()
 
     if rank == 0:
         line = {
@@ -893,6 +963,8 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if cpu_cfg is not None:
+            line["cpu_configs"] = cpu_cfg
         if vendor is not None:
             line["vendor_scaled_mm"] = vendor
         if decode is not None:
