@@ -376,7 +376,7 @@ def vendor_scaled_mm(sets, M, N, K, reps=50):
 
 
 def decode_section(nv, dev, pk, reps=30):
-    """skinny-M GEMMs against the two FFN weights, judged on HBM
+    """skinny-M GEMMs against the two FFN weights, measured on HBM
     GB/s.  Weights rotate over 3 sets (> 3x L2).  Bytes per call follow the
     algorithmic count N*K/2 + N*K/16 + M*K/2 + M*K/16 + 2*M*N.  `gbs` is device time
     per call with the calls replayed from a CUDA graph (how a decode loop launches
@@ -585,7 +585,7 @@ def moe_section(nv, dev, reps=20):
            "dense_same_shape_ms": dense_ms, "dense_same_shape_tflops": flops / (dense_ms / 1e3) / 1e12}
 
     # Decode: 32 tokens x top-2 = 64 routed rows.  The grouped call (m_total <= 128:
-    # the stream-K kernel over the active experts' weight tiles) is judged on HBM
+    # the stream-K kernel over the active experts' weight tiles) is measured on HBM
     # bytes: each active expert's weights and scales read once (the 8 experts' 235 MB
     # exceed L2).  Beside it, one decode GEMM per active expert.
     dec_tokens = 32

@@ -7,8 +7,8 @@ D = alpha * A . B^T with B [N, K/2] split by rows: rank p owns B rows
 replicated.  Each rank computes D_p = A . B_p^T [M, n1_p - n0_p] with no
 communication; the full D is assembled with one all-gather only when asked for.
 
-The reference has no multi-GPU path (SURVEY: "Distributed communication backend:
-none"); this module is new.  It is backend-agnostic (NCCL on GPUs, gloo in the
+The reference has no multi-GPU path (its kernels and runner use one GPU and no
+communication library); this module is new.  It is backend-agnostic (NCCL on GPUs, gloo in the
 CPU tests) and takes the per-rank GEMM as a function so the host logic can be
 tested without a GPU.
 """

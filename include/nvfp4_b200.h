@@ -117,7 +117,7 @@ NVFP4_API int nvfp4_gemm_persistent(const uint8_t *A, const uint8_t *SFA, const 
                const uint8_t *SFB, float alpha, uint16_t *D, int M, int N, int K, void *stream);
 
 /*
- * Skinny-M (1 <= M <= 128) split-K / stream-K GEMM, bf16 out, judged on HBM GB/s.
+ * Skinny-M (1 <= M <= 128) split-K / stream-K GEMM, bf16 out, bound by HBM bandwidth.
  * Replaces nothing that runs in the reference: its launchers produce zero tiles
  * for M < 128 (matmul/sm100_nvfp4/nvfp4_v5.cu:163-176, 287-309).
  * `workspace` (256-byte aligned, >= nvfp4_gemm_decode_workspace_size(M, N) bytes)
