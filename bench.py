@@ -869,6 +869,8 @@ def run_ours(args):
         step(i)
     torch.cuda.synchronize()
     nv.device_status()
+    # the SM clock the GEMM runs at as the timed region starts (one traced launch)
+    in_kernel_before = in_kernel_clock(nv, sets[0], d, M, N, K, dev)
 
     # ---- timed region: device time with CUDA events on the launching stream
     launches0 = nv.launch_count()
@@ -884,7 +886,7 @@ def run_ours(args):
         barrier(world)
     launches = nv.launch_count() - launches0
     nv.device_status()
-    in_kernel_mhz = in_kernel_clock(nv, sets[0], d, M, N, K, dev)
+    in_kernel_after = in_kernel_clock(nv, sets[0], d, M, N, K, dev)
     per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
     total_ms = max_over_ranks(sum(per), world)
     ms_step = total_ms / args.steps
@@ -955,9 +957,12 @@ def run_ours(args):
                          "frac_of_nominal_9000": achieved / 9000.0,
                          "kernel_ms": kernel_ms, "flops_per_launch": flops},
             "gpu_launches": int(launches),
-            "clocks": dict(clk.summary(), in_kernel_sm_mhz=in_kernel_mhz,
+            "clocks": dict(clk.summary(), in_kernel_sm_mhz=in_kernel_before,
+                           in_kernel_sm_mhz_after=in_kernel_after,
                            in_kernel_note="SM cycles (clock64) / ns (globaltimer) of the MMA thread over one "
-                                          "traced launch of the same GEMM right after the timed region"),
+                                          "traced launch of the same GEMM right before the timed region (after "
+                                          "warm-up) and right after it; the 1 kW power cap can lower the clock "
+                                          "after a long run of these GEMMs"),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                     "ms_per_step": e2e_ms, "path": "pinned host -> nvfp4_gemm_host (4x4 blocks, copies overlapped) -> pinned host"},
         }
