@@ -146,6 +146,36 @@ def test_c2_full_size_sampled(nv, oracle, cuda_dev, N, K):
     assert not torch.isnan(d).any()
 
 
+def test_c4_full_size_properties(nv, oracle, cuda_dev):
+    """BASELINE config 3's prefill shape on one GPU (M=16384, N=28672, K=8192: 7.7e15
+    FLOP, 940 MB of bf16 D), checked through properties that hold at any size: 32-row
+    slices against the oracle (first, middle, last tile rows); every one of 8 weight
+    shards (the multi-GPU split, whole 128-row scale blocks) gives bit for bit the
+    same columns as the full GEMM (each output element is accumulated by one CTA over
+    the same K order); two runs identical."""
+    from nvfp4_b200.dist import shard_bounds, shard_weight
+    M, N, K = 16384, 28672, 8192
+    a, sfa, gsa = quantized_operands(oracle, M, K, seed=31)
+    b, sfb, gsb = quantized_operands(oracle, N, K, seed=32)
+    alpha = float(np.float32(gsa) * np.float32(gsb))
+    ta, tsa, tb, tsb = (to_dev(t, cuda_dev) for t in (a, sfa, b, sfb))
+    d = nv.gemm(ta, tsa, tb, tsb, alpha)
+    d2 = nv.gemm(ta, tsa, tb, tsb, alpha)
+    torch.cuda.synchronize()
+    nv.device_status()
+    assert torch.equal(d, d2), "run-to-run determinism"
+    del d2
+    for r in range(8):
+        n0, n1 = shard_bounds(N, 8, r)
+        bs, ss = shard_weight(tb, tsb, K, 8, r)
+        ds = nv.gemm(ta, tsa, bs.contiguous(), ss.contiguous(), alpha)
+        torch.cuda.synchronize()
+        assert torch.equal(ds, d[:, n0:n1]), f"shard {r}"
+    check_against_oracle(oracle, d, a, sfa, b, sfb, alpha, M, N, K,
+                         rows=[(0, 32), (8192 + 96, 32), (M - 32, 32)])
+    assert not torch.isnan(d).any()
+
+
 @pytest.mark.parametrize("variant,ring,shape", [
     ("single", "11x64", (520, 776, 1344)),
     ("pair", "11x64", (520, 776, 1344)),
