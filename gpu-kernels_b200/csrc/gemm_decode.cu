@@ -37,6 +37,9 @@ constexpr int kBlockKBytes = 128;    // 256 fp4 per stage row
 constexpr int kKGroups = 4;
 constexpr int kThreads = 32 * 6;     // producer, MMA, 4 epilogue warps
 constexpr int kSmemBudget = 225 * 1024;
+// Grouped form: activation rows are loaded in boxes of 16 (two 1 KB swizzle atoms;
+// MPAD rows when MPAD is 8), only as many as the tile's group has rows.
+constexpr int kXBoxRows = 16;
 
 // Two CTAs per SM (COLOC): 228 KB of shared memory per SM, 1 KB of it reserved per CTA.
 constexpr int kColocSmemMax = (233472 - 2 * 1024) / 2;
@@ -469,11 +472,19 @@ __global__ void __launch_bounds__(kThreads, COLOC ? 2 : 1)
                 const int tile = (int)(it / p.num_kb), kb = (int)(it % p.num_kb);
                 const DTile dt = dtile(tile);
                 const int kg = min(kKGroups, p.k_groups - kb * kKGroups);
-                mbar_arrive_expect_tx(bar_full + 8 * s, L::kW + L::kX + 2u * kg * 512u);
+                // grouped: only the group's rows of activations (16-row boxes); the MMA
+                // still reads MPAD rows, and the output rows past the group that the
+                // stale ones feed are never stored
+                constexpr int XB = MPAD < kXBoxRows ? MPAD : kXBoxRows;  // rows per activation box
+                const int x_boxes = GROUPED ? min(MPAD / XB, (dt.rows + XB - 1) / XB) : 1;
+                const uint32_t x_bytes = GROUPED ? (uint32_t)(x_boxes * XB * kBlockKBytes) : (uint32_t)L::kX;
+                mbar_arrive_expect_tx(bar_full + 8 * s, L::kW + x_bytes + 2u * kg * 512u);
                 issued_mask |= 1u << s;
                 issued_parity = (issued_parity & ~(1u << s)) | (ph << s);
                 tma_load_2d_hint(sW + s * L::kW, &tmap_w, bar_full + 8 * s, kb * kBlockKBytes, dt.w_row, pol_w);
-                tma_load_2d_hint(sX + s * L::kX, &tmap_x, bar_full + 8 * s, kb * kBlockKBytes, dt.x_row, pol_x);
+                for (int xb = 0; xb < x_boxes; xb++)
+                    tma_load_2d_hint(sX + s * L::kX + xb * XB * kBlockKBytes, &tmap_x, bar_full + 8 * s,
+                                     kb * kBlockKBytes, dt.x_row + xb * XB, pol_x);
                 bulk_load_hint(sSfw + s * L::kSfw, p.sfb + (dt.sfw_block * rest_k + kb * kKGroups) * 512, kg * 512u,
                                bar_full + 8 * s, pol_w);
                 bulk_load_hint(sSfx + s * L::kSfx, p.sfa + (dt.sfx_block * rest_k + kb * kKGroups) * 512, kg * 512u,
@@ -728,7 +739,8 @@ static int launch_ring(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     const int w_rows = GROUPED ? groups * N : N;
     CUtensorMap tw, tx;
     int st = gemm::operand_map(B, w_rows, K, kTileN, kBlockKBytes, &tw);  // cached tensor maps
-    if (!st) st = gemm::operand_map(A, M, K, MPAD, kBlockKBytes, &tx);
+    // grouped: activations in 16-row boxes, as many as the tile's group has rows
+    if (!st) st = gemm::operand_map(A, M, K, GROUPED ? (MPAD < kXBoxRows ? MPAD : kXBoxRows) : MPAD, kBlockKBytes, &tx);
     if (st) return st;
     Params p;
     p.sfa = SFA;
