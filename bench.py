@@ -247,7 +247,7 @@ def cpu_configs_section():
     {1, 16, 64, 128} (each call dequantises the weight and multiplies: HBM-metric GB/s
     of the same algorithmic bytes), configs[4] (quantize the Student-t activations +
     dequant GEMM of all 4096 rows against W [14336, 4096], whose dequantisation is
-    charged once)."""
+    charged once), and a 1024 x 2048 x 8192 slice of configs[3]."""
     from oracle import oracle as o
     import numpy as np
     T = o.max_threads()
@@ -305,6 +305,25 @@ def cpu_configs_section():
     out["c5"] = {"ms": dt * 1e3, "tflops": 2.0 * M * N * K / dt / 1e12,
                  "what": "amax + quantize of X [4096, 4096] + dequant GEMM against W [14336, 4096] "
                          f"(W's dequantisation, {t_w:.2f} s, included)"}
+    del w, wsf, wf, xf
+
+    # the full 16384 x 28672 x 8192 job is 7.7e12 FLOP (~30-50 s on the
+    # host, too long for the default run), so a slice of it: 1024 rows of A against
+    # 2048 rows of W, full K, both slices dequantised inside the timed region; the rate
+    # stands for the whole job.
+    M, N, K = 1024, 2048, 8192
+    a, sfa, ga = quantized(M, K, 11)
+    w, wsf, gw = quantized(N, K, 12, std=0.02)
+    t0 = time.perf_counter()
+    af = o.dequant_rows(a, sfa, 0, M, K, nthreads=T)
+    wf = o.dequant_rows(w, wsf, 0, N, K, nthreads=T)
+    o.sgemm_nt(af, wf, float(np.float32(ga) * np.float32(gw)), nthreads=T)
+    dt = time.perf_counter() - t0
+    full = 2.0 * 16384 * 28672 * 8192
+    rate = 2.0 * M * N * K / dt
+    out["c4_slice"] = {"ms": dt * 1e3, "tflops": rate / 1e12, "full_job_s_extrapolated": full / rate,
+                       "what": "dequant GEMM of A[0:1024] x W[0:2048] at K=8192, a slice of "
+                               "configs[3] (16384 x 28672 x 8192)"}
     return out
 
 
