@@ -837,6 +837,17 @@ def gather_section(nv, dev, world, rank, reps=10):
     return res
 
 
+def run_moe_workload(args):
+    """The mixture-of-experts section alone (grouped prefill and decode, the SwiGLU
+    expert FFN), one JSON line: for profiling its kernels."""
+    import nvfp4_b200 as nv
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    res = moe_section(nv, dev)
+    print(json.dumps({"workload": "moe", **res}), flush=True)
+    return 0
+
+
 def run_decode_workload(args, M, N, K):
     """One skinny-M shape alone (for profiling): weights rotate over 3 sets."""
     import nvfp4_b200 as nv
@@ -1053,7 +1064,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-shape GB/s section")
     ap.add_argument("--no-gather", action="store_true", help="skip the N>1 all-gather section")
     ap.add_argument("--workload", default="square",
-                    help="square (default, the bench line), decode:M:N:K or quantize:M:K (one kernel, for profiling)")
+                    help="square (default, the bench line), decode:M:N:K or quantize:M:K (one kernel, for "
+                         "profiling), moe (the mixture-of-experts section alone)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1062,6 +1074,8 @@ def main():
     if args.workload.startswith("decode:"):
         M, N, K = (int(v) for v in args.workload.split(":")[1:])
         return run_decode_workload(args, M, N, K)
+    if args.workload == "moe":
+        return run_moe_workload(args)
     if args.workload.startswith("quantize:"):
         M, K = (int(v) for v in args.workload.split(":")[1:])
         return run_quantize_workload(args, M, K)

@@ -61,6 +61,9 @@ CASES = [
     ([0, 3, 3, 10, 40], 48, 512, 1024),
     ([0, 0, 9, 9, 9, 30, 31, 31, 64], 64, 1024, 2048),
     ([0, 128], 128, 256, 512),
+    # the group limit: 256 experts, 96 routed rows over a few dozen of them
+    ([0] + np.cumsum(np.bincount(np.random.default_rng(5).integers(0, 256, 96), minlength=256)).tolist(),
+     96, 128, 256),
 ]
 
 
@@ -162,6 +165,47 @@ def test_gemm_grouped_graph_follows_device_routing(nv, oracle, cuda_dev):
     torch.cuda.synchronize()
     got, want = out.float(), ref.float()
     assert (got - want).abs().max().item() <= 1e-2 * want.abs().max().item()
+    assert not torch.equal(first, out)
+
+
+@pytest.mark.gpu
+def test_gemm_grouped_decode_graph_follows_device_routing(nv, oracle, cuda_dev):
+    """The decode-size grouped kernel (m_total <= 128) derives its schedule from the
+    device-side offsets, so a captured call follows a routing written after capture:
+    three experts, then every row in one expert (a 64-row tile)."""
+    offsets, m_total, N, K = [0, 20, 50, 64], 64, 256, 512
+    x, gsa, offs, q, sf, bq, bsf, alphas = _make(oracle, nv, cuda_dev, offsets, m_total, N, K, seed=13)
+    b, sfb, al = (torch.from_numpy(t).to(cuda_dev) for t in (bq, bsf, alphas))
+    out = torch.zeros(m_total, N, dtype=torch.bfloat16, device=cuda_dev)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        nv.gemm_grouped(q, sf, b, sfb, al, offs, out=out)  # warm-up: tensor maps, this stream's workspace
+        s.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            nv.gemm_grouped(q, sf, b, sfb, al, offs, out=out)
+    graph.replay()
+    torch.cuda.synchronize()
+    first = out.clone()
+    qh, sfh = q.cpu().numpy(), sf.cpu().numpy()
+    blk = 128 * K // 16
+    for g, (a, z) in enumerate(_group_rows(offsets, m_total)):
+        _, d16 = oracle.gemm(qh[a:z], sfh[g * blk:(g + 1) * blk], bq[g * N:(g + 1) * N],
+                             bsf[g * (N // 128) * blk:(g + 1) * (N // 128) * blk], float(alphas[g]), z - a, N, K)
+        ref = oracle.bf16_bits_to_f32(d16).reshape(z - a, N)
+        assert np.abs(first[a:z].float().cpu().numpy() - ref).max() <= 1e-2 * np.abs(ref).max(), g
+    new = torch.tensor([0, 0, 64, 64], dtype=torch.int32, device=cuda_dev)
+    xt = torch.from_numpy(x.view(np.int16)).to(cuda_dev).view(torch.bfloat16)
+    nv.quantize_grouped(xt, torch.tensor([gsa], dtype=torch.float32, device=cuda_dev), new, q_out=q, sf_out=sf)
+    offs.copy_(new)
+    graph.replay()
+    torch.cuda.synchronize()
+    nv.device_status()
+    del graph
+    _, d16 = oracle.gemm(q.cpu().numpy(), sf.cpu().numpy()[:blk], bq[N:2 * N], bsf[(N // 128) * blk:2 * (N // 128) * blk],
+                         float(alphas[1]), m_total, N, K)
+    ref = oracle.bf16_bits_to_f32(d16).reshape(m_total, N)
+    assert np.abs(out.float().cpu().numpy() - ref).max() <= 1e-2 * np.abs(ref).max()
     assert not torch.equal(first, out)
 
 
