@@ -7,9 +7,10 @@ cudaMalloc's possible device-wide synchronisation is not acceptable).  Its split
 scratch is a fixed 4 MiB device array inside the library, shared by every call.
 
 Checked here through the C ABI: two calls in a row, each against the existing
-entry point nvfp4_gemm_decode with a caller-provided workspace, within the GEMM
-tolerance the other tests use (max |D - D_ref| / max |D_ref| <= 1e-2); and shapes
-whose scratch need exceeds the fixed array are refused.  This file is collected
+entry point nvfp4_gemm_decode with a caller-provided workspace and against the CPU
+oracle's dequantise-then-fp32 GEMM, within the GEMM tolerance the other tests use
+(max |D - D_ref| / max |D_ref| <= 1e-2); and shapes whose scratch need exceeds the
+fixed array are refused.  This file is collected
 last so that a run stopping at the first failure has already run every other
 test; it also passes alone in a fresh process.
 """
@@ -62,7 +63,7 @@ def _rel_err(d, ref):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 28672, 8192), (16, 8192, 28672), (9, 1000, 320)])
-def test_no_alloc_matches_workspace_entry_point_twice(nv, cuda_dev, M, N, K):
+def test_no_alloc_matches_workspace_entry_point_twice(nv, oracle, cuda_dev, M, N, K):
     L = nv.lib()
     assert L.nvfp4_gemm_decode_workspace_size(M, N) <= SCRATCH_LIMIT
     for call, (seed, alpha) in enumerate([(11, 1.0), (12, 0.25)]):  # two calls in a row, different data
@@ -73,6 +74,11 @@ def test_no_alloc_matches_workspace_entry_point_twice(nv, cuda_dev, M, N, K):
         nv.device_status()
         err = _rel_err(d, ref)
         assert err <= TOL, f"call {call}: rel err {err:.3e}"
+        a, sfa, b, sfb = (t.cpu().numpy() for t in ops)
+        _, d16 = oracle.gemm(a, sfa, b, sfb, alpha, M, N, K)
+        ref_o = torch.from_numpy(oracle.bf16_bits_to_f32(d16).reshape(M, N))
+        err_o = _rel_err(d.cpu(), ref_o)
+        assert err_o <= TOL, f"call {call}: rel err against the oracle {err_o:.3e}"
 
 
 def test_no_alloc_refuses_shapes_beyond_its_scratch(nv, cuda_dev):
