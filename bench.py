@@ -47,6 +47,16 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
+def host_threads():
+    """Host cores this process may run on.  Passed explicitly to every oracle call:
+    torch.distributed.run exports OMP_NUM_THREADS=1, which would otherwise pin the
+    OpenMP default (omp_get_max_threads) of every rank to one thread."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return max(1, os.cpu_count() or 1)
+
+
 def committed_traffic():
     """DRAM bytes per GEMM launch from the committed ncu capture summary, if any."""
     path = os.path.join(ROOT, "profiles", "roofline_traffic.json")
@@ -163,12 +173,18 @@ def max_over_ranks(x, world):
 
 
 def in_kernel_clock(nv, operands, d, M, N, K, dev):
-    """SM clock the GEMM itself runs at: one launch of the traced CTA-pair kernel on
-    the bench's operands, clock64 cycles over globaltimer ns of each pair's MMA thread."""
+    """SM clock the GEMM itself runs at: one launch of the traced CTA-pair kernel (the
+    diagnostic library, nvfp4_diag; outside every timed region) on the bench's
+    operands, clock64 cycles over globaltimer ns of each pair's MMA thread."""
+    try:
+        import nvfp4_diag
+        diag = nvfp4_diag.lib()
+    except ImportError:
+        return None
     a, sfa, b, sfb, alpha = operands
     sms = torch.cuda.get_device_properties(dev).multi_processor_count  # one trace row per CTA, grid <= #SMs
     tr = torch.zeros(sms * 12, dtype=torch.int64, device=dev)
-    st = nv.lib().nvfp4_gemm_trace(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), alpha, d.data_ptr(),
+    st = diag.nvfp4_gemm_trace(a.data_ptr(), sfa.data_ptr(), b.data_ptr(), sfb.data_ptr(), alpha, d.data_ptr(),
                                    M, N, K, tr.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
     torch.cuda.synchronize()
     if st != 0:
@@ -207,7 +223,7 @@ class CpuDequantGemm:
     def __init__(self, a, sfa, b, sfb, alpha, M, N, K):
         from oracle import oracle as o
         self.o, self.a, self.sfa, self.alpha, self.M, self.N, self.K = o, a, sfa, alpha, M, N, K
-        self.threads = o.max_threads()
+        self.threads = host_threads()
         t0 = time.perf_counter()
         self.bf = o.dequant_rows(b, sfb, 0, N, K, nthreads=self.threads)
         self.t_b = time.perf_counter() - t0
@@ -250,12 +266,12 @@ def cpu_configs_section():
     charged once), and a 1024 x 2048 x 8192 slice of configs[3]."""
     from oracle import oracle as o
     import numpy as np
-    T = o.max_threads()
+    T = host_threads()
     out = {"cores": T, "kind": "port"}
 
     def quantized(rows, cols, seed, std=1.0):
         x = o.normal_bf16((rows, cols), seed=seed, std=std, nthreads=T)
-        gs = o.global_scale_for(o.amax_bf16(x))
+        gs = o.global_scale_for(o.amax_bf16(x, nthreads=T))
         q, sf = o.quantize(x, gs, nthreads=T)
         return q, sf, gs
 
@@ -264,7 +280,7 @@ def cpu_configs_section():
     xa = o.normal_bf16((M, K), seed=1, nthreads=T)
     xb = o.normal_bf16((N, K), seed=2, nthreads=T)
     t0 = time.perf_counter()
-    ga, gb = o.global_scale_for(o.amax_bf16(xa)), o.global_scale_for(o.amax_bf16(xb))
+    ga, gb = o.global_scale_for(o.amax_bf16(xa, nthreads=T)), o.global_scale_for(o.amax_bf16(xb, nthreads=T))
     a, sfa = o.quantize(xa, ga, nthreads=T)
     b, sfb = o.quantize(xb, gb, nthreads=T)
     o.gemm(a, sfa, b, sfb, float(np.float32(ga) * np.float32(gb)), M, N, K, nthreads=T)
@@ -291,7 +307,7 @@ def cpu_configs_section():
 
     # quantize X + GEMM against a pre-quantized W
     M, N, K = 4096, 14336, 4096
-    x = o.student_t3_bf16(M, K, seed=9, n_outlier_cols=4, gain=50.0)
+    x = o.student_t3_bf16(M, K, seed=9, n_outlier_cols=4, gain=50.0, nthreads=T)
     w, wsf, gw = quantized(N, K, 10, std=0.02)
     t0 = time.perf_counter()
     wf = o.dequant_rows(w, wsf, 0, N, K, nthreads=T)
@@ -336,10 +352,11 @@ def run_reference(args):
     import numpy as np
     M, N, K = M_, N_, K_
     # same workload semantics: N(0,1) bf16 quantized per tensor; operands built on the host
-    threads = o.max_threads()
+    threads = host_threads()
     xa = o.normal_bf16((M, K), seed=1, nthreads=threads)
     xb = o.normal_bf16((N, K), seed=2, nthreads=threads)
-    gsa, gsb = o.global_scale_for(o.amax_bf16(xa)), o.global_scale_for(o.amax_bf16(xb))
+    gsa = o.global_scale_for(o.amax_bf16(xa, nthreads=threads))
+    gsb = o.global_scale_for(o.amax_bf16(xb, nthreads=threads))
     a, sfa = o.quantize(xa, gsa, nthreads=threads)
     b, sfb = o.quantize(xb, gsb, nthreads=threads)
     alpha = float(np.float32(gsa) * np.float32(gsb))
@@ -392,6 +409,108 @@ def vendor_scaled_mm(sets, M, N, K, reps=50):
                 "what": "torch._scaled_mm (cuBLASLt) NVFP4, same operands, bf16 out; comparison only"}
     except Exception as e:  # pragma: no cover - depends on the torch build
         return {"unavailable": f"{type(e).__name__}: {str(e)[:120]}"}
+
+
+def sustained_section(nv, sets, d, M, N, K, dev, seconds=1.5):
+    """The bench GEMM looped back to back for ~`seconds` (after the burst of the
+    timed region), with NVML clock samples over the loop and the in-kernel SM clock of
+    a traced launch right after it: the rate under the 1 kW power cap."""
+    stream = torch.cuda.current_stream(dev)
+    flops = 2.0 * M * N * K
+    n = len(sets)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)  # calibrate the count of launches from 50 calls
+    for i in range(50):
+        a, sfa, b, sfb, alpha = sets[i % n]
+        nv.gemm(a, sfa, b, sfb, alpha, out=d)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    calls = max(100, int(seconds * 1e3 / (e0.elapsed_time(e1) / 50)))
+    with ClockSampler(dev) as clk:
+        e0.record(stream)
+        for i in range(calls):
+            a, sfa, b, sfb, alpha = sets[i % n]
+            nv.gemm(a, sfa, b, sfb, alpha, out=d)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    nv.device_status()
+    ms = e0.elapsed_time(e1) / calls
+    return {"calls": calls, "seconds": calls * ms / 1e3, "ms_per_gemm": ms, "tflops": flops / ms / 1e9,
+            "clocks": clk.summary(), "in_kernel_sm_mhz_after": in_kernel_clock(nv, sets[0], d, M, N, K, dev),
+            "what": "8192^3 GEMM back to back for >= 1 s, operands rotating as in the timed region"}
+
+
+# The reference harness's shape list (matmul/sm100_nvfp4/main.py:117-130): it times and
+# verifies each of these against torch._scaled_mm.
+SWEEP_SHAPES = [(1024, 1024, 1024), (1024, 1024, 2048), (1024, 1024, 4096), (2048, 2048, 2048),
+                (2048, 2048, 4096), (2048, 2048, 8192), (4096, 4096, 4096), (4096, 4096, 8192),
+                (4096, 4096, 16384), (8192, 8192, 8192), (8192, 8192, 4096), (8192, 8192, 16384)]
+
+
+def shape_sweep_section(nv, dev, reps=20, check_rows=16):
+    """Per shape of the reference harness: this library's nvfp4_gemm and
+    torch._scaled_mm (cuBLASLt, the reference's oracle; comparison only) on the same
+    operands, each launch timed alone with CUDA events and L2 flushed between launches
+    (a 256 MB write) — median TFLOP/s; and `check_rows` sampled rows of our output
+    against the CPU oracle (max |D - D_ref| / max |D_ref|, bound 1e-2)."""
+    from oracle import oracle as o
+    import numpy as np
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev)
+    out = []
+    for (M, N, K) in SWEEP_SHAPES:
+        g.manual_seed(M * 3 + N * 5 + K)
+        xa = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+        xb = torch.randn(N, K, device=dev, generator=g).to(torch.bfloat16)
+        _, gsa = nv.global_scale(xa)
+        _, gsb = nv.global_scale(xb)
+        a, sfa = nv.quantize(xa, gsa)
+        b, sfb = nv.quantize(xb, gsb)
+        del xa, xb
+        alpha = float((gsa * gsb).item())
+        d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+
+        def per_launch(fn):
+            fn()
+            fn()
+            ts = []
+            for _ in range(reps):
+                flush.fill_(1)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            return statistics.median(ts)
+
+        ours = per_launch(lambda: nv.gemm(a, sfa, b, sfb, alpha, out=d))
+        row = {"M": M, "N": N, "K": K, "ms": round(ours, 4), "tflops": round(2.0 * M * N * K / ours / 1e9, 1)}
+        try:
+            va = (a.view(torch.float4_e2m1fn_x2), b.view(torch.float4_e2m1fn_x2).t(),
+                  sfa.view(torch.float8_e4m3fn), sfb.view(torch.float8_e4m3fn))
+            vend = per_launch(lambda: torch._scaled_mm(va[0], va[1], va[2], va[3], out_dtype=torch.bfloat16))
+            row["scaled_mm_ms"] = round(vend, 4)
+            row["scaled_mm_tflops"] = round(2.0 * M * N * K / vend / 1e9, 1)
+            row["ratio_vs_scaled_mm"] = round(vend / ours, 3)
+        except Exception as e:  # pragma: no cover - depends on the torch build
+            row["scaled_mm"] = f"unavailable: {type(e).__name__}"
+        nv.gemm(a, sfa, b, sfb, alpha, out=d)
+        torch.cuda.synchronize()
+        nv.device_status()
+        m0 = (M // 2) // 128 * 128 + 7  # rows in a middle tile, off the tile edge
+        d32, d16 = o.gemm(a.cpu().numpy(), sfa.cpu().numpy(), b.cpu().numpy(), sfb.cpu().numpy(), alpha, M, N, K,
+                          m0=m0, mrows=check_rows, nthreads=host_threads())
+        ref = o.bf16_bits_to_f32(d16).reshape(check_rows, N)
+        got = d[m0:m0 + check_rows].float().cpu().numpy()
+        err = float(np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30))
+        row["oracle_rel_err"] = float(f"{err:.3e}")
+        row["oracle_ok"] = bool(np.isfinite(got).all() and err <= 1e-2)
+        out.append(row)
+        del a, sfa, b, sfb, d
+    del flush
+    return {"unit": "TFLOP/s", "timing": f"median of {reps} single launches, L2 flushed before each",
+            "check": f"{check_rows} rows per shape against the CPU oracle", "shapes": out}
 
 
 def decode_section(nv, dev, pk, reps=30):
@@ -767,14 +886,15 @@ def epilogue_section(nv, sets, M, N, K, reps=30):
 
 
 def gather_section(nv, dev, world, rank, reps=10):
-    """BASELINE configs[3] with the full output requested: prefill FFN up-projection
-    M=16384, N=28672, K=8192, B sharded by 128-row blocks across the ranks.  Per call,
-    max over ranks: the shard GEMM alone; GEMM + NCCL all-gather of the bf16 shards
-    (nvfp4_b200.dist.gather_columns); the gather fused into the GEMM epilogue
-    (nvfp4_b200.dist.FusedGather) with NVLink stores to every rank's buffer, and with
-    one NVLink-multicast store per element where the fabric offers it."""
+    """BASELINE configs[3], N-sharded, strong scaling: prefill FFN up-projection
+    M=16384, N=28672, K=8192 (7.7e15 FLOP in all), B sharded by 128-row blocks across
+    the ranks.  Per call, max over ranks: the shard GEMM alone (at one GPU the whole
+    GEMM, the first point of the curve); and with the full output requested on every
+    rank (N > 1): GEMM + NCCL all-gather of the bf16 shards
+    (nvfp4_b200.dist.gather_columns), and the gather fused into the GEMM epilogue
+    (nvfp4_b200.dist.FusedGather, NVLink stores to every rank's buffer)."""
     import torch.distributed as dist
-    from nvfp4_b200.dist import FusedGather, gather_columns, shard_bounds, shard_weight
+    from nvfp4_b200.dist import FusedGather, gather_columns, shard_bounds
     M, N, K = 16384, 28672, 8192
     g = torch.Generator(device=dev).manual_seed(91)
     x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
@@ -792,7 +912,7 @@ def gather_section(nv, dev, world, rank, reps=10):
         for _ in range(2):
             fn()
         torch.cuda.synchronize()
-        dist.barrier()
+        barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(reps):
@@ -802,38 +922,33 @@ def gather_section(nv, dev, world, rank, reps=10):
         return max_over_ranks(e0.elapsed_time(e1) / reps, world)
 
     d = torch.empty(M, n1 - n0, dtype=torch.bfloat16, device=dev)
-    res = {"what": "prefill FFN M=16384 N=28672 K=8192, N-sharded, full bf16 D on every rank",
-           "full_output_bytes": M * N * 2, "n_gpus": world}
+    res = {"what": "prefill FFN M=16384 N=28672 K=8192, N-sharded across the GPUs (strong scaling); with the "
+                   "full output, bf16 D [16384, 28672] on every rank",
+           "full_output_bytes": M * N * 2, "n_gpus": world, "shard_columns": n1 - n0}
     res["shard_gemm_ms"] = timed(lambda: nv.gemm(a, sfa, bs, ss, alpha, out=d))
-    res["gemm_plus_nccl_all_gather_ms"] = timed(lambda: gather_columns(nv.gemm(a, sfa, bs, ss, alpha, out=d), N))
-    fg = FusedGather(M, N, dev, multicast=False)
-    res["fused_nvlink_stores_ms"] = timed(lambda: fg.gemm(a, sfa, bs, ss, alpha, n0))
-    del fg
-    try:
-        fm = FusedGather(M, N, dev, multicast=True)
-    except RuntimeError:
-        fm = None
-    ok = [fm is not None]
-    oks = [None] * world
-    dist.all_gather_object(oks, ok[0])
-    if all(oks):
-        res["fused_nvlink_multicast_ms"] = timed(lambda: fm.gemm(a, sfa, bs, ss, alpha, n0))
-    else:
-        res["fused_nvlink_multicast_ms"] = None
-    del fm
+    if world > 1:
+        res["gemm_plus_nccl_all_gather_ms"] = timed(
+            lambda: gather_columns(nv.gemm(a, sfa, bs, ss, alpha, out=d), N))
+        fg = FusedGather(M, N, dev, multicast=False)
+        res["fused_nvlink_stores_ms"] = timed(lambda: fg.gemm(a, sfa, bs, ss, alpha, n0))
+        del fg
+        dist.barrier()
     nv.device_status()
     flops = 2.0 * M * N * K
     for k in [k for k in res if k.endswith("_ms") and res[k]]:
         res[k.replace("_ms", "_tflops")] = flops / (res[k] / 1e3) / 1e12
-    # Roofline of the fused form: the slower of this rank's shard GEMM and the NVLink
-    # bytes every rank must receive ((P-1)/P of the output) at the measured 770 GB/s
-    # per direction of a peer copy on this pool.
+    # Roofline of the full-output forms: the slower of this rank's shard GEMM and the
+    # NVLink bytes every rank must receive ((P-1)/P of the output) at the measured
+    # 770 GB/s per direction of a peer copy on this pool.
     in_bytes = M * N * 2 * (world - 1) / world
     link_ms = in_bytes / 770e9 * 1e3
     bound_ms = max(link_ms, res["shard_gemm_ms"])
     res["roofline"] = {"bound": "nvlink" if link_ms >= res["shard_gemm_ms"] else "tensor",
-                       "nvlink_in_bytes_per_rank": in_bytes, "nvlink_gbs_basis": 770.0, "bound_ms": bound_ms,
-                       "frac_fused_stores": bound_ms / res["fused_nvlink_stores_ms"]}
+                       "limiter": ("incoming NVLink bytes of the gather" if link_ms >= res["shard_gemm_ms"]
+                                   else "the shard GEMM (tensor pipe)"),
+                       "nvlink_in_bytes_per_rank": in_bytes, "nvlink_gbs_basis": 770.0, "bound_ms": bound_ms}
+    if world > 1:
+        res["roofline"]["frac_fused_stores"] = bound_ms / res["fused_nvlink_stores_ms"]
     return res
 
 
@@ -986,6 +1101,9 @@ def run_ours(args):
         e2e_value = flops * world / (e2e_ms / 1e3) / 1e12
         barrier(world)
 
+    sustained = None
+    if not args.no_sustained:
+        sustained = sustained_section(nv, sets, d, M, N, K, dev)
     pk = peaks()
     fp4_peak_est = 4.0 * pk["bf16_tflops"]
     traffic = committed_traffic().get("gemm_8192", {}).get("dram_bytes_per_launch")
@@ -997,7 +1115,8 @@ def run_ours(args):
         quant = quantize_section(nv, dev, pk)
         moe = moe_section(nv, dev)
         epi = epilogue_section(nv, sets, M, N, K)
-    gath = gather_section(nv, dev, world, rank) if (world > 1 and not args.no_gather) else None
+    gath = gather_section(nv, dev, world, rank) if not args.no_gather else None
+    sweep = shape_sweep_section(nv, dev) if (rank == 0 and not args.no_sweep) else None
     cpu_cfg = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu, _, _ = cpu_reference_sample(a, sfa, b, sfb, alpha, M, N, K, target_s=args.cpu_seconds)
@@ -1045,6 +1164,10 @@ def run_ours(args):
             line["fused_epilogue"] = epi
         if gath is not None:
             line["gather"] = gath
+        if sustained is not None:
+            line["sustained"] = sustained
+        if sweep is not None:
+            line["shape_sweep"] = sweep
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
@@ -1062,7 +1185,9 @@ def main():
     ap.add_argument("--sets", type=int, default=0, help="operand sets to rotate (default: > 3x L2)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-shape GB/s section")
-    ap.add_argument("--no-gather", action="store_true", help="skip the N>1 all-gather section")
+    ap.add_argument("--no-gather", action="store_true", help="skip the configs[3] N-sharded section")
+    ap.add_argument("--no-sustained", action="store_true", help="skip the >= 1 s sustained GEMM loop")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the reference harness's shape sweep")
     ap.add_argument("--workload", default="square",
                     help="square (default, the bench line), decode:M:N:K or quantize:M:K (one kernel, for "
                          "profiling), moe (the mixture-of-experts section alone)")

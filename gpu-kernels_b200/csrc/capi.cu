@@ -15,9 +15,6 @@ namespace nvfp4 {
 int gemm_dispatch_epi(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                       int M, int N, int K, cudaStream_t stream, bool f16, const Epi &epi);
 int sf_pad_zero(uint8_t *SF, int M, int K, cudaStream_t s, const DeviceInfo &di);
-int decode_trace_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
-                          uint16_t *D, int M, int N, int K, void *ws, size_t ws_bytes, unsigned long long *trace,
-                          cudaStream_t stream);
 int gather_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, int M,
                     int N, int K, const uint64_t *dst, int n_dst, int multicast, int64_t ld, int col_off,
                     cudaStream_t stream);
@@ -37,12 +34,11 @@ int quantize_dynamic_dispatch(const uint16_t *X, uint8_t *Q, uint8_t *SF, float 
 int gemm_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                   int M, int N, int K, cudaStream_t stream, bool f16);
 size_t decode_workspace_bytes(int M, int N);
+bool decode_tiles_fit(int N, int groups);
 int decode_noalloc_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
                             uint16_t *D, int M, int N, int K, cudaStream_t stream);
 int gemm_host(const uint8_t *hA, const uint8_t *hSFA, const uint8_t *hB, const uint8_t *hSFB, float alpha,
               uint16_t *hD, int M, int N, int K, cudaStream_t stream);
-int gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D, int M,
-               int N, int K, unsigned long long *trace, cudaStream_t stream, const Epi &epi);
 int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, const void *D, int M,
                   int N, int K);
 int decode_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
@@ -67,22 +63,31 @@ static int decode_max_m() {
 
 // nvfp4_gemm's own decode workspace: one zero-initialised buffer per (device,
 // stream), grown on demand and kept for the life of the process.  Calls on the
-// same stream are ordered, so they may share it.
+// same stream are ordered, so they may share it.  Kernels leave its counters at
+// zero, except one that timed out: after nvfp4_device_status has reported a timeout
+// on the device the buffer is cleared again before its next use.
 // kind separates users whose workspace contents must not meet (0: decode split-K
 // counters and partials, 1: the dynamic quantizer's barrier and amax partials).
+struct Workspace {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+    uint64_t epoch = 0;  // timeout_epoch() when it was last cleared
+};
+
 static int internal_workspace(size_t need, cudaStream_t stream, void **ws, size_t *bytes, int kind = 0) {
     static std::mutex mu;
-    static std::map<std::tuple<int, cudaStream_t, int>, std::pair<void *, size_t>> cache;
+    static std::map<std::tuple<int, cudaStream_t, int>, Workspace> cache;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return NVFP4_ERR_CUDA;
     if (!need) return NVFP4_ERR_CUDA;
     std::lock_guard<std::mutex> lock(mu);
-    auto &slot = cache[{dev, stream, kind}];
-    if (slot.second < need) {
-        if (slot.first) {
+    Workspace &slot = cache[{dev, stream, kind}];
+    const uint64_t epoch = timeout_epoch(dev);
+    if (slot.bytes < need) {
+        if (slot.ptr) {
             cudaStreamSynchronize(stream);
-            cudaFree(slot.first);
-            slot = {nullptr, 0};
+            cudaFree(slot.ptr);
+            slot = Workspace();
         }
         void *p = nullptr;
         if (cudaMalloc(&p, need) != cudaSuccess) return NVFP4_ERR_CUDA;
@@ -90,10 +95,15 @@ static int internal_workspace(size_t need, cudaStream_t stream, void **ws, size_
             cudaFree(p);
             return NVFP4_ERR_CUDA;
         }
-        slot = {p, need};
+        slot.ptr = p;
+        slot.bytes = need;
+        slot.epoch = epoch;
+    } else if (slot.epoch != epoch) {  // a timeout since the last clear: counters may be left set
+        if (cudaMemsetAsync(slot.ptr, 0, slot.bytes, stream) != cudaSuccess) return NVFP4_ERR_CUDA;
+        slot.epoch = epoch;
     }
-    *ws = slot.first;
-    *bytes = slot.second;
+    *ws = slot.ptr;
+    *bytes = slot.bytes;
     return NVFP4_OK;
 }
 
@@ -104,7 +114,7 @@ int nvfp4_gemm(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uin
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
     if (st) return st;
-    if (M <= decode_max_m()) {
+    if (M <= decode_max_m() && decode_tiles_fit(N, 1)) {
         void *ws = nullptr;
         size_t bytes = 0;
         st = internal_workspace(decode_workspace_bytes(M, N), s, &ws, &bytes);
@@ -120,7 +130,7 @@ int nvfp4_gemm(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uin
 static int epi_out_cols(const Epi &e, int N) { return e.act == NVFP4_ACT_SWIGLU ? N / 2 : N; }
 
 // The C epilogue description as the kernels' Epi, with its argument checks.
-static int epilogue_from(const nvfp4_epilogue *epi, int N, Epi *out) {
+int epilogue_from(const nvfp4_epilogue *epi, int N, Epi *out) {
     Epi e;
     e.bias = epi->bias;
     e.act = epi->activation;
@@ -152,7 +162,7 @@ int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, 
     if (st) return st;
     st = gemm_validate(A, SFA, B, SFB, e.q ? static_cast<const void *>(e.q) : D, M, N, K);
     if (st) return st;
-    if (M <= decode_max_m()) {
+    if (M <= decode_max_m() && decode_tiles_fit(N, 1)) {
         void *ws = nullptr;
         size_t bytes = 0;
         if ((st = internal_workspace(decode_workspace_bytes(M, N), s, &ws, &bytes))) return st;
@@ -174,7 +184,8 @@ int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, 
 static int gemm_grouped_epi(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
                             const float *alpha, uint16_t *D, const int32_t *m_offsets, int groups, int m_total, int N,
                             int K, cudaStream_t s, const Epi &e) {
-    if (m_total >= 1 && m_total <= decode_max_m() && groups >= 1 && groups <= 256 && N >= 128 && N % 128 == 0) {
+    if (m_total >= 1 && m_total <= decode_max_m() && groups >= 1 && groups <= 256 && N >= 128 && N % 128 == 0 &&
+        decode_tiles_fit(N, groups)) {
         void *ws = nullptr;
         size_t bytes = 0;
         int st = internal_workspace(decode_grouped_workspace_bytes(m_total, N, groups), s, &ws, &bytes);
@@ -231,7 +242,7 @@ int nvfp4_gemm_persistent(const uint8_t *A, const uint8_t *SFA, const uint8_t *B
 }
 
 size_t nvfp4_gemm_decode_workspace_size(int M, int N) {
-    if (M < 1 || M > 128 || N < 1) return 0;
+    if (M < 1 || M > 128 || N < 1 || !decode_tiles_fit(N, 1)) return 0;
     return decode_workspace_bytes(M, N);
 }
 
@@ -263,31 +274,6 @@ int nvfp4_gemm_decode_noalloc(const uint8_t *A, const uint8_t *SFA, const uint8_
 int nvfp4_gemm_host(const uint8_t *hA, const uint8_t *hSFA, const uint8_t *hB, const uint8_t *hSFB, float alpha,
                     uint16_t *hD, int M, int N, int K, void *stream) {
     return gemm_host(hA, hSFA, hB, hSFB, alpha, hD, M, N, K, static_cast<cudaStream_t>(stream));
-}
-
-int nvfp4_gemm_decode_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
-                            uint16_t *D, int M, int N, int K, void *workspace, size_t workspace_bytes, uint64_t *trace,
-                            void *stream) {
-    return decode_trace_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, workspace, workspace_bytes,
-                                 reinterpret_cast<unsigned long long *>(trace), static_cast<cudaStream_t>(stream));
-}
-
-int nvfp4_gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha,
-                     uint16_t *D, int M, int N, int K, uint64_t *trace, void *stream) {
-    return gemm_trace(A, SFA, B, SFB, alpha, D, M, N, K, reinterpret_cast<unsigned long long *>(trace),
-                      static_cast<cudaStream_t>(stream), Epi());
-}
-
-int nvfp4_gemm_trace_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
-                              float alpha, uint16_t *D, int M, int N, int K, const nvfp4_epilogue *epi,
-                              uint64_t *trace, void *stream) {
-    Epi e;
-    if (epi) {
-        int st = epilogue_from(epi, N, &e);
-        if (st) return st;
-    }
-    return gemm_trace(A, SFA, B, SFB, alpha, e.q ? static_cast<void *>(e.q) : D, M, N, K,
-                      reinterpret_cast<unsigned long long *>(trace), static_cast<cudaStream_t>(stream), e);
 }
 
 }  // extern "C"

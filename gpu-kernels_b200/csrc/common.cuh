@@ -21,9 +21,21 @@ struct KernelCtl {
     uint32_t *status;          // device address of the status word
 };
 
+// Number of device-side timeouts nvfp4_device_status has reported on device `dev`.
+// A kernel that gave up a wait may leave split-K arrival counters or grid-barrier
+// counters non-zero, so a library-owned workspace remembers the count it was last
+// cleared at and clears itself again once the count has moved.
+uint64_t timeout_epoch(int dev);
+
 // Current limits (nvfp4_set_wait_timeout_ns) and the current device's status word.
 int kernel_ctl(KernelCtl *out);
 void count_launch();          // bump nvfp4_launch_count()
+
+// Signal pads of the ranks of one node, as this process addresses them.
+constexpr int kMaxRanks = 8;
+struct RankPads {
+    uint64_t ptr[kMaxRanks];
+};
 
 // Per-device facts cached on first use.
 struct DeviceInfo {

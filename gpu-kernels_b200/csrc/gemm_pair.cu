@@ -694,8 +694,14 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     if (F16 && !epi.plain()) return NVFP4_ERR_UNSUPPORTED;     // the fused epilogue writes bf16 / NVFP4
     if (epi.act == kActSwiglu && BN % 256 != 0) return NVFP4_ERR_UNSUPPORTED;  // 128-column halves
     using L = PairLayout<STAGES, BKB, BN>;
+#ifdef NVFP4_DIAG
+    // the per-CTA cycle trace exists only in the diagnostic library (nvfp4_diag)
     auto kern = trace ? nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, true>
                       : nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, false>;
+#else
+    if (trace) return NVFP4_ERR_UNSUPPORTED;
+    auto kern = nvfp4_gemm_pair_kernel<STAGES, BKB, BN, F16, false>;
+#endif
     static int configured[2][64] = {};
     if (!configured[trace != nullptr][di.device]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynamicSmem) != cudaSuccess)
@@ -864,7 +870,9 @@ int gather_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, cons
                                                  stream, di, nullptr, Epi(), gemm::Grouped(), g);
 }
 
-// Pair kernel with the per-CTA cycle trace on (trace: 148 x kTraceSlots u64 on the device).
+#ifdef NVFP4_DIAG
+// Pair kernel with the per-CTA cycle trace on (trace: 148 x kTraceSlots u64 on the
+// device); diagnostic library only.
 int gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D, int M,
                int N, int K, unsigned long long *trace, cudaStream_t stream, const Epi &epi) {
     int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
@@ -874,5 +882,6 @@ int gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uin
     if ((st = device_info(&di))) return st;
     return gemm::launch_pair_cfg<false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, trace, epi);
 }
+#endif
 
 }  // namespace nvfp4

@@ -304,21 +304,6 @@ __global__ void global_scale_kernel(const uint32_t *amax_bits, float *amax_out, 
     if (gs_out) *gs_out = __fdiv_rn(a, 2688.0f);  // amax / (6 * 448)
 }
 
-// Scale codes of blocks with the given bf16 amax values, taken the way the fused GEMM
-// epilogue takes them: per-CTA threshold tables of the global scale, no division.
-__global__ void __launch_bounds__(256) scale_codes_kernel(const uint16_t *__restrict__ amax, int64_t n,
-                                                          const float *__restrict__ gs_ptr,
-                                                          uint8_t *__restrict__ codes) {
-    __shared__ ScaleTables tab;
-    const float gs = *gs_ptr;
-    build_scale_tables(&tab, gs, threadIdx.x, blockDim.x);
-    __syncthreads();
-    const ScaleGuess guess = scale_guess_factor(gs);
-    const bool ok = gs_usable(gs);
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        codes[i] = (uint8_t)table_scale_code(fabsf(__uint_as_float((uint32_t)amax[i] << 16)), guess, &tab, ok);
-}
-
 int sf_pad_zero(uint8_t *SF, int M, int K, cudaStream_t s, const DeviceInfo &di);
 
 // Workspace of quantize_dynamic_dispatch: the barrier's two counters (zero between
@@ -421,22 +406,6 @@ extern "C" int nvfp4_quantize(const uint16_t *X, uint8_t *Q, uint8_t *SF, const 
     count_launch();
     if ((st = cuda_status(cudaGetLastError()))) return st;
     return sf_pad_zero(SF, M, K, s, di);
-}
-
-extern "C" int nvfp4_scale_codes(const uint16_t *amax_bf16, int64_t n, const float *global_scale, uint8_t *codes,
-                                 void *stream) {
-    if (!amax_bf16 || !global_scale || !codes) return NVFP4_ERR_INVALID;
-    if (n < 1) return NVFP4_ERR_SHAPE;
-    if ((reinterpret_cast<uintptr_t>(amax_bf16) & 1u) || (reinterpret_cast<uintptr_t>(global_scale) & 3u))
-        return NVFP4_ERR_ALIGN;
-    DeviceInfo di;
-    int st = device_info(&di);
-    if (st) return st;
-    const int64_t blocks = std::min<int64_t>((n + 255) / 256, di.sm_count);
-    scale_codes_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(amax_bf16, n, global_scale,
-                                                                                          codes);
-    count_launch();
-    return cuda_status(cudaGetLastError());
 }
 
 extern "C" int nvfp4_quantize_grouped(const uint16_t *X, uint8_t *Q, uint8_t *SF, const float *global_scale,

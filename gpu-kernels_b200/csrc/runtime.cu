@@ -14,6 +14,11 @@ __device__ uint32_t g_device_status = 0;
 
 static std::atomic<uint64_t> g_wait_timeout_ns{2000000000ull};
 static std::atomic<uint64_t> g_launches{0};
+static std::atomic<uint64_t> g_timeout_epoch[64];
+
+uint64_t timeout_epoch(int dev) {
+    return dev >= 0 && dev < 64 ? g_timeout_epoch[dev].load(std::memory_order_acquire) : 0;
+}
 
 static uint32_t *status_word_address() {
     static std::mutex mu;
@@ -112,6 +117,35 @@ __global__ void wait_selftest_kernel(uint64_t timeout_ns, uint32_t *status) {
     __syncthreads();
 }
 
+// Cross-rank barrier over signal slots in memory every rank has mapped (symmetric
+// memory signal pads).  Thread t (t != rank) adds 1 to slot [channel][rank] of rank
+// t's pad with release semantics, then waits — bounded — until slot [channel][t] of
+// its own pad is non-zero, and takes 1 from it.  Counting, not a 0/1 flag, so a fast
+// rank may signal the next barrier of a channel before a slow one has consumed the
+// last.  A wait that gives up latches the timeout bit and returns; the slots are then
+// out of step and the pads must not be used by this barrier again.
+__global__ void rank_barrier_kernel(RankPads pads, int n, int rank, int slot0, uint64_t timeout_ns,
+                                    uint32_t *status) {
+    const int t = threadIdx.x;
+    if (t >= n || t == rank) return;
+    unsigned int *remote = reinterpret_cast<unsigned int *>(pads.ptr[t]) + slot0 + rank;
+    unsigned int *local = reinterpret_cast<unsigned int *>(pads.ptr[rank]) + slot0 + t;
+    __threadfence_system();
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(remote) : "memory");
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        unsigned int v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(local) : "memory");
+        if (v) break;
+        if (global_timer_ns() - t0 > timeout_ns) {
+            atomicOr(status, kDevTimeout);
+            return;
+        }
+        __nanosleep(64);
+    }
+    atomicSub(local, 1u);
+}
+
 }  // namespace nvfp4
 
 using namespace nvfp4;
@@ -144,7 +178,37 @@ int nvfp4_device_status(void *stream) {
     uint32_t v = 0, zero = 0;
     if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v)) != cudaSuccess) return NVFP4_ERR_CUDA;
     if (v && cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero)) != cudaSuccess) return NVFP4_ERR_CUDA;
-    return (v & kDevTimeout) ? NVFP4_ERR_TIMEOUT : NVFP4_OK;
+    if (v & kDevTimeout) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < 64)
+            g_timeout_epoch[dev].fetch_add(1, std::memory_order_acq_rel);
+        return NVFP4_ERR_TIMEOUT;
+    }
+    return NVFP4_OK;
+}
+
+int nvfp4_rank_barrier(const uint64_t *signal_pads, int n_ranks, int rank, int channel, size_t pad_bytes,
+                       void *stream) {
+    if (!signal_pads || n_ranks < 1 || n_ranks > kMaxRanks || rank < 0 || rank >= n_ranks || channel < 0)
+        return NVFP4_ERR_INVALID;
+    // this barrier's slots: the upper half of each pad, n_ranks words per channel
+    const size_t words = pad_bytes / 4, slot0 = words / 2 + static_cast<size_t>(channel) * n_ranks;
+    if (slot0 + n_ranks > words) return NVFP4_ERR_INVALID;
+    RankPads pads;
+    for (int r = 0; r < n_ranks; ++r) {
+        if (!signal_pads[r] || (signal_pads[r] & 3u)) return NVFP4_ERR_ALIGN;
+        pads.ptr[r] = signal_pads[r];
+    }
+    DeviceInfo di;
+    int st = device_info(&di);
+    if (st) return st;
+    if (n_ranks == 1) return NVFP4_OK;
+    KernelCtl ctl;
+    if ((st = kernel_ctl(&ctl))) return st;
+    rank_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(pads, n_ranks, rank, static_cast<int>(slot0),
+                                                                        ctl.wait_timeout_ns, ctl.status);
+    count_launch();
+    return cuda_status(cudaGetLastError());
 }
 
 int nvfp4_selftest_wait_timeout(uint64_t timeout_ns) {

@@ -44,11 +44,7 @@ SIGNATURES = {
     "nvfp4_set_wait_timeout_ns": (None, [C.c_uint64]),
     "nvfp4_selftest_wait_timeout": (C.c_int, [C.c_uint64]),
     "nvfp4_launch_count": (C.c_uint64, []),
-    "nvfp4_gemm_trace": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp, _vp]),
     "nvfp4_quantize_dynamic": (C.c_int, [_u16p, _u8p, _u8p, _f32p, _f32p, C.c_int, C.c_int, _vp]),
-    "nvfp4_scale_codes": (C.c_int, [_u16p, C.c_int64, _vp, _u8p, _vp]),
-    "nvfp4_gemm_trace_epilogue": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int,
-                                            C.POINTER(Epilogue), _vp, _vp]),
     "nvfp4_gemm_grouped": (C.c_int, [_u8p, _u8p, _u8p, _u8p, _f32p, _u16p, _vp, C.c_int, C.c_int, C.c_int, C.c_int,
                                      _vp]),
     "nvfp4_gemm_grouped_epilogue": (C.c_int, [_u8p, _u8p, _u8p, _u8p, _f32p, _u16p, _vp, C.c_int, C.c_int,
@@ -56,12 +52,10 @@ SIGNATURES = {
     "nvfp4_quantize_grouped": (C.c_int, [_u16p, _u8p, _u8p, _f32p, _vp, C.c_int, C.c_int, C.c_int, _vp]),
     "nvfp4_gemm_gather": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, C.c_int, C.c_int, C.c_int,
                                     C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_int64, C.c_int, _vp]),
+    "nvfp4_rank_barrier": (C.c_int, [C.POINTER(C.c_uint64), C.c_int, C.c_int, C.c_int, C.c_size_t, _vp]),
     "nvfp4_gemm_host": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int, _vp]),
     "nvfp4_gemm_decode_noalloc": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int,
                                             _vp]),
-    "nvfp4_gemm_decode_trace": (C.c_int, [_u8p, _u8p, _u8p, _u8p, C.c_float, _u16p, C.c_int, C.c_int, C.c_int,
-                                          _vp, C.c_size_t, _vp, _vp]),
-    "nvfp4_probe_mma_rate": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
 }
 
 STATUS = {

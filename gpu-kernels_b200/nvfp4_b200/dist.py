@@ -91,10 +91,15 @@ class FusedGather:
     nvfp4_gemm_gather, whose epilogue stores each output tile straight into every
     rank's full output — with one multimem store to the buffer's NVLink multicast
     address when the fabric offers one (the switch replicates it, so each GPU sends
-    its shard once), else with one NVLink store per rank — then a device-side barrier
-    across the ranks orders those stores before anyone reads the result.  Unlike
-    gather_columns, no separate collective moves the shards and no per-shard copy
-    follows.  Shard widths and column offsets must be multiples of 16.
+    its shard once), else with one NVLink store per rank.  Two device-side barriers
+    across the ranks (nvfp4_rank_barrier over the symmetric memory's signal pads, every
+    wait bounded) bracket the GEMM: the first keeps a rank from writing into a peer's
+    output before that peer's stream has reached this call (it may still be reading the
+    previous result), the second orders all stores before anyone reads.  A barrier that
+    times out latches NVFP4_ERR_TIMEOUT (nvfp4_device_status raises) and leaves the
+    object unusable.  Unlike gather_columns, no separate collective moves the shards
+    and no per-shard copy follows.  Shard widths and column offsets must be multiples
+    of 16.
 
     Collective: every rank constructs it with the same (M, N) and calls `gemm` in the
     same order.
@@ -127,6 +132,16 @@ class FusedGather:
             raise RuntimeError("no NVLink multicast address for this buffer (NVLS unavailable)")
         self.multicast = bool(mc)
         self.dst = [mc + off] if mc else [p + off for p in ptrs]
+        self.rank, self.world = rank, dist.get_world_size(self.group)
+        self.pads = list(self.handle.signal_pad_ptrs)
+        self.pad_bytes = int(self.handle.signal_pad_size)
+
+    def _barrier(self, channel: int, stream: int) -> None:
+        import ctypes as C
+        from ._lib import check, lib
+        arr = (C.c_uint64 * len(self.pads))(*self.pads)
+        check(lib().nvfp4_rank_barrier(arr, self.world, self.rank, channel, self.pad_bytes, stream),
+              "nvfp4_rank_barrier")
 
     def gemm(self, a: torch.Tensor, sfa: torch.Tensor, b_shard: torch.Tensor, sfb_shard: torch.Tensor,
              alpha: float, col_off: int) -> torch.Tensor:
@@ -139,9 +154,10 @@ class FusedGather:
             raise ValueError("shard does not fit the gathered output")
         arr = (C.c_uint64 * len(self.dst))(*self.dst)
         stream = torch.cuda.current_stream(a.device).cuda_stream
+        self._barrier(0, stream)
         if n > 0:
             check(lib().nvfp4_gemm_gather(a.data_ptr(), sfa.data_ptr(), b_shard.data_ptr(), sfb_shard.data_ptr(),
                                           float(alpha), M, n, K, arr, len(self.dst), int(self.multicast), self.N,
                                           col_off, stream), "nvfp4_gemm_gather")
-        self.handle.barrier(channel=0)
+        self._barrier(1, stream)
         return self.out

@@ -1,11 +1,12 @@
 """Diagnostics for the NVFP4 kernels on a B200.
 
-    python -m nvfp4_b200.diag probe [iters]        measured mxf4nvf4 tensor rate per issue mode
-    python -m nvfp4_b200.diag trace M N K [reps] [epi]  per-CTA cycle breakdown of the CTA-pair GEMM (last
-                                                   of reps); epi: one of EPILOGUES (fused epilogue)
-    python -m nvfp4_b200.diag decode M N K          timeline of back-to-back decode GEMMs (graph replay)
+    python -m nvfp4_diag probe [iters]        measured mxf4nvf4 tensor rate per issue mode
+    python -m nvfp4_diag trace M N K [reps] [epi]  per-CTA cycle breakdown of the CTA-pair GEMM (last
+                                              of reps); epi: one of EPILOGUES (fused epilogue)
+    python -m nvfp4_diag decode M N K          timeline of back-to-back decode GEMMs (graph replay)
 
-(run with gpu-kernels_b200/ on sys.path).  Each prints JSON lines.
+(run with gpu-kernels_b200/ on sys.path).  Each prints JSON lines.  Everything here
+runs the diagnostic library (libnvfp4_diag.so), never the product one.
 """
 import ctypes as C
 import json
@@ -14,7 +15,7 @@ import sys
 
 import torch
 
-from ._lib import check, lib
+from nvfp4_diag import check, lib
 
 PROBE_MODES = {0: "single-CTA MMA only", 1: "single-CTA MMA + 3 scale copies each",
                2: "CTA-pair MMA only", 3: "CTA-pair MMA + 3 scale copies each",
@@ -47,10 +48,10 @@ def trace(M: int, N: int, K: int, reps: int = 3, epi: str = "none"):
     """Per-CTA cycle breakdown of the CTA-pair kernel (the last of `reps` launches),
     plus the kernel's event time and where the time outside the MMA span goes; with
     `epi`, the same launch with that fused epilogue."""
-    from ._lib import ACTIVATIONS, Epilogue
-    from ._lib import lib as _l
-    from .layout import sf_bytes
-    from .ops import create_tensors
+    from nvfp4_b200._lib import ACTIVATIONS, Epilogue
+    from nvfp4_b200.layout import sf_bytes
+    from nvfp4_b200.ops import create_tensors
+    _l = lib
     slots = 12
     dev = torch.device("cuda", 0)
     a, b, sfa, sfb = create_tensors(M, N, K, seed=1)
@@ -110,8 +111,8 @@ def decode_trace(M: int, N: int, K: int, calls: int = 8, sets: int = 3):
     per-CTA %globaltimer stamps.  Per call, in us: gap from the previous call's last
     CTA exit to this call's wait release, first data after release, streaming span,
     tail (last data to last exit), and the call's period."""
-    from ._lib import lib as _l
-    from .ops import create_tensors
+    from nvfp4_b200.ops import create_tensors
+    _l = lib
     dev = torch.device("cuda", 0)
     ops = [create_tensors(M, N, K, seed=10 + i) for i in range(sets)]
     d = torch.empty(M, N, dtype=torch.bfloat16, device=dev)

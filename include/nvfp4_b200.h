@@ -120,9 +120,13 @@ NVFP4_API int nvfp4_gemm_persistent(const uint8_t *A, const uint8_t *SFA, const 
  * Skinny-M (1 <= M <= 128) split-K / stream-K GEMM, bf16 out, bound by HBM bandwidth.
  * Replaces nothing that runs in the reference: its launchers produce zero tiles
  * for M < 128 (matmul/sm100_nvfp4/nvfp4_v5.cu:163-176, 287-309).
- * `workspace` (256-byte aligned, >= nvfp4_gemm_decode_workspace_size(M, N) bytes)
- * must be zero-filled before its first use; every call leaves it zeroed again.
+ * `workspace` (256-byte aligned, >= nvfp4_gemm_decode_workspace_size(M, N) bytes: a
+ * fixed 256 KB region of arrival counters, then the fp32 partial tiles) must be
+ * zero-filled before its first use; every call that completes leaves its counters
+ * at zero again, so one buffer serves calls of any shape.  After
+ * nvfp4_device_status has reported NVFP4_ERR_TIMEOUT, zero it again before reuse.
  * Calls that share a workspace must be ordered (same stream); overlapping calls race.
+ * At most 65536 weight tiles (N <= 8388608); workspace_size returns 0 beyond that.
  */
 NVFP4_API size_t nvfp4_gemm_decode_workspace_size(int M, int N);
 NVFP4_API int nvfp4_gemm_decode(const uint8_t *A, const uint8_t *SFA, const uint8_t *B,
@@ -229,6 +233,22 @@ NVFP4_API int nvfp4_gemm_gather(const uint8_t *A, const uint8_t *SFA, const uint
                                 int64_t ld, int col_off, void *stream);
 
 /*
+ * Cross-rank barrier on `stream` for the ranks of one node (no counterpart in the
+ * reference, which has no multi-GPU path).  signal_pads holds n_ranks (<= 8) device
+ * addresses, as this process sees them, of each rank's zero-initialised signal pad of
+ * pad_bytes bytes — e.g. the signal pads of torch symmetric memory, whose lower half
+ * this barrier leaves alone.  Each rank signals every other rank's pad slot for
+ * `channel` with a system-scope release, then waits until every other rank has
+ * signalled its own; work queued on the stream before the barrier on any rank
+ * (NVLink stores included) is then visible to work queued after it on every rank.
+ * Every wait is bounded by the nvfp4_set_wait_timeout_ns limit: one that gives up
+ * latches NVFP4_ERR_TIMEOUT (nvfp4_device_status), and the pads must not be used by
+ * this barrier again.  n_ranks == 1 returns at once.
+ */
+NVFP4_API int nvfp4_rank_barrier(const uint64_t *signal_pads, int n_ranks, int rank, int channel, size_t pad_bytes,
+                                 void *stream);
+
+/*
  * Reference-signature shim: drop-in for matmul_nvfp4_vN in
  * matmul/sm100_nvfp4/runner.cu:61-96 (fp16 D, alpha = 1, legacy default
  * stream, no return value).  The status of the last call is kept for
@@ -285,55 +305,15 @@ NVFP4_API int nvfp4_gemm_host(const uint8_t *hA, const uint8_t *hSFA, const uint
  * SFA, B, SFB and D.  Shapes whose
  * scratch need (nvfp4_gemm_decode_workspace_size) exceeds it are refused with
  * NVFP4_ERR_WORKSPACE — on a 148-SM B200 that admits M <= 16.  The first call on a
- * device looks up the array's device address (cudaGetSymbolAddress), so make that
- * first call before any stream capture.  All calls on a device share the one array:
- * calls whose kernels overlap on the GPU (different streams, no ordering) race.
+ * device looks up the array's device address (cudaGetSymbolAddress) and clears its
+ * arrival counters (a memset on `stream`), so make that first call before any
+ * stream capture; later calls clear them again only after nvfp4_device_status has
+ * reported a device-side timeout (which can leave counters set) — make that call,
+ * too, outside capture.  All calls on a device share the one array: calls whose
+ * kernels overlap on the GPU (different streams, no ordering) race.
  */
 NVFP4_API int nvfp4_gemm_decode_noalloc(const uint8_t *A, const uint8_t *SFA, const uint8_t *B,
                const uint8_t *SFB, float alpha, uint16_t *D, int M, int N, int K, void *stream);
-
-/*
- * Diagnostics (no counterpart in the reference, which only has a host timer and
- * an unused per-SM event recorder, matmul/sm100_nvfp4/profiler.cuh:4-72).
- *
- * nvfp4_gemm_trace: the CTA-pair GEMM with a per-CTA cycle trace written to
- * `trace` (device, #SMs x 12 uint64; the grid is at most one CTA per SM): [0] MMA
- * wait on full stages, [1] MMA wait on
- * a free accumulator, [2] producer wait on empty stages, [3] epilogue wait on a
- * full accumulator, [4] epilogue drain + stores, [5] tiles, [6] MMA-thread span
- * in cycles, [7] the same in ns, [8]/[9] %globaltimer at CTA entry/exit,
- * [10]/[11] at the first MMA issue / last accumulator commit.
- *
- * nvfp4_probe_mma_rate: measured kind::mxf4nvf4 tensor rate on every SM with
- * operands resident in shared memory (mode 0/1: single CTA without/with the
- * scale copies; 2/3: CTA pair without/with; 4: pair, scale copies batched per
- * 4-MMA stage; 5: pair with N = 192 and the scale copies; 6-9 measure the issuing
- * thread: 6 scale copies alone, 7 N = 64 MMAs, 8 N = 64 MMA + 2 commits, 9 copies +
- * N = 64 MMA + 2 commits).  Synchronous; returns TFLOP/s and cycles per iteration
- * (one MMA, or one group of copies in mode 6).
- */
-NVFP4_API int nvfp4_gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
-               float alpha, uint16_t *D, int M, int N, int K, uint64_t *trace, void *stream);
-/* nvfp4_gemm_trace with a fused epilogue (nvfp4_gemm_epilogue's arguments; epi may be
- * NULL): the same trace, for the cost of the epilogue per tile ([3], [4]). */
-NVFP4_API int nvfp4_gemm_trace_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B,
-                                        const uint8_t *SFB, float alpha, uint16_t *D, int M, int N, int K,
-                                        const nvfp4_epilogue *epi, uint64_t *trace, void *stream);
-NVFP4_API int nvfp4_probe_mma_rate(int mode, int iters, double *tflops, double *cycles_per_mma);
-/* nvfp4_scale_codes: the e4m3 scale code of n blocks given each block's bf16 amax
- * (device, sign ignored) and the device fp32 global scale, computed the way the fused
- * GEMM epilogue computes them for NVFP4 output — from per-launch threshold tables,
- * without a division per block — so that path can be checked against the
- * specification for every bf16 amax. */
-NVFP4_API int nvfp4_scale_codes(const uint16_t *amax_bf16, int64_t n, const float *global_scale, uint8_t *codes,
-                                void *stream);
-/* nvfp4_gemm_decode with per-CTA %globaltimer stamps in `trace` (device, grid x 6
- * uint64, grid = min(#SMs, ceil(N/128) * ceil(K/256))): [0] CTA entry, [1] release of
- * the wait on the preceding kernel, [2] first and [3] last ring slot reaching the
- * MMA thread, [4] CTA exit, [5] k-block iterations of the CTA. */
-NVFP4_API int nvfp4_gemm_decode_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
-                                      float alpha, uint16_t *D, int M, int N, int K, void *workspace,
-                                      size_t workspace_bytes, uint64_t *trace, void *stream);
 
 /* Number of kernel launches this library has issued in this process. */
 NVFP4_API uint64_t nvfp4_launch_count(void);

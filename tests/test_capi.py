@@ -75,3 +75,36 @@ def test_quantize_dynamic_rejects_bad_arguments_on_host(nv):
     assert L.nvfp4_quantize_dynamic(f, f, f, None, f, 0, 256, None) == -2           # M < 1
     assert L.nvfp4_quantize_dynamic(f + 16, f, f, None, f, 128, 256, None) == -3    # X 32-byte aligned
     assert L.nvfp4_quantize_dynamic(f, f, f, None, f + 2, 128, 256, None) == -3     # gs 4-byte aligned
+
+
+DIAG_HEADER = os.path.join(ROOT, "gpu-kernels_b200", "nvfp4_diag", "nvfp4_diag.h")
+
+
+def test_product_library_holds_no_diagnostics(nv):
+    """The traced kernels, the tensor-rate probe and the scale-code check are in the
+    separate diagnostic library only."""
+    raw = C.CDLL(nv.LIB_PATH)
+    diag_names = re.findall(r"^NVFP4_API\s+[\w\s\*]*?\b(\w+)\s*\(", open(DIAG_HEADER).read(), re.M)
+    assert diag_names
+    for name in diag_names:
+        assert name not in declared_symbols()
+        assert not hasattr(raw, name), f"{name} exported by the product library"
+
+
+def test_diagnostic_library_exports_its_header_and_the_product_api():
+    import nvfp4_diag
+    L = nvfp4_diag.lib()
+    text = open(DIAG_HEADER).read()
+    for name in re.findall(r"^NVFP4_API\s+[\w\s\*]*?\b(\w+)\s*\(", text, re.M) + declared_symbols():
+        assert hasattr(L, name), f"{name} not exported by the diagnostic library"
+
+
+def test_rank_barrier_rejects_bad_arguments_on_host(nv):
+    L = nv.lib()
+    pads = (C.c_uint64 * 2)(1 << 20, 1 << 21)
+    assert L.nvfp4_rank_barrier(None, 2, 0, 0, 4096, None) == -1              # no pads
+    assert L.nvfp4_rank_barrier(pads, 9, 0, 0, 4096, None) == -1              # more than 8 ranks
+    assert L.nvfp4_rank_barrier(pads, 2, 2, 0, 4096, None) == -1              # rank out of range
+    assert L.nvfp4_rank_barrier(pads, 2, 0, 1024, 4096, None) == -1           # channel beyond the pad
+    bad = (C.c_uint64 * 2)(1 << 20, (1 << 21) + 2)
+    assert L.nvfp4_rank_barrier(bad, 2, 0, 0, 4096, None) == -3               # 4-byte aligned slots

@@ -105,3 +105,25 @@ def test_gemm_dispatch_matches_persistent(nv, oracle, cuda_dev, M):
     torch.cuda.synchronize()
     assert rel_err(oracle, d1, a, sfa, b, sfb, alpha, M, N, K) <= TOL
     assert rel_err(oracle, d2, a, sfa, b, sfb, alpha, M, N, K) <= TOL
+
+
+def test_workspace_reused_across_shapes(nv, oracle, cuda_dev):
+    """One workspace serves calls of any shape: a call with few weight tiles (whose
+    fp32 partials fill the workspace) followed by one with more tiles than CTAs, whose
+    cut tiles' arrival counters must still read zero — through nvfp4_gemm's own
+    per-stream workspace and through one caller buffer passed to nvfp4_gemm_decode."""
+    shapes = [(16, 1024, 4096, 41), (1, 28672, 1024, 42), (64, 2048, 2048, 43), (3, 20480, 512, 44)]
+    ops = [operands(oracle, M, N, K, seed) for M, N, K, seed in shapes]
+    s = torch.cuda.Stream(cuda_dev)
+    with torch.cuda.stream(s):  # a fresh stream: its library workspace starts here
+        for (M, N, K, _), (a, sfa, b, sfb, alpha) in zip(shapes, ops):
+            d = nv.gemm(*(dev_t(t, cuda_dev) for t in (a, sfa, b, sfb)), alpha)
+            s.synchronize()
+            nv.device_status()
+            assert rel_err(oracle, d, a, sfa, b, sfb, alpha, M, N, K) <= TOL, (M, N, K)
+    L = nv.lib()
+    ws = torch.zeros(max(L.nvfp4_gemm_decode_workspace_size(M, N) for M, N, _, _ in shapes), dtype=torch.uint8,
+                     device=cuda_dev)
+    for (M, N, K, _), (a, sfa, b, sfb, alpha) in zip(shapes, ops):
+        out, _ = decode_call(nv, cuda_dev, a, sfa, b, sfb, alpha, M, N, K, ws=ws)
+        assert rel_err(oracle, out, a, sfa, b, sfb, alpha, M, N, K) <= TOL, (M, N, K)

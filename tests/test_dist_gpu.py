@@ -71,19 +71,26 @@ def test_column_parallel_nccl_matches_single_gpu(M, N, K):
     procs = [ctx.Process(target=_rank, args=(r, world, port, M, N, K, q)) for r in range(world)]
     for p in procs:
         p.start()
-    for p in procs:
-        p.join(timeout=240)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
+    _join_without_kill(procs, 300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert q.get(timeout=5) is True
 
 
+def _agree(dist, world, value):
+    """Every rank's value (an all-gather of Python objects, bounded by the process
+    group's timeout)."""
+    vals = [None] * world
+    dist.all_gather_object(vals, value)
+    return vals
+
+
 def _rank_fused(rank, world, port, M, N, K, q):
     """Fused GEMM + all-gather (nvfp4_gemm_gather through symmetric memory): NVLink
-    stores to every rank's buffer first; the NVLink-multicast form only once that
-    matched, and only where the fabric offers a multicast address."""
+    stores to every rank's buffer first; the NVLink-multicast form only once every rank
+    matched and every rank has a multicast address.  Every wait here is bounded: the
+    process group's 60 s timeout, and the library's own device waits (its rank barrier
+    included, limit 5 s) — so every rank returns by itself, and it releases its
+    symmetric buffers and the process group on the way out whatever happened."""
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -91,30 +98,31 @@ def _rank_fused(rank, world, port, M, N, K, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     result = {"unicast": None, "multicast": None}
+    fg = probe = d = d2 = None
     try:
         nv, a, sfa, b, sfb = _operands(M, N, K, dev)
+        nv.set_wait_timeout_ns(5_000_000_000)
         from nvfp4_b200.dist import FusedGather, shard_bounds, shard_weight
         bs, ss = shard_weight(b, sfb, K, world, rank)
         n0, _ = shard_bounds(N, world, rank)
         full = nv.gemm(a, sfa, b, sfb, 0.5)
         fg = FusedGather(M, N, dev, multicast=False)
         fg.out.fill_(float("nan"))
+        torch.cuda.synchronize()
         dist.barrier()
         d = fg.gemm(a, sfa, bs.contiguous(), ss.contiguous(), 0.5, n0)
         torch.cuda.synchronize()
-        nv.device_status()
-        ok = bool(torch.equal(d, full))
-        result["unicast"] = ok
-        oks = [None] * world
-        dist.all_gather_object(oks, ok)
-        if all(oks):
-            # multicast when the buffer has a multicast address
+        nv.device_status()  # raises if a bounded wait gave up
+        result["unicast"] = bool(torch.equal(d, full))
+        if all(_agree(dist, world, result["unicast"])):
             try:
                 probe = FusedGather(M, N, dev, multicast=True)
             except RuntimeError:
                 probe = None
-            if probe is not None and probe.multicast:
+            have = probe is not None and probe.multicast
+            if all(_agree(dist, world, have)):  # every rank takes the multicast arm, or none does
                 probe.out.fill_(float("nan"))
+                torch.cuda.synchronize()
                 dist.barrier()
                 d2 = probe.gemm(a, sfa, bs.contiguous(), ss.contiguous(), 0.5, n0)
                 torch.cuda.synchronize()
@@ -125,7 +133,23 @@ def _rank_fused(rank, world, port, M, N, K, q):
         if rank == 0:
             q.put(result)
     finally:
-        dist.destroy_process_group()
+        try:
+            torch.cuda.synchronize()
+        finally:
+            fg = probe = d = d2 = None  # symmetric buffers released before the group goes
+            dist.destroy_process_group()
+
+
+def _join_without_kill(procs, limit_s):
+    """Wait for the ranks; never kill one (a rank may hold memory bound to an NVLink
+    multicast object).  Every wait inside the ranks is bounded, so they end by
+    themselves; a rank still running after `limit_s` fails the test."""
+    import time
+    deadline = time.monotonic() + limit_s
+    for p in procs:
+        p.join(timeout=max(0.0, deadline - time.monotonic()))
+    alive = [i for i, p in enumerate(procs) if p.is_alive()]
+    assert not alive, f"ranks {alive} still running after {limit_s} s"
 
 
 @pytest.mark.parametrize("M,N,K", [(512, 3072, 1024), (300, 1280, 2048)])
@@ -139,11 +163,7 @@ def test_fused_gather_matches_single_gpu(M, N, K):
     procs = [ctx.Process(target=_rank_fused, args=(r, world, port, M, N, K, q)) for r in range(world)]
     for p in procs:
         p.start()
-    for p in procs:
-        p.join(timeout=240)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
+    _join_without_kill(procs, 300)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     res = q.get(timeout=5)
     print("fused gather:", res)

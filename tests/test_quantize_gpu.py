@@ -94,9 +94,12 @@ def test_scale_code_of_every_bf16_amax(nv, oracle, cuda_dev, gs):
 @pytest.mark.parametrize("gs", GS_SWEEP + [0.0, float("nan"), -1.0, 2.0 ** -120])
 def test_table_scale_codes_every_bf16_amax(nv, oracle, cuda_dev, gs):
     """The fused GEMM epilogue's division-free scale codes (threshold tables built per
-    launch, a first guess corrected by two comparisons; nvfp4_scale_codes runs that
+    launch, a first guess corrected by two comparisons; nvfp4_scale_codes of the
+    diagnostic library (the same sources, nvfp4_diag) runs that
     arithmetic) against the specification's code for every bf16 amax from +0 to +inf,
     negative zero and negative values (the sign is ignored) included."""
+    import nvfp4_diag
+    diag = nvfp4_diag.lib()
     x = _every_amax_blocks()
     _, sf_ref = oracle.quantize(x, gs)
     rows, K = x.shape
@@ -106,7 +109,7 @@ def test_table_scale_codes_every_bf16_amax(nv, oracle, cuda_dev, gs):
         t = torch.from_numpy(amax.view(np.int16)).to(cuda_dev)
         codes = torch.empty(len(vals), dtype=torch.uint8, device=cuda_dev)
         g = torch.tensor([gs], dtype=torch.float32, device=cuda_dev)
-        st = nv.lib().nvfp4_scale_codes(t.data_ptr(), len(vals), g.data_ptr(), codes.data_ptr(),
+        st = diag.nvfp4_scale_codes(t.data_ptr(), len(vals), g.data_ptr(), codes.data_ptr(),
                                         torch.cuda.current_stream(cuda_dev).cuda_stream)
         assert st == 0
         torch.cuda.synchronize()
