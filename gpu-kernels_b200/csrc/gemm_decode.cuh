@@ -119,10 +119,12 @@ struct Params {
     int m_total;
     // Optional per-CTA %globaltimer stamps (nullptr = off), kDecodeTraceSlots u64 per
     // CTA: [0] entry [1] dependency wait released [2] first slot full (MMA thread)
-    // [3] last slot full [4] epilogue done [5] iterations
+    // [3] last slot full [4] epilogue done [5] iterations; of the CTA's last segment:
+    // [6] accumulator in registers [7] arrival counted (cut tiles) [8] partials summed
+    // (the tile's last contributor)
     unsigned long long *trace;
 };
-constexpr int kDecodeTraceSlots = 6;
+constexpr int kDecodeTraceSlots = 9;
 
 // The tile schedule: host-computed for one weight matrix, computed on the device from
 // the active groups in the grouped form (tiles = active experts x weight tiles).
@@ -604,6 +606,8 @@ __global__ void __launch_bounds__(kThreads, COLOC ? 2 : 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_acc_empty + 8 * buf);
+            const bool last_seg = v >= n_iters;  // v already counts this segment
+            if (trace && etid == 0 && last_seg) trace[6] = global_timer_ns();
 
             const DTile dt = dtile(tile);
             const int n = dt.ncol0 + nl;
@@ -627,23 +631,54 @@ __global__ void __launch_bounds__(kThreads, COLOC ? 2 : 1)
                 if (etid == 0) {
                     const int prev = atomic_add_acq_rel_gpu(p.counters + tile, seg_len);
                     *last_flag = (prev + seg_len == p.num_kb);
+                    if (trace && last_seg) trace[7] = global_timer_ns();
                 }
                 named_barrier(1, 128);
                 if (!*last_flag) continue;
                 // last contributor: add every partial (its own included, re-read from L2)
-                // in CTA order, so the result does not depend on who finished last
+                // in CTA order, so the result does not depend on who finished last.
+                // This is the tail of a call whose tiles are all cut, so: the partials
+                // of kCh contributors are loaded at once (one L2 round trip per kCh, the
+                // loads unconditional — clamped to the tile's last owner, whose range is
+                // never empty — and the unused ones dropped), range bounds in 32-bit
+                // arithmetic where they fit, and a contributor's partial slot read off
+                // its range start (slot 0: the range starts inside this tile) instead of
+                // a division.
+                constexpr int kCh = MPAD <= 16 ? 4 : (MPAD <= 32 ? 2 : 1);
+                const bool narrow = q.sk_iters <= (int64_t)(0x7fffffff / q.grid);
+                auto begin_of = [&](int c) -> int64_t {
+                    return narrow ? (int64_t)((uint32_t)c * (uint32_t)q.sk_iters / (uint32_t)q.grid)
+                                  : range_begin(c, q);
+                };
                 const int c_lo = owner_of(tile_first, q), c_hi = owner_of(tile_last, q);
 #pragma unroll
                 for (int m = 0; m < MPAD; m++) sum[m] = 0.0f;
-                for (int c = c_lo; c <= c_hi; c++) {
-                    const int64_t cb = range_begin(c, q);
-                    if (cb == range_begin(c + 1, q)) continue;  // empty range: no partial
-                    const int cslot = ((int)(cb / p.num_kb) == tile) ? 0 : 1;
-                    const float *part = p.partials + ((int64_t)c * 2 + cslot) * MPAD * kTileN;
+                int64_t cb = begin_of(c_lo);
+                for (int c0 = c_lo; c0 <= c_hi; c0 += kCh) {
+                    float part_v[kCh][MPAD];
+                    bool has[kCh];
 #pragma unroll
-                    for (int m = 0; m < MPAD; m++) sum[m] += __ldcg(part + m * kTileN + nl);
+                    for (int j = 0; j < kCh; j++) {
+                        const int c = min(c0 + j, c_hi);
+                        const int64_t ce = begin_of(c + 1);
+                        has[j] = c0 + j <= c_hi && ce != cb;  // an empty range leaves no partial
+                        const int cslot = cb >= tile_first ? 0 : 1;
+                        const float *part = p.partials + ((int64_t)c * 2 + cslot) * MPAD * kTileN;
+#pragma unroll
+                        for (int m = 0; m < MPAD; m++) part_v[j][m] = __ldcg(part + m * kTileN + nl);
+                        cb = ce;
+                    }
+#pragma unroll
+                    for (int j = 0; j < kCh; j++)
+                        if (has[j]) {
+#pragma unroll
+                            for (int m = 0; m < MPAD; m++) sum[m] += part_v[j][m];
+                        }
                 }
-                if (etid == 0) p.counters[tile] = 0;  // reusable by the next call
+                if (etid == 0) {
+                    p.counters[tile] = 0;  // reusable by the next call
+                    if (trace && last_seg) trace[8] = global_timer_ns();
+                }
             }
             if (p.epi.plain()) {
                 if (n < p.N) {

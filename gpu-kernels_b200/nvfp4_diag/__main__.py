@@ -24,7 +24,9 @@ PROBE_MODES = {0: "single-CTA MMA only", 1: "single-CTA MMA + 3 scale copies eac
                6: "CTA-pair, 3 scale copies per iteration, no MMA (issue cost)",
                7: "CTA-pair N=64 MMA only (issue cost)",
                8: "CTA-pair N=64 MMA + 2 commits (issue cost)",
-               9: "CTA-pair 3 copies + N=64 MMA + 2 commits (issue cost)"}
+               9: "CTA-pair 3 copies + N=64 MMA + 2 commits (issue cost)",
+               10: "as 4, pseudo-random operands and scales",
+               11: "as 2 (MMA only), pseudo-random operands and scales"}
 
 
 def probe(iters: int = 20000):
@@ -119,7 +121,8 @@ def decode_trace(M: int, N: int, K: int, calls: int = 8, sets: int = 3):
     ws_bytes = _l().nvfp4_gemm_decode_workspace_size(M, N)
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
     grid = torch.cuda.get_device_properties(dev).multi_processor_count  # grid <= #SMs
-    tr = torch.zeros(calls, grid * 6, dtype=torch.int64, device=dev)
+    slots = 9
+    tr = torch.zeros(calls, grid * slots, dtype=torch.int64, device=dev)
     s = torch.cuda.Stream()
 
     def launch(c):
@@ -148,7 +151,7 @@ def decode_trace(M: int, N: int, K: int, calls: int = 8, sets: int = 3):
         e1.record(s)
     torch.cuda.synchronize()
     del g
-    t = tr.view(calls, grid, 6).cpu()
+    t = tr.view(calls, grid, slots).cpu()
     used = t[0, :, 0] > 0
     t = t[:, used]
     t0 = int(t[0, :, 0].min())
@@ -176,6 +179,19 @@ def decode_trace(M: int, N: int, K: int, calls: int = 8, sets: int = 3):
                "entry_to_release": pct(c[:, 1] - c[:, 0]),
                "release_after_first_release": pct(c[:, 1] - c[:, 1].min()),
                "exit_after_first_exit": pct(c[:, 4] - c[:, 4].min())}
+    # the last segment's epilogue: last data -> accumulator in registers -> arrival
+    # counted -> partials summed (the tile's last contributor) -> CTA exit
+    cut = c[:, 7] > 0
+    fin = c[:, 8] > 0
+    if cut.any():
+        per_cta["last_data_to_acc_regs"] = pct(c[cut, 6] - c[cut, 3])
+        per_cta["acc_regs_to_counted"] = pct(c[cut, 7] - c[cut, 6])
+    if fin.any():
+        per_cta["finisher_counted_to_summed"] = pct(c[fin, 8] - c[fin, 7])
+        per_cta["finisher_summed_to_exit"] = pct(c[fin, 4] - c[fin, 8])
+    nonfin = cut & ~fin
+    if nonfin.any():
+        per_cta["nonfinisher_counted_to_exit"] = pct(c[nonfin, 4] - c[nonfin, 7])
     tail = ((c[:, 4] - c[:, 3]) / 1e3).tolist()
     slow = [i for i, x in enumerate(tail) if x > 2.0]
     per_cta["slow_tail_ctas"] = slow

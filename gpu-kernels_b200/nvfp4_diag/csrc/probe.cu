@@ -19,6 +19,10 @@
 //        7 CTA pair M=256 N=64 MMA only (32 cycles of tensor work each)
 //        8 CTA pair N=64 MMA + 2 commits (one per CTA's barrier) per iteration
 //        9 CTA pair, 3 scale copies + N=64 MMA + 2 commits per iteration
+// Operand-value modes (pseudo-random e2m1 codes and scale codes 0x30..0x3f instead
+// of zeros, to see whether the rate depends on the data):
+//       10 as 4 (CTA pair, 12 scale copies per 4-MMA stage, then 4 MMAs)
+//       11 as 2 (CTA pair, MMA only)
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -35,9 +39,23 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, unsigned l
     __shared__ __align__(8) uint64_t bar;
     __shared__ __align__(8) uint64_t bar2;  // per-iteration commits of modes 8 and 9 (never waited on)
     const int warp = threadIdx.x >> 5;
-    // zero operands and scales: throughput does not depend on the values
-    for (int i = threadIdx.x * 16; i < kProbeSmem - 1024; i += blockDim.x * 16)
-        st_shared_v4(base + i, 0, 0, 0, 0);
+    // zero operands and scales (modes 0-9), or pseudo-random ones (10, 11)
+    constexpr bool kRandom = MODE >= 10;
+    for (int i = threadIdx.x * 16; i < kProbeSmem - 1024; i += blockDim.x * 16) {
+        uint32_t w[4] = {0, 0, 0, 0};
+        if (kRandom) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                uint32_t h = (uint32_t)(i + 4 * q) * 2654435761u + blockIdx.x * 40503u;
+                h ^= h >> 15;
+                h *= 2246822519u;
+                h ^= h >> 13;
+                // scale region (from 48 KB): e4m3 codes 0x30..0x3f; operands: any e2m1 nibbles
+                w[q] = i >= 49152 ? (h & 0x0f0f0f0fu) | 0x30303030u : h;
+            }
+        }
+        st_shared_v4(base + i, w[0], w[1], w[2], w[3]);
+    }
     fence_proxy_async_smem();
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(&bar), 1);
@@ -60,7 +78,7 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, unsigned l
     const uint32_t sA = base, sB = base + 16384, sSf = base + 49152;
     const bool issuer = kPair ? (cluster_ctarank() == 0) : true;
     if (warp == 0 && issuer && elect_one()) {
-        constexpr uint32_t idesc = idesc_mxf4nvf4(kPair ? 256 : 128, MODE == 5 ? 192 : (MODE >= 7 ? 64 : 256));
+        constexpr uint32_t idesc = idesc_mxf4nvf4(kPair ? 256 : 128, MODE == 5 ? 192 : ((MODE >= 7 && MODE <= 9) ? 64 : 256));
         const uint32_t c0 = map_to_cta(smem_u32(&bar2), 0), c1 = map_to_cta(smem_u32(&bar2), 1);
         const unsigned long long t0 = clock64();
         for (int i = 0; i < iters; i++) {
@@ -74,7 +92,7 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, unsigned l
                 tmem_cp_32x128_x4(col + 4, smem_desc(sSf + 2048 + j * 512, 16, 128, 0));
                 tmem_cp_32x128_x4(col + 8, smem_desc(sSf + 4096 + j * 512, 16, 128, 0));
                 mma_mxf4nvf4(tmem, ad, bd, idesc, col, col + 4, i != 0);
-            } else if constexpr (MODE == 2) {
+            } else if constexpr (MODE == 2 || MODE == 11) {
                 mma_mxf4nvf4_pair(tmem, ad, bd, idesc, col, col + 4, i != 0);
             } else if constexpr (MODE == 3 || MODE == 5) {
                 tmem_cp_32x128_x4_pair(col, smem_desc(sSf + j * 512, 16, 128, 0));
@@ -160,7 +178,7 @@ using namespace nvfp4;
 // (FLOP of all MMAs / elapsed device time measured with CUDA events) and the
 // longest per-SM MMA-issue time in cycles.  Synchronous; allocates a few bytes.
 extern "C" NVFP4_API int nvfp4_probe_mma_rate(int mode, int iters, double *tflops, double *cycles_per_mma) {
-    if (mode < 0 || mode > 9 || iters < 16 || !tflops) return NVFP4_ERR_INVALID;
+    if (mode < 0 || mode > 11 || iters < 16 || !tflops) return NVFP4_ERR_INVALID;
     DeviceInfo di;
     int st = device_info(&di);
     if (st) return st;
@@ -181,7 +199,9 @@ extern "C" NVFP4_API int nvfp4_probe_mma_rate(int mode, int iters, double *tflop
             case 6: return run_probe<6>(it, di.sm_count, nullptr, dcyc);
             case 7: return run_probe<7>(it, di.sm_count, nullptr, dcyc);
             case 8: return run_probe<8>(it, di.sm_count, nullptr, dcyc);
-            default: return run_probe<9>(it, di.sm_count, nullptr, dcyc);
+            case 9: return run_probe<9>(it, di.sm_count, nullptr, dcyc);
+            case 10: return run_probe<10>(it, di.sm_count, nullptr, dcyc);
+            default: return run_probe<11>(it, di.sm_count, nullptr, dcyc);
         }
     };
     st = go(iters);  // warm-up (clocks ramp)
@@ -199,7 +219,7 @@ extern "C" NVFP4_API int nvfp4_probe_mma_rate(int mode, int iters, double *tflop
         const int ctas = pair ? di.sm_count / 2 * 2 : di.sm_count;
         // per MMA: 2 * M * N * K with M = 256 over a pair (128 per CTA), N = 256 (192 in
         // mode 5, 64 in modes 7-9, no MMA in mode 6), K = 64
-        const int n = mode == 5 ? 192 : (mode >= 7 ? 64 : (mode == 6 ? 0 : 256));
+        const int n = mode == 5 ? 192 : ((mode >= 7 && mode <= 9) ? 64 : (mode == 6 ? 0 : 256));
         const double flop = (double)ctas * iters * 2.0 * 128 * n * 64;
         *tflops = flop / (ms * 1e-3) / 1e12;
         unsigned long long cyc = 0;

@@ -30,10 +30,12 @@ NVFP4_API int nvfp4_gemm_trace(const uint8_t *A, const uint8_t *SFA, const uint8
 NVFP4_API int nvfp4_gemm_trace_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B,
                                         const uint8_t *SFB, float alpha, uint16_t *D, int M, int N, int K,
                                         const nvfp4_epilogue *epi, uint64_t *trace, void *stream);
-/* nvfp4_gemm_decode with per-CTA %globaltimer stamps in `trace` (device, grid x 6
+/* nvfp4_gemm_decode with per-CTA %globaltimer stamps in `trace` (device, grid x 9
  * uint64, grid = min(#SMs, ceil(N/128) * ceil(K/256))): [0] CTA entry, [1] release of
  * the wait on the preceding kernel, [2] first and [3] last ring slot reaching the
- * MMA thread, [4] CTA exit, [5] k-block iterations of the CTA. */
+ * MMA thread, [4] CTA exit, [5] k-block iterations of the CTA; for its last segment
+ * [6] accumulator in registers, [7] arrival counted (a cut tile), [8] partials summed
+ * (the tile's last contributor); 0 where a stamp does not apply. */
 NVFP4_API int nvfp4_gemm_decode_trace(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
                                       float alpha, uint16_t *D, int M, int N, int K, void *workspace,
                                       size_t workspace_bytes, uint64_t *trace, void *stream);
@@ -42,7 +44,8 @@ NVFP4_API int nvfp4_gemm_decode_trace(const uint8_t *A, const uint8_t *SFA, cons
  * resident in shared memory (mode 0/1: single CTA without/with the scale copies; 2/3:
  * CTA pair without/with; 4: pair, scale copies batched per 4-MMA stage; 5: pair with
  * N = 192 and the scale copies; 6-9 measure the issuing thread: 6 scale copies alone,
- * 7 N = 64 MMAs, 8 N = 64 MMA + 2 commits, 9 copies + N = 64 MMA + 2 commits).
+ * 7 N = 64 MMAs, 8 N = 64 MMA + 2 commits, 9 copies + N = 64 MMA + 2 commits; 10 and
+ * 11 are modes 4 and 2 with pseudo-random operands and scales instead of zeros).
  * Synchronous; returns TFLOP/s and cycles per iteration (one MMA, or one group of
  * copies in mode 6).
  */
