@@ -384,22 +384,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 const uint32_t use = L::kAccBufs == 2 ? (uint32_t)(local >> 1) : (uint32_t)local;
                 const uint32_t d_tmem = tmem_base + buf * BN;
                 const uint32_t sfb_shift = (uint32_t)(((tn * BN) & 127) >> 5);
-                long long c0 = TRACE ? clock64() : 0;
-                if (!(p.spin ? spin_parity(bar_acc_empty + 8 * buf, (use & 1) ^ 1, tmo, abort_flag)
-                             : wait_parity(bar_acc_empty + 8 * buf, (use & 1) ^ 1, tmo, abort_flag))) {
-                    report_timeout(abort_flag, p.ctl.status);
-                    ok = false;
-                    break;
-                }
-                if (TRACE) {
-                    const long long c1 = clock64();
-                    t_acc += c1 - c0;
-                    if (!t_first) {
-                        t_first = c1;
-                        ns_first = global_timer_ns();
+                long long c0 = 0;
+                // The accumulator is waited for just before the tile's first MMA: the first
+                // slot's scale copies (other tensor-memory columns) go out before, so they
+                // run while the epilogue is still reading the previous tile out.
+                auto wait_acc = [&]() -> bool {
+                    if (TRACE) c0 = clock64();
+                    if (!(p.spin ? spin_parity(bar_acc_empty + 8 * buf, (use & 1) ^ 1, tmo, abort_flag)
+                                 : wait_parity(bar_acc_empty + 8 * buf, (use & 1) ^ 1, tmo, abort_flag))) {
+                        report_timeout(abort_flag, p.ctl.status);
+                        return false;
                     }
-                }
-                tc_fence_after();
+                    if (TRACE) {
+                        const long long c1 = clock64();
+                        t_acc += c1 - c0;
+                        if (!t_first) {
+                            t_first = c1;
+                            ns_first = global_timer_ns();
+                        }
+                    }
+                    tc_fence_after();
+                    return true;
+                };
                 for (int kb = 0; kb < p.num_kb; kb++) {
                     if (TRACE) c0 = clock64();
                     if (!(p.spin ? spin_parity(full_bar, phase, tmo, abort_flag)
@@ -413,12 +419,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     const uint32_t acc0 = kb != 0;
                     if ((kb + 1) * KG <= p.k_groups) {
                         // full slot: descriptor offsets are immediates (addr >> 4 units)
+                        any_issued = true;  // an abort after these copies drains them
 #pragma unroll
                         for (int j = 0; j < KG; j++) {
                             const uint32_t col = sf_col + j * L::kSfColsPerGroup;
                             tmem_cp_32x128_x4_pair(col, sfa_d + j * 32);
                             tmem_cp_32x128_x4_pair(col + 4, sfb_d + j * 32);
                             tmem_cp_32x128_x4_pair(col + 8, sfb_d + (KG + j) * 32);
+                        }
+                        if (kb == 0 && !wait_acc()) {
+                            ok = false;
+                            break;
                         }
 #pragma unroll
                         for (int j = 0; j < KG; j++) {
@@ -428,6 +439,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                         }
                     } else {
                         const int kg = p.k_groups - kb * KG;  // last, partial slot
+                        if (kb == 0 && !wait_acc()) {
+                            ok = false;
+                            break;
+                        }
                         for (int j = 0; j < kg; j++) {
                             const uint32_t col = sf_col + j * L::kSfColsPerGroup;
                             tmem_cp_32x128_x4_pair(col, sfa_d + j * 32);
