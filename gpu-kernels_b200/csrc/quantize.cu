@@ -399,7 +399,16 @@ extern "C" int nvfp4_quantize(const uint16_t *X, uint8_t *Q, uint8_t *SF, const 
     const int64_t n_blocks = (int64_t)M * K / 16;
     const int threads = 256;
     int64_t blocks = (n_blocks + threads - 1) / threads;
-    const int64_t cap = (int64_t)di.sm_count * 8;  // 8 x 256 threads resident per SM
+    // at most one wave of resident CTAs (the loop strides over the rest): a grid beyond
+    // what fits on the SMs at once leaves a partial second wave
+    static int per_sm[64] = {};
+    if (!per_sm[di.device]) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, quantize_kernel, threads, 0) != cudaSuccess || n < 1)
+            n = 1;
+        per_sm[di.device] = n;
+    }
+    const int64_t cap = (int64_t)di.sm_count * per_sm[di.device];
     if (blocks > cap) blocks = cap;
     quantize_kernel<<<(unsigned)blocks, threads, 0, s>>>(reinterpret_cast<const __nv_bfloat16 *>(X), Q, SF,
                                                          global_scale, n_blocks, K);
