@@ -152,8 +152,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
     const int n_m = (p.M + 255) / 256, n_n = (p.N + BN - 1) / BN;
     const int G = p.grouped.groups;
-    if (G > 0 && warp == 2)
-        build_group_tables(p.grouped.m_offsets, G, p.grouped.m_total, n_n, lane, g_row0, g_rend, g_sfa0, g_tile0);
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
             mbar_init(bar_full + 8 * s, 1);
@@ -181,6 +179,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         tmem_alloc_pair(smem_u32(tmem_slot), L::kTmemCols);
         tmem_relinquish_pair();
     }
+    // Launched as a programmatic dependent of the previous kernel in the stream: the
+    // set-up above overlapped that kernel's tail; nothing of global memory is read or
+    // written before it has completed.
+    grid_dependency_wait();
+    if (G > 0 && warp == 2)
+        build_group_tables(p.grouped.m_offsets, G, p.grouped.m_total, n_n, lane, g_row0, g_rend, g_sfa0, g_tile0);
     tc_fence_before();
     cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
     tc_fence_after();
@@ -317,6 +321,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     }
                 }
             }
+            if (ab) grid_launch_dependents();  // all loads issued: the next kernel may start its set-up
             if (!ok && ab && rank == 0) {
                 volatile int never = 0;
                 for (int s = 0; s < STAGES; s++)
@@ -673,6 +678,17 @@ static int pair_spin() {
     return v;
 }
 
+// Programmatic dependent launch of the pair kernel (1, the default): its set-up runs
+// while the previous kernel in the stream finishes, every global access waits for
+// it (griddepcontrol.wait); env NVFP4_PAIR_PDL=0 launches it in plain stream order.
+static int pair_pdl() {
+    static int v = [] {
+        const char *e = std::getenv("NVFP4_PAIR_PDL");
+        return e ? (std::atoi(e) ? 1 : 0) : 1;
+    }();
+    return v;
+}
+
 // Tile scheduler of the pair kernel: static persistent (0) or cluster launch control
 // (1); env NVFP4_PAIR_SCHED=static|clc overrides.  Measured at M=N=K=8192 on one box:
 // static 203.2 us, cluster launch control 208.2 us (MoE grouped: 232 vs 242 us) —
@@ -770,7 +786,17 @@ static int launch_pair(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, c
     // static: one persistent cluster per SM pair; cluster launch control: one cluster
     // per tile, the running ones cancelling the rest as they finish
     const int pairs = p.clc ? p.num_tiles : std::min(p.num_tiles, di.sm_count / 2);
-    kern<<<2 * pairs, kPairThreads, L::kDynamicSmem, stream>>>(ta, tb, tsa, tsb, td, p);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(kPairThreads);
+    cfg.dynamicSmemBytes = L::kDynamicSmem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = pair_pdl() ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, kern, ta, tb, tsa, tsb, td, p) != cudaSuccess) return NVFP4_ERR_CUDA;
     count_launch();
     return cuda_status(cudaGetLastError());
 }
