@@ -1103,9 +1103,6 @@ def run_ours(args):
         e2e_value = flops * world / (e2e_ms / 1e3) / 1e12
         barrier(world)
 
-    sustained = None
-    if not args.no_sustained:
-        sustained = sustained_section(nv, sets, d, M, N, K, dev)
     pk = peaks()
     fp4_peak_est = 4.0 * pk["bf16_tflops"]
     traffic = committed_traffic().get("gemm_8192", {}).get("dram_bytes_per_launch")
@@ -1119,6 +1116,9 @@ def run_ours(args):
         epi = epilogue_section(nv, sets, M, N, K)
     gath = gather_section(nv, dev, world, rank) if not args.no_gather else None
     sweep = shape_sweep_section(nv, dev) if (rank == 0 and not args.no_sweep) else None
+    # last of the GPU sections: a second of GEMMs at the power cap leaves the clocks low
+    # for a while, which would slow whatever is measured after it
+    sustained = sustained_section(nv, sets, d, M, N, K, dev) if not args.no_sustained else None
     cpu_cfg = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu, _, _ = cpu_reference_sample(a, sfa, b, sfb, alpha, M, N, K, target_s=args.cpu_seconds)
