@@ -51,9 +51,22 @@ __device__ __forceinline__ void quantize_blocks(const __nv_bfloat16 *__restrict_
     const int64_t rest_k = K >> 6;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    // Row and block-in-row of each of this lane's blocks, kept as running values: the
+    // lane's blocks advance by a fixed step, so a division happens once per lane, not
+    // once per block (a 64-bit division was a large share of the loop's instructions).
+    const int per_row = (int)(K >> 4);
+    const int64_t step = stride * kQuantUnroll;
+    const int step_rows = (int)(step / per_row), step_rem = (int)(step % per_row);
+    int row[kQuantUnroll], col[kQuantUnroll];
+#pragma unroll
+    for (int u = 0; u < kQuantUnroll; u++) {
+        const int64_t gi = g + u * stride;
+        row[u] = (int)(gi / per_row);
+        col[u] = (int)(gi - (int64_t)row[u] * per_row);
+    }
     // The trip count is warp-uniform: every warp covers 32 consecutive blocks and
     // n_blocks % 4 == 0 (K % 64 == 0), so whole 4-lane k-groups are active or not.
-    for (; g - lane < n_blocks; g += stride * kQuantUnroll) {
+    for (; g - lane < n_blocks; g += step) {
         uint32_t raw[kQuantUnroll][8];
 #pragma unroll
         for (int u = 0; u < kQuantUnroll; u++) {
@@ -86,20 +99,27 @@ __device__ __forceinline__ void quantize_blocks(const __nv_bfloat16 *__restrict_
             const uint32_t c3 = __shfl_down_sync(0xffffffffu, code, 3);
             if (gi < n_blocks) {
                 *reinterpret_cast<uint2 *>(Q + gi * 8) = make_uint2(lo, hi);
-                if ((lane & 3) == 0) {
-                    const int64_t e = gi * 16;  // first element of the k-group
-                    const int64_t r = e / K, kg = (e - r * K) >> 6;
-                    *reinterpret_cast<uint32_t *>(SF + sf_group_offset(r, kg, rest_k)) =
+                if ((lane & 3) == 0)  // first block of the k-group
+                    *reinterpret_cast<uint32_t *>(SF + sf_group_offset(row[u], col[u] >> 2, rest_k)) =
                         code | (c1 << 8) | (c2 << 16) | (c3 << 24);
-                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kQuantUnroll; u++) {
+            row[u] += step_rows;
+            col[u] += step_rem;
+            if (col[u] >= per_row) {
+                col[u] -= per_row;
+                row[u]++;
             }
         }
     }
 }
 
-__global__ void __launch_bounds__(256) quantize_kernel(const __nv_bfloat16 *__restrict__ X, uint8_t *__restrict__ Q,
-                                                       uint8_t *__restrict__ SF, const float *__restrict__ gs_ptr,
-                                                       int64_t n_blocks, int64_t K) {
+// 5 CTAs (40 warps) per SM: the register bound keeps the loop at 48 registers.
+__global__ void __launch_bounds__(256, 5)
+    quantize_kernel(const __nv_bfloat16 *__restrict__ X, uint8_t *__restrict__ Q, uint8_t *__restrict__ SF,
+                    const float *__restrict__ gs_ptr, int64_t n_blocks, int64_t K) {
     __shared__ float inv_table[256];
     const float gs = *gs_ptr;
     const bool gs_ok = gs_usable(gs);
