@@ -121,6 +121,8 @@ __global__ void __launch_bounds__(256, 5)
     quantize_kernel(const __nv_bfloat16 *__restrict__ X, uint8_t *__restrict__ Q, uint8_t *__restrict__ SF,
                     const float *__restrict__ gs_ptr, int64_t n_blocks, int64_t K) {
     __shared__ float inv_table[256];
+    grid_dependency_wait();    // X and gs may come from the previous kernel in the stream
+    grid_launch_dependents();  // the next kernel may be placed as this one's CTAs finish
     const float gs = *gs_ptr;
     const bool gs_ok = gs_usable(gs);
     inv_table[threadIdx.x] = block_inverse(threadIdx.x, gs, gs_ok);  // blockDim.x == 256
@@ -430,8 +432,20 @@ extern "C" int nvfp4_quantize(const uint16_t *X, uint8_t *Q, uint8_t *SF, const 
     }
     const int64_t cap = (int64_t)di.sm_count * per_sm[di.device];
     if (blocks > cap) blocks = cap;
-    quantize_kernel<<<(unsigned)blocks, threads, 0, s>>>(reinterpret_cast<const __nv_bfloat16 *>(X), Q, SF,
-                                                         global_scale, n_blocks, K);
+    // a programmatic dependent of the previous kernel in the stream: the CTAs are
+    // placed while that kernel finishes, and wait for it before reading anything
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(threads);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, quantize_kernel, reinterpret_cast<const __nv_bfloat16 *>(X), Q, SF, global_scale,
+                           n_blocks, (int64_t)K) != cudaSuccess)
+        return NVFP4_ERR_CUDA;
     count_launch();
     if ((st = cuda_status(cudaGetLastError()))) return st;
     return sf_pad_zero(SF, M, K, s, di);
