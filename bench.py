@@ -1157,7 +1157,10 @@ def run_ours(args):
                                           "warm-up) and right after it; the 1 kW power cap can lower the clock "
                                           "after a long run of these GEMMs"),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                    "ms_per_step": e2e_ms, "path": "pinned host -> nvfp4_gemm_host (4x4 blocks, copies overlapped) -> pinned host"},
+                    "ms_per_step": e2e_ms, "path": "pinned host -> nvfp4_gemm_host (4x4 blocks, copies overlapped) -> pinned host",
+                    "bound": "host link: the step's copies, not the GEMM (the device-timed GEMM is ~6 % of it)",
+                    "host_link_gbs": ((h2d + d2h) / (e2e_ms / 1e3) / 1e9) if e2e_ms else None,
+                    "gemm_share": (kernel_ms / e2e_ms) if e2e_ms else None},
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
