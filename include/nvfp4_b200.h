@@ -282,9 +282,12 @@ NVFP4_API int nvfp4_selftest_wait_timeout(uint64_t timeout_ns);
 /*
  * The GEMM on HOST buffers (A, SFA, B, SFB in, D out; pinned memory for overlap):
  * the device-side counterpart of the reference runner's copy-in / GEMM / copy-out
- * (matmul/sm100_nvfp4/runner.cu:45-59, 78-90), pipelined.  D is cut into up to 4x4
- * blocks; operand uploads, per-block GEMMs and 2-D copies of D back to the host run
- * on three internal streams, so the transfers overlap each other and the compute.
+ * (matmul/sm100_nvfp4/runner.cu:45-59, 78-90), pipelined.  D is cut into blocks of up
+ * to 2048 x 2048, taken in growing squares from the top-left corner; operand uploads,
+ * per-block GEMMs and 2-D copies of D back to the host run on three internal streams,
+ * so the transfers overlap each other and the compute.  Consecutive calls overlap as
+ * well (the next call's uploads start once this call's GEMMs have run; D alternates
+ * between two device buffers).
  * Asynchronous: `stream` (the caller's) is made to wait for D to reach the host;
  * synchronise it before reading hD.  Device buffers are allocated on first use per
  * device and kept; calls on one device are serialised.
