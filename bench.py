@@ -958,6 +958,42 @@ def gather_section(nv, dev, world, rank, reps=10):
                        "nvlink_in_bytes_per_rank": in_bytes, "nvlink_gbs_basis": 770.0, "bound_ms": bound_ms}
     if world > 1:
         res["roofline"]["frac_fused_stores"] = bound_ms / res["fused_nvlink_stores_ms"]
+    del a, sfa, bs, ss, d
+    res["down_proj"] = gather_down_proj(nv, dev, world, rank, timed)
+    return res
+
+
+def gather_down_proj(nv, dev, world, rank, timed):
+    """BASELINE configs[3]'s down-projection, N-sharded the same way: H [16384, 28672]
+    (the up-projection's width) times W_down [8192, 28672], 7.7e15 FLOP in all."""
+    from nvfp4_b200.dist import FusedGather, gather_columns, shard_bounds
+    M, N, K = 16384, 8192, 28672
+    g = torch.Generator(device=dev).manual_seed(93)
+    h = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    _, gh = nv.global_scale(h)
+    a, sfa = nv.quantize(h, gh)
+    del h
+    n0, n1 = shard_bounds(N, world, rank)
+    w = (torch.randn(n1 - n0, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    _, gw = nv.global_scale(w)
+    bs, ss = nv.quantize(w, gw)
+    del w
+    alpha = float((gh * gw).item())
+    d = torch.empty(M, n1 - n0, dtype=torch.bfloat16, device=dev)
+    res = {"what": "prefill FFN down-projection M=16384 N=8192 K=28672, N-sharded; with the full output, "
+                   "bf16 D [16384, 8192] on every rank", "shard_columns": n1 - n0}
+    res["shard_gemm_ms"] = timed(lambda: nv.gemm(a, sfa, bs, ss, alpha, out=d))
+    if world > 1:
+        res["gemm_plus_nccl_all_gather_ms"] = timed(
+            lambda: gather_columns(nv.gemm(a, sfa, bs, ss, alpha, out=d), N))
+        fg = FusedGather(M, N, dev, multicast=False)
+        res["fused_nvlink_stores_ms"] = timed(lambda: fg.gemm(a, sfa, bs, ss, alpha, n0))
+        del fg
+        torch.distributed.barrier()
+    nv.device_status()
+    flops = 2.0 * M * N * K
+    for k in [k for k in res if k.endswith("_ms") and res[k]]:
+        res[k.replace("_ms", "_tflops")] = flops / (res[k] / 1e3) / 1e12
     return res
 
 

@@ -146,15 +146,16 @@ def test_c2_full_size_sampled(nv, oracle, cuda_dev, N, K):
     assert not torch.isnan(d).any()
 
 
-def test_c4_full_size_properties(nv, oracle, cuda_dev):
-    """BASELINE config 3's prefill shape on one GPU (M=16384, N=28672, K=8192: 7.7e15
-    FLOP, 940 MB of bf16 D), checked through properties that hold at any size: 32-row
-    slices against the oracle (first, middle, last tile rows); every one of 8 weight
-    shards (the multi-GPU split, whole 128-row scale blocks) gives bit for bit the
-    same columns as the full GEMM (each output element is accumulated by one CTA over
-    the same K order); two runs identical."""
+@pytest.mark.parametrize("M,N,K", [(16384, 28672, 8192), (16384, 8192, 28672)], ids=["up", "down"])
+def test_c4_full_size_properties(nv, oracle, cuda_dev, M, N, K):
+    """BASELINE config 3's prefill FFN on one GPU — the up-projection (M=16384,
+    N=28672, K=8192) and the down-projection (N=8192, K=28672), 7.7e15 FLOP each —
+    checked through properties that hold at any size: 32-row slices against the
+    oracle (first, middle, last tile rows); every one of 8 weight shards (the
+    multi-GPU split, whole 128-row scale blocks) gives bit for bit the same columns as
+    the full GEMM (each output element is accumulated by one CTA over the same K
+    order); two runs identical."""
     from nvfp4_b200.dist import shard_bounds, shard_weight
-    M, N, K = 16384, 28672, 8192
     a, sfa, gsa = quantized_operands(oracle, M, K, seed=31)
     b, sfb, gsb = quantized_operands(oracle, N, K, seed=32)
     alpha = float(np.float32(gsa) * np.float32(gsb))
