@@ -57,7 +57,10 @@ struct Params {
     // [3] epilogue wait on acc_full  [4] epilogue drain+store  [5] tiles
     // [6] MMA-thread cycles from first issue to last commit  [7] the same span in ns
     // [8] %globaltimer at CTA entry  [9] at CTA exit  [10] at the first MMA issue
-    // [11] at the last accumulator commit
+    // [11] at the last accumulator commit; hand-off sample (%globaltimer ns): [12] the
+    // MMA thread seeing tile 3's first slot landed, [13] its return from the
+    // accumulator wait of tile 3, [14] epilogue warp 2 woken by tile 2's accumulator, [15] the last
+    // epilogue warp of the CTA with tile 2 read out of tensor memory
     unsigned long long *trace;
     int group_m;  // pair kernel: 256-row tile rows per raster group
     int clc;      // pair kernel: tiles handed out by cluster launch control (else static persistent)
@@ -68,7 +71,7 @@ struct Params {
     Grouped grouped;
     Gather gather;
 };
-constexpr int kTraceSlots = 12;
+constexpr int kTraceSlots = 16;
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool f16) {
     if (f16) {

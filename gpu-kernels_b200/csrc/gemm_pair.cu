@@ -379,7 +379,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             int local = 0;
             bool ok = true, any_issued = false;
             long long t_full = 0, t_acc = 0, t_first = 0;
-            uint64_t ns_first = 0;
+            uint64_t ns_first = 0, ns_landed3 = 0, ns_resume3 = 0;  // hand-off sample (kept in registers)
             for (int k = 0; ok; k++, local++) {
                 const int t = tile_at(k, ok);
                 if (t < 0) break;
@@ -403,6 +403,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                     if (TRACE) {
                         const long long c1 = clock64();
                         t_acc += c1 - c0;
+                        if (local == 3) ns_resume3 = global_timer_ns();  // hand-off sample: MMA resumes
                         if (!t_first) {
                             t_first = c1;
                             ns_first = global_timer_ns();
@@ -420,6 +421,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                         break;
                     }
                     if (TRACE) t_full += clock64() - c0;
+                    if (TRACE && local == 3 && kb == 0) ns_landed3 = global_timer_ns();  // tile 3's first slot landed
                     tc_fence_after();
                     const uint32_t acc0 = kb != 0;
                     if ((kb + 1) * KG <= p.k_groups) {
@@ -505,6 +507,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 tr[7] = ns_last - ns_first;
                 tr[10] = ns_first;
                 tr[11] = ns_last;
+                tr[12] = ns_landed3;
+                tr[13] = ns_resume3;
             }
         }
     } else {
@@ -532,6 +536,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         int local = 0;
         uint32_t chunk = 0;  // TMA-store boxes issued by this warp (two staging boxes alternate)
         long long t_accw = 0, t_store = 0, c_ready = 0;
+        uint64_t ns_wake2 = 0, ns_read2 = 0;  // hand-off sample (kept in registers)
         for (int k = 0;; k++, local++) {
             bool okq = true;
             int t = 0;
@@ -547,9 +552,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                 ok = p.spin ? spin_parity(bar_acc_full + 8 * buf, use & 1, tmo, abort_flag)
                             : wait_parity(bar_acc_full + 8 * buf, use & 1, tmo, abort_flag);
             ok = __shfl_sync(0xffffffffu, ok, 0);
+            uint64_t ns_ready = 0;
             if (TRACE) {
                 c_ready = clock64();
                 t_accw += c_ready - c0;
+                ns_ready = global_timer_ns();
             }
             if (!ok) {
                 if (lane == 0) report_timeout(abort_flag, p.ctl.status);
@@ -562,9 +569,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
             for (int c = 0; c < kCols / 32; c++)
                 tmem_ld_32x32b_x32(taddr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&acc[c * 32]));
             tmem_ld_wait();
+            if (TRACE && local == 2) {  // hand-off sample: tile 2 woken, read out (no memory access here)
+                ns_wake2 = ns_ready;
+                ns_read2 = global_timer_ns();
+            }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(lead_acc_empty + 8 * buf);
+            if (lane == 0) mbar_arrive_cluster_cta_release(lead_acc_empty + 8 * buf);
             const int row = ti.a_row0 + (int)rank * 128 + quarter * 32 + lane, col0 = ti.tn * BN + half * kCols;
             if (p.gather.n_dst > 0) {
                 if constexpr (L::kHasStage && kCols % 64 == 0)
@@ -621,6 +632,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                                               row + ti.sf_row_off, tab, guess, gs_ok);
             }
             if (TRACE && warp == 2 && lane == 0) t_store += clock64() - c_ready;
+        }
+        if (TRACE && lane == 0 && ns_read2) {  // the last epilogue warp's read-out time of tile 2
+            atomicMax(p.trace + blockIdx.x * kTraceSlots + 15, (unsigned long long)ns_read2);
+            if (warp == 2) p.trace[blockIdx.x * kTraceSlots + 14] = ns_wake2;
         }
         if (TRACE && warp == 2 && lane == 0) {
             p.trace[blockIdx.x * kTraceSlots + 3] = t_accw;

@@ -417,6 +417,16 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// The same arrive with CTA-scope release: for a barrier that carries no memory data
+// between the CTAs, only the order of tensor-memory accesses, which the tcgen05
+// fences around the arrive and the wait provide (an accumulator released after
+// tcgen05.ld + tcgen05.wait::ld + tcgen05.fence::before_thread_sync).  The
+// cluster-scope release would first make every earlier memory access of the thread
+// visible to the whole cluster.
+__device__ __forceinline__ void mbar_arrive_cluster_cta_release(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 // 2-D tiled load into this CTA's smem whose transaction bytes complete on an
 // mbarrier that may live in either CTA of the pair (cta_group::2).  It has one
 // destination CTA: each CTA fetches only its own tile.

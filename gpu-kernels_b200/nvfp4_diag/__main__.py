@@ -54,7 +54,7 @@ def trace(M: int, N: int, K: int, reps: int = 3, epi: str = "none"):
     from nvfp4_b200.layout import sf_bytes
     from nvfp4_b200.ops import create_tensors
     _l = lib
-    slots = 12
+    slots = 16
     dev = torch.device("cuda", 0)
     a, b, sfa, sfb = create_tensors(M, N, K, seed=1)
     sfa = torch.full_like(sfa, 0x38)
@@ -104,6 +104,21 @@ def trace(M: int, N: int, K: int, reps: int = 3, epi: str = "none"):
         "last_commit_max_us": us(leaders[:, 11].max() - t0),
         "epilogue_tail_us": us((leaders[:, 9] - leaders[:, 11]).double().mean()),  # last commit -> CTA exit
     })
+    # accumulator hand-off between tiles 2 and 3 of each pair (%globaltimer ns; pairs
+    # with fewer than 4 tiles have no sample)
+    sel = (leaders[:, 13] > 0) & (leaders[:, 14] > 0)
+    hs, peers = leaders[sel].double(), t[1::2][sel].double()
+    if len(hs):
+        last_read = torch.maximum(hs[:, 15], peers[:, 15])
+        res["handoff_sample_ns"] = {
+            "pairs": len(hs),
+            "first_slot_landed_after_leader_wake": float((hs[:, 12] - hs[:, 14]).mean()),
+            "peer_wake_after_leader": float((peers[:, 14] - hs[:, 14]).mean()),
+            "leader_read": float((hs[:, 15] - hs[:, 14]).mean()),  # wake -> last warp read out
+            "peer_read": float((peers[:, 15] - peers[:, 14]).mean()),
+            "last_read_to_mma_resume": float((hs[:, 13] - last_read).mean()),  # arrivals -> MMA thread
+            "leader_wake_to_mma_resume": float((hs[:, 13] - hs[:, 14]).mean()),
+        }
     return res
 
 
