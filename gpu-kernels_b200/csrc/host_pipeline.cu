@@ -42,7 +42,7 @@ struct DeviceBuffers {
     cudaEvent_t comp_done = nullptr;     // the previous call's GEMMs have run: operand buffers free
     cudaEvent_t out_done[2] = {};        // each D buffer's last downloads have finished
     int calls = 0;                       // which D buffer the next call uses (calls & 1)
-    size_t d_set = 0;                    // the previous call's D buffer size (its layout)
+    size_t off_d = 0, d_set = 0;         // the previous call's layout: D buffers' offset and size
     bool ready = false;
 };
 
@@ -118,7 +118,15 @@ int gemm_host(const uint8_t *hA, const uint8_t *hSFA, const uint8_t *hB, const u
     cudaStreamWaitEvent(b.s_in, b.comp_done, 0);       // the previous call's GEMMs no longer read A, B
     cudaStreamWaitEvent(b.s_comp, start, 0);
     cudaStreamWaitEvent(b.s_comp, b.out_done[set], 0);  // this D buffer's earlier downloads are done
-    if (b.d_set != d_set) cudaStreamWaitEvent(b.s_comp, b.out_done[set ^ 1], 0);  // new layout: both
+    if (b.off_d != off_d || b.d_set != d_set) {
+        // a new layout: this call's operands or D may cover memory that an earlier
+        // call's D still occupies, so its uploads and GEMMs wait for every download
+        for (int k = 0; k < 2; k++) {
+            cudaStreamWaitEvent(b.s_in, b.out_done[k], 0);
+            cudaStreamWaitEvent(b.s_comp, b.out_done[k], 0);
+        }
+    }
+    b.off_d = off_d;
     b.d_set = d_set;
     cudaStreamWaitEvent(b.s_out, start, 0);
 

@@ -66,3 +66,28 @@ def test_back_to_back_calls_overlap_correctly(nv, oracle, cuda_dev):
     nv.device_status()
     for n, (_, ref, out) in enumerate(cases):
         assert torch.equal(out, ref), f"call {n} {shapes[n]}"
+
+
+def test_grown_operands_wait_for_earlier_downloads(nv, oracle, cuda_dev):
+    """A call whose operands take more room than the previous call's moves the D
+    buffers: its uploads must not land on memory an earlier call's D is still being
+    downloaded from.  A wide D with small operands (a long download), then a square
+    problem with large operands, issued without waiting on two streams."""
+    shapes = [(4096, 8192, 512), (2048, 2048, 8192), (4096, 8192, 512)]
+    cases = []
+    for n, (M, N, K) in enumerate(shapes):
+        a, sfa = oracle.random_codes(M, K, seed=300 + n, sf_lo=0x30, sf_hi=0x40)
+        b, sfb = oracle.random_codes(N, K, seed=400 + n, sf_lo=0x30, sf_hi=0x40)
+        host = [torch.from_numpy(t).pin_memory() for t in (a, sfa, b, sfb)]
+        ref = nv.gemm(*[t.to(cuda_dev) for t in host], 0.25).cpu()
+        out = torch.full((M, N), float("nan"), dtype=torch.bfloat16).pin_memory()
+        cases.append((host, ref, out))
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(cuda_dev), torch.cuda.Stream(cuda_dev)]
+    for n, (host, _, out) in enumerate(cases):
+        with torch.cuda.stream(streams[n % 2]):
+            nv.gemm_host(*host, 0.25, out)
+    torch.cuda.synchronize()
+    nv.device_status()
+    for n, (_, ref, out) in enumerate(cases):
+        assert torch.equal(out, ref), f"call {n} {shapes[n]}"
