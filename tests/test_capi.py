@@ -108,3 +108,14 @@ def test_rank_barrier_rejects_bad_arguments_on_host(nv):
     assert L.nvfp4_rank_barrier(pads, 2, 0, 1024, 4096, None) == -1           # channel beyond the pad
     bad = (C.c_uint64 * 2)(1 << 20, (1 << 21) + 2)
     assert L.nvfp4_rank_barrier(bad, 2, 0, 0, 4096, None) == -3               # 4-byte aligned slots
+
+
+def test_gemm_host_rejects_bad_arguments_on_host(nv):
+    """The host-buffer entry point validates before touching a device or a buffer."""
+    L = nv.lib()
+    p = C.c_void_p(1 << 20)  # never dereferenced: validation runs first
+    assert L.nvfp4_gemm_host(None, p, p, p, 1.0, p, 128, 256, 256, None) == -1     # no A
+    assert L.nvfp4_gemm_host(p, p, p, p, 1.0, None, 128, 256, 256, None) == -1     # no D
+    assert L.nvfp4_gemm_host(p, p, p, p, 1.0, p, 0, 256, 256, None) == -2          # M < 1
+    assert L.nvfp4_gemm_host(p, p, p, p, 1.0, p, 128, 12, 256, None) == -2         # N % 8
+    assert L.nvfp4_gemm_host(p, p, p, p, 1.0, p, 128, 256, 96, None) == -2         # K % 64
