@@ -368,9 +368,16 @@ int gemm_validate(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
 int pair_dispatch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB, float alpha, void *D,
                   int M, int N, int K, cudaStream_t stream, bool f16, const DeviceInfo &di, const Epi &epi);
 
-// Kernel choice for the persistent path: the CTA-pair kernel for M > 128, the
-// single-CTA kernel otherwise.  NVFP4_GEMM_VARIANT=single|pair forces one.
-static int gemm_variant(int M) {
+// Kernel choice for the persistent path: the single-CTA kernel for M <= 128 and for
+// small grids with short K, the CTA-pair kernel otherwise.  The two give the same
+// bits (each output element is one fp32 sum over K in the same order, then the same
+// rounding).  A launch of at most one wave of 256 x 256 tiles is bound by fixed
+// per-tile costs, which are lower in the single-CTA kernel (no cluster set-up, one
+// accumulator hand-off inside the CTA): measured, 1024³ 10.2 against 13.3 us, 2048³
+// 13.1 against 15.1 us, 512 x 2048 x 4096 16.4 against 17.2 us; with longer K the
+// pair kernel's lower cost per k-block wins (1536 x 1536 x 8192: 23.4 against 22.0
+// us).  NVFP4_GEMM_VARIANT=single|pair forces one.
+static int gemm_variant(int M, int N, int K, int pairs, const Epi &epi) {
     static int forced = [] {
         const char *e = std::getenv("NVFP4_GEMM_VARIANT");
         if (!e) return 0;
@@ -379,7 +386,11 @@ static int gemm_variant(int M) {
         return 0;
     }();
     if (forced) return forced;
-    return M > 128 ? 2 : 1;
+    if (M <= 128) return 1;
+    if (epi.act == kActSwiglu) return 2;  // the single-CTA epilogue has no SwiGLU
+    const int64_t tiles = (int64_t)((M + 255) / 256) * ((N + 255) / 256);
+    if (tiles <= pairs && (K <= 2048 || (K <= 4096 && tiles <= 32))) return 1;
+    return 2;
 }
 
 // Persistent GEMM (single-CTA or CTA-pair kernel) with an optional fused epilogue;
@@ -390,7 +401,8 @@ int gemm_dispatch_epi(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, co
     if (st) return st;
     DeviceInfo di;
     if ((st = device_info(&di))) return st;
-    if (gemm_variant(M) == 2) return pair_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, stream, f16, di, epi);
+    if (gemm_variant(M, N, K, di.sm_count / 2, epi) == 2)
+        return pair_dispatch(A, SFA, B, SFB, alpha, D, M, N, K, stream, f16, di, epi);
     if (epi.act == kActSwiglu) return NVFP4_ERR_UNSUPPORTED;  // the single-CTA epilogue has no SwiGLU
     if (f16) return gemm::launch<256, 4, true>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, epi);
     return gemm::launch<256, 4, false>(A, SFA, B, SFB, alpha, D, M, N, K, stream, di, epi);
