@@ -228,3 +228,39 @@ print("ok", err)
                NVFP4_PAIR_TMA_STORE="1" if store == "tma" else "0")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
+
+
+def test_single_and_pair_kernels_give_the_same_bits(tmp_path):
+    """nvfp4_gemm picks the single-CTA kernel for one-wave grids with short K and the
+    CTA-pair kernel otherwise; the choice must not change a result.  Both kernels,
+    forced in fresh processes, on shapes either side of the choice (bf16 and fp16
+    outputs, ragged edges), give identical bits."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    shapes = [(1024, 1024, 1024), (2048, 2048, 2048), (300, 1280, 2048), (520, 776, 1344), (1536, 1536, 8192)]
+    code = f"""
+import sys, torch
+sys.path[:0] = [{root!r}, {os.path.join(root, 'gpu-kernels_b200')!r}]
+import nvfp4_b200 as nv
+from oracle import oracle as o
+out = {{}}
+for (M, N, K) in {shapes!r}:
+    a, sfa = o.random_codes(M, K, seed=M, sf_lo=0x30, sf_hi=0x40)
+    b, sfb = o.random_codes(N, K, seed=N, sf_lo=0x30, sf_hi=0x40)
+    t = lambda x: torch.from_numpy(x).cuda()
+    out[(M, N, K)] = nv.gemm(t(a), t(sfa), t(b), t(sfb), 0.5).cpu()
+    out[(M, N, K, 'f16')] = nv.gemm(t(a), t(sfa), t(b), t(sfb), 0.5, out_dtype=torch.float16).cpu()
+torch.cuda.synchronize(); nv.device_status()
+torch.save(out, sys.argv[1])
+"""
+    res = {}
+    for variant in ("single", "pair"):
+        path = str(tmp_path / f"{variant}.pt")
+        env = dict(os.environ, NVFP4_GEMM_VARIANT=variant)
+        r = subprocess.run([sys.executable, "-c", code, path], env=env, capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stdout + r.stderr
+        res[variant] = torch.load(path)
+    for key, d in res["single"].items():
+        assert torch.equal(d, res["pair"][key]), key
