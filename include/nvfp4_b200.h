@@ -103,7 +103,9 @@ NVFP4_API int nvfp4_quantize_dynamic(const uint16_t *X, uint8_t *Q, uint8_t *SF,
  * launcher matmul_nvfp4_v5 (matmul/sm100_nvfp4/nvfp4_v5.cu:287-309, declared at
  * block_scaled_nvfp4.cuh:15-16), adding alpha, bf16 output, a stream, any
  * M >= 1 / N % 8 / K % 64 shape and a status code.  For M > 128 it runs the
- * persistent, warp-specialised tcgen05 kernel (nvfp4_gemm_persistent).  For
+ * persistent, warp-specialised tcgen05 kernels (nvfp4_gemm_persistent: CTA pairs,
+ * or single CTAs for grids of at most one wave of 256 x 256 tiles with short K —
+ * the two give the same bits).  For
  * M <= 128 (decode shapes; env NVFP4_DECODE_MAX_M lowers the bound, 0 disables)
  * it runs the stream-K decode kernel (nvfp4_gemm_decode) with a workspace that
  * this function allocates with cudaMalloc on the first such call per (device,
@@ -175,7 +177,8 @@ typedef struct nvfp4_epilogue {
 } nvfp4_epilogue;
 
 /* nvfp4_gemm with the fused epilogue `epi` (NULL = plain nvfp4_gemm).  Same kernel
- * choice (split-K decode kernel for M <= 128, CTA-pair kernel above). */
+ * choice (split-K decode kernel for M <= 128, the persistent kernels above; SwiGLU
+ * always on CTA pairs). */
 NVFP4_API int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uint8_t *SFB,
                                   float alpha, uint16_t *D, int M, int N, int K, const nvfp4_epilogue *epi,
                                   void *stream);
