@@ -61,6 +61,24 @@ static int decode_max_m() {
     return v;
 }
 
+// nvfp4_gemm's kernel for M <= decode_max_m(): the split-K decode kernel (128-row
+// weight tiles spread over every SM), or the persistent single-CTA kernel (one 128 x
+// 256 tile per 256 weight rows: the activations are read once per 256 weight rows
+// instead of once per 128, and no split-K partials are written).  The second wins
+// once the activations are a sizeable share of each k-block and there are enough
+// 256-row tiles to keep most SMs streaming.  Measured (CUDA-graph replay, us, decode
+// against persistent): N=28672 K=8192 (112 tiles) M=32 26.1/25.5, M=64 28.6/26.0,
+// M=128 31.1/26.8, M=16 25.5/29.6; N=57344 K=4096 (224) M=32 29.6/28.6, M=128 50.1/29.5;
+// N=20480 K=8192 (80) M=32 20.0/21.2, M=64 23.7/21.6; N=14336 K=4096 (56) M=32
+// 13.3/11.6; N=8192 (32 tiles) decode always, 26.8-36.8 against 49.7-50.8.
+static bool use_decode(int M, int N, int K, const Epi &e) {
+    if (M > decode_max_m() || !decode_tiles_fit(N, 1)) return false;
+    if (e.act == kActSwiglu) return true;  // the single-CTA epilogue has no SwiGLU
+    const int tiles = (N + 255) / 256;
+    if (tiles >= 48 && (M >= 64 || (M >= 32 && (tiles >= 100 || K <= 4096)))) return false;
+    return true;
+}
+
 // nvfp4_gemm's own decode workspace: one zero-initialised buffer per (device,
 // stream), grown on demand and kept for the life of the process.  Calls on the
 // same stream are ordered, so they may share it.  Kernels leave its counters at
@@ -114,7 +132,7 @@ int nvfp4_gemm(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const uin
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     int st = gemm_validate(A, SFA, B, SFB, D, M, N, K);
     if (st) return st;
-    if (M <= decode_max_m() && decode_tiles_fit(N, 1)) {
+    if (use_decode(M, N, K, Epi())) {
         void *ws = nullptr;
         size_t bytes = 0;
         st = internal_workspace(decode_workspace_bytes(M, N), s, &ws, &bytes);
@@ -162,7 +180,7 @@ int nvfp4_gemm_epilogue(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, 
     if (st) return st;
     st = gemm_validate(A, SFA, B, SFB, e.q ? static_cast<const void *>(e.q) : D, M, N, K);
     if (st) return st;
-    if (M <= decode_max_m() && decode_tiles_fit(N, 1)) {
+    if (use_decode(M, N, K, e)) {
         void *ws = nullptr;
         size_t bytes = 0;
         if ((st = internal_workspace(decode_workspace_bytes(M, N), s, &ws, &bytes))) return st;
