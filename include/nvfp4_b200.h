@@ -107,7 +107,10 @@ NVFP4_API int nvfp4_quantize_dynamic(const uint16_t *X, uint8_t *Q, uint8_t *SF,
  * or single CTAs for grids of at most one wave of 256 x 256 tiles with short K —
  * the two give the same bits).  For
  * M <= 128 (decode shapes; env NVFP4_DECODE_MAX_M lowers the bound, 0 disables)
- * it runs the stream-K decode kernel (nvfp4_gemm_decode) with a workspace that
+ * it runs the stream-K decode kernel (nvfp4_gemm_decode) — or, for weights of at
+ * least 48 tiles of 256 rows with M >= 64 (M >= 32 for the widest), the persistent
+ * single-CTA kernel, which reads the activations once per 256 weight rows — with a
+ * decode workspace that
  * this function allocates with cudaMalloc on the first such call per (device,
  * stream) and keeps; make that first call outside CUDA-graph capture.
  */
