@@ -103,6 +103,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
         tmem_relinquish();
     }
+    // Launched as a programmatic dependent of the previous kernel in the stream: the
+    // set-up above overlapped that kernel's tail; nothing of global memory is read or
+    // written before it has completed.
+    grid_dependency_wait();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -146,6 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   kg * 512u, bar_full + 8 * s);
                 }
             }
+            grid_launch_dependents();  // all loads issued: the next kernel may start its set-up
             if (!ok) {
                 // Drain: every load already issued must land before the CTA exits.
                 volatile int never = 0;
@@ -350,7 +355,28 @@ static int launch(const uint8_t *A, const uint8_t *SFA, const uint8_t *B, const 
     p.epi = epi;
     if ((st = kernel_ctl(&p.ctl))) return st;
     const int grid = p.num_tiles < di.sm_count ? p.num_tiles : di.sm_count;
-    kern<<<grid, kThreads, L::kDynamicSmem, stream>>>(ta, tb, p);
+    // A programmatic dependent of the previous kernel in the stream for M > 128: its
+    // set-up then overlaps that kernel's tail (back-to-back 2048³ 14.6 -> 13.5 us,
+    // 1024 x 1024 x 4096 14.4 -> 13.5 us).  Not for M <= 128, the weight-streaming
+    // calls, where it measured 2 % slower (28672 x 8192 weights, M = 32-128, from
+    // CUDA-graph replays: 24.9-26.4 against 25.4-27.0 us).  Env NVFP4_SINGLE_PDL=0|1
+    // overrides.
+    static const int pdl_env = [] {
+        const char *e = std::getenv("NVFP4_SINGLE_PDL");
+        return e ? (std::atoi(e) ? 1 : 0) : -1;
+    }();
+    const int pdl = pdl_env >= 0 ? pdl_env : (M > kBlockM ? 1 : 0);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::kDynamicSmem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, kern, ta, tb, p) != cudaSuccess) return NVFP4_ERR_CUDA;
     count_launch();
     return cuda_status(cudaGetLastError());
 }
