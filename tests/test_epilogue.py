@@ -87,7 +87,9 @@ def test_epilogue_host_checks(nv):
     assert call(256, 256, 256, E(activation=5)) == -1                                   # unknown activation
 
 
-SHAPES = [(16, 1024, 512), (77, 512, 1024), (300, 768, 1024), (520, 1024, 512)]
+# (72, 12544, 512): M <= 128 with a wide weight (49 tiles of 256 rows) runs on the
+# persistent single-CTA kernel, the other small-M shapes on the split-K decode kernel
+SHAPES = [(16, 1024, 512), (77, 512, 1024), (300, 768, 1024), (520, 1024, 512), (72, 12544, 512)]
 
 
 def _operands(oracle, M, N, K, seed):
@@ -168,7 +170,7 @@ def test_torch_ops_epilogue(nv, oracle, cuda_dev):
     assert torch.equal(d1, d2) and torch.equal(q1, q2) and torch.equal(s1, s2)
 
 
-SWIGLU_SHAPES = [(16, 1024, 512), (77, 512, 1024), (300, 768, 1024), (520, 1024, 512)]
+SWIGLU_SHAPES = [(16, 1024, 512), (77, 512, 1024), (300, 768, 1024), (520, 1024, 512), (72, 12544, 512)]
 
 
 @pytest.mark.gpu
